@@ -1,0 +1,190 @@
+"""CPU oracle (numpy, float64) for RACE attention forward and backward.
+
+TEST INFRASTRUCTURE ONLY: this module is the parity checker.  The product path
+(``race_attention_b200``) never imports it.
+
+Parity pin: checked against golden vectors produced by running the reference's
+own torch modules under autograd (``tests/golden/make_golden.py``) and against
+the reference's compiled OpenMP prefix-mean kernel (``oracle/_ref``, built by
+``oracle/Makefile`` from ``kernels/cpu/race_pref.cpp``).
+
+Notation: N streams, T tokens, D head dim, K hyperplanes per table, L tables,
+R = 2**K buckets per table, S = L*R.
+
+Reference semantics restated here (paths inside the reference project):
+  * corners in ``itertools.product([-1, +1], repeat=K)`` order
+    (``misc/vit.py:911-912``, ``misc/race.py:54-58``)
+  * soft hash ``softmax(tanh(x @ planes_T) / scale @ protos_T)`` per table
+    (``misc/vit.py:943-958``, ``misc/race.py:79-105``)
+  * non-causal aggregation ``E = (pK^T V) / (sum_t pK + eps)`` and readout
+    ``out = pQ @ E`` summed over all L*R buckets (``misc/vit.py:967-975``)
+  * causal per-bucket prefix mean (``misc/race.py:108-138``,
+    ``kernels/cpu/race_pref.cpp:36-101``) and its backward
+    (``kernels/cpu/race_pref.cpp:104-220``).
+"""
+from __future__ import annotations
+
+import itertools
+
+import numpy as np
+
+
+def corners(K: int) -> np.ndarray:
+    """[R, K] bucket prototypes, ``itertools.product`` order (misc/vit.py:911)."""
+    return np.array(list(itertools.product([-1.0, 1.0], repeat=K)), dtype=np.float64)
+
+
+def soft_hash(x, planes, K, L, scale):
+    """Soft bucket probabilities.
+
+    x: [N, T, D]; planes: [N, L*K, D] (the hyperplanes each stream uses).
+    Returns probs [N, T, L*R] (table-major, as misc/vit.py:962-963 flattens)
+    plus the intermediates (h = tanh(proj)) the backward needs.
+    """
+    x = np.asarray(x, np.float64)
+    planes = np.asarray(planes, np.float64)
+    N, T, D = x.shape
+    proj = np.einsum("ntd,njd->ntj", x, planes)          # misc/vit.py:943-944
+    h = np.tanh(proj).reshape(N, T, L, K)
+    logits = (h / scale) @ corners(K).T                   # misc/vit.py:955-956
+    logits = logits - logits.max(-1, keepdims=True)
+    e = np.exp(logits)
+    p = e / e.sum(-1, keepdims=True)                      # misc/vit.py:957-958
+    return p.reshape(N, T, L * (1 << K)), h
+
+
+def soft_hash_backward(dp, p, h, planes, K, L, scale):
+    """Back-propagate d(probs) through softmax, the corner matmul, /scale and tanh.
+
+    Returns (dx [N,T,D], dscale scalar).
+    """
+    N, T, S = dp.shape
+    R = 1 << K
+    c = corners(K)                                        # [R, K]
+    p4 = p.reshape(N, T, L, R)
+    dp4 = dp.reshape(N, T, L, R)
+    g = p4 * (dp4 - (p4 * dp4).sum(-1, keepdims=True))    # d logits
+    du = g @ c                                            # [N,T,L,K]; u = h/scale
+    dh = du / scale
+    dscale = float(-(du * h).sum() / scale / scale)
+    dproj = (dh * (1.0 - h * h)).reshape(N, T, L * K)
+    dx = np.einsum("ntj,njd->ntd", dproj, np.asarray(planes, np.float64))
+    return dx, dscale
+
+
+# ----------------------------------------------------------------------------- non-causal
+def noncausal_forward(q, k, v, planes, K, L, scale, eps=1e-6):
+    """misc/vit.py:918-978 for one ensemble slice: returns (out, A, Bsum)."""
+    pK, _ = soft_hash(k, planes, K, L, scale)
+    pQ, _ = soft_hash(q, planes, K, L, scale)
+    v = np.asarray(v, np.float64)
+    Bsum = np.einsum("nts,ntd->nsd", pK, v)               # misc/vit.py:967
+    A = pK.sum(1)                                         # misc/vit.py:969
+    E = Bsum / (A[..., None] + eps)                       # misc/vit.py:972
+    out = np.einsum("nts,nsd->ntd", pQ, E)                # misc/vit.py:975
+    return out, A, Bsum
+
+
+def noncausal_backward(q, k, v, planes, K, L, scale, dout, eps=1e-6):
+    """Analytic gradient of ``noncausal_forward``: (dq, dk, dv, dscale)."""
+    pK, hK = soft_hash(k, planes, K, L, scale)
+    pQ, hQ = soft_hash(q, planes, K, L, scale)
+    v = np.asarray(v, np.float64)
+    dout = np.asarray(dout, np.float64)
+    Bsum = np.einsum("nts,ntd->nsd", pK, v)
+    A = pK.sum(1)
+    inv = 1.0 / (A + eps)
+    E = Bsum * inv[..., None]
+    dpQ = np.einsum("ntd,nsd->nts", dout, E)
+    dE = np.einsum("nts,ntd->nsd", pQ, dout)
+    dB = dE * inv[..., None]
+    dA = -(dB * E).sum(-1)
+    dv = np.einsum("nts,nsd->ntd", pK, dB)
+    dpK = np.einsum("ntd,nsd->nts", v, dB) + dA[:, None, :]
+    dq, dsq = soft_hash_backward(dpQ, pQ, hQ, planes, K, L, scale)
+    dk, dsk = soft_hash_backward(dpK, pK, hK, planes, K, L, scale)
+    return dq, dk, dv, dsq + dsk
+
+
+# ----------------------------------------------------------------------------- causal
+def prefix_mean_flat(w, V, eps=1e-6):
+    """kernels/cpu/race_pref.cpp:36-101: w [NS,T], V [NS,T,D] -> E [NS,T,D]."""
+    w = np.asarray(w, np.float64)
+    V = np.asarray(V, np.float64)
+    A = np.cumsum(w, axis=1)
+    B = np.cumsum(w[..., None] * V, axis=1)
+    return B / (A[..., None] + eps)
+
+
+def prefix_mean_flat_backward(w, V, gE, eps=1e-6):
+    """kernels/cpu/race_pref.cpp:104-220: returns (grad_w [NS,T], grad_V [NS,T,D])."""
+    w = np.asarray(w, np.float64)
+    V = np.asarray(V, np.float64)
+    gE = np.asarray(gE, np.float64)
+    A = np.cumsum(w, axis=1)
+    B = np.cumsum(w[..., None] * V, axis=1)
+    invA = 1.0 / (A + eps)
+    alpha = -(invA ** 2) * (gE * B).sum(-1)                       # race_pref.cpp:175-181
+    beta = gE * invA[..., None]
+    beta_suf = np.cumsum(beta[:, ::-1], axis=1)[:, ::-1]          # race_pref.cpp:194-199
+    alpha_suf = np.cumsum(alpha[:, ::-1], axis=1)[:, ::-1]
+    gw = alpha_suf + (beta_suf * V).sum(-1)                       # race_pref.cpp:202-208
+    gV = w[..., None] * beta_suf                                  # race_pref.cpp:210-215
+    return gw, gV
+
+
+def _causal_states(pK, v, eps):
+    A = np.cumsum(pK, axis=1)                                     # [N,T,S]
+    B = np.cumsum(pK[..., None] * v[:, :, None, :], axis=1)       # [N,T,S,D]
+    return A, B
+
+
+def causal_forward(q, k, v, planes, K, L, scale, eps=1e-6):
+    """misc/race.py:63-142 (per-bucket normalised prefix mean): returns out."""
+    pK, _ = soft_hash(k, planes, K, L, scale)
+    pQ, _ = soft_hash(q, planes, K, L, scale)
+    v = np.asarray(v, np.float64)
+    A, B = _causal_states(pK, v, eps)
+    E = B / (A[..., None] + eps)                                  # misc/race.py:110
+    return np.einsum("nts,ntsd->ntd", pQ, E)                      # misc/race.py:135-138
+
+
+def causal_backward(q, k, v, planes, K, L, scale, dout, eps=1e-6):
+    """Gradient of ``causal_forward`` built on the race_pref.cpp backward: (dq, dk, dv, dscale)."""
+    pK, hK = soft_hash(k, planes, K, L, scale)
+    pQ, hQ = soft_hash(q, planes, K, L, scale)
+    v = np.asarray(v, np.float64)
+    dout = np.asarray(dout, np.float64)
+    N, T, S = pK.shape
+    D = v.shape[-1]
+    A, B = _causal_states(pK, v, eps)
+    E = B / (A[..., None] + eps)
+    dpQ = np.einsum("ntd,ntsd->nts", dout, E)
+    # per-bucket streams, flat layout [N*S, T(, D)] as race_pref.cpp expects
+    w_flat = pK.transpose(0, 2, 1).reshape(N * S, T)
+    V_flat = np.broadcast_to(v[:, None], (N, S, T, D)).reshape(N * S, T, D)
+    gE = (pQ.transpose(0, 2, 1)[..., None] * dout[:, None]).reshape(N * S, T, D)
+    gw, gV = prefix_mean_flat_backward(w_flat, V_flat, gE, eps)
+    dpK = gw.reshape(N, S, T).transpose(0, 2, 1)
+    dv = gV.reshape(N, S, T, D).sum(1)
+    dq, dsq = soft_hash_backward(dpQ, pQ, hQ, planes, K, L, scale)
+    dk, dsk = soft_hash_backward(dpK, pK, hK, planes, K, L, scale)
+    return dq, dk, dv, dsq + dsk
+
+
+def forward(q, k, v, planes, K, L, scale, causal, eps=1e-6):
+    if causal:
+        return causal_forward(q, k, v, planes, K, L, scale, eps)
+    return noncausal_forward(q, k, v, planes, K, L, scale, eps)[0]
+
+
+def backward(q, k, v, planes, K, L, scale, causal, dout, eps=1e-6):
+    fn = causal_backward if causal else noncausal_backward
+    return fn(q, k, v, planes, K, L, scale, dout, eps)
+
+
+def rel_l2(a, b) -> float:
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    den = np.linalg.norm(b.ravel())
+    return float(np.linalg.norm((a - b).ravel()) / (den if den > 0 else 1.0))

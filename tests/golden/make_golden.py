@@ -1,0 +1,104 @@
+"""Generate the golden parity vectors from the reference's own torch modules.
+
+Run in the build container, where the reference project is mounted read-only:
+
+    python tests/golden/make_golden.py /path/to/reference
+
+It extracts the class definitions ``BatchedACE`` from ``misc/vit.py``
+(non-causal, lines 888-978) and from ``misc/race.py`` (causal, lines 26-142)
+with ``ast`` -- the files themselves cannot be imported as-is (``misc/race.py:7``
+imports a CPU extension whose loader is broken as shipped) -- runs them in
+float64 under autograd on seeded inputs, and writes the inputs, outputs and
+gradients to ``tests/golden/*.npz``.  The fixtures are what the committed tests
+compare the oracle (and, on a GPU, the CUDA path) against; nothing at test time
+reads the reference tree.
+"""
+from __future__ import annotations
+
+import ast
+import itertools
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def load_class(path: str, name: str):
+    src = open(path).read()
+    tree = ast.parse(src)
+    for node in tree.body:
+        if isinstance(node, ast.ClassDef) and node.name == name:
+            seg = ast.get_source_segment(src, node)
+            ns = {"torch": torch, "nn": nn, "F": F, "itertools": itertools, "math": math}
+            exec(compile(seg, f"{path}:{name}", "exec"), ns)
+            return ns[name]
+    raise KeyError(name)
+
+
+def run_case(cls, *, causal, M, B, T, H, d, K, L, share_planes, logit_temp, seed):
+    torch.manual_seed(seed)
+    ace = cls(d, K, L, M, device="cpu", share_planes=share_planes).double()  # planes drawn in fp32
+    if hasattr(ace, "logit_temp"):
+        with torch.no_grad():
+            ace.logit_temp.fill_(logit_temp)
+    # inputs are drawn in float32 and widened, so the fp32 CUDA path sees the
+    # exact same values the float64 reference run saw
+    x = lambda: torch.randn(B, T, H, d, dtype=torch.float32).double()
+    q, k, v = x(), x(), x()
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    pack = lambda z: z.unsqueeze(0).expand(M, -1, -1, -1, -1)   # misc/vit.py:1022-1028
+    out = ace(pack(k), pack(v), pack(q))                        # [M,B,T,H,d]
+    dout = torch.randn(out.shape, dtype=torch.float32).double()
+    out.backward(dout)
+    planes_T = ace.planes_T.detach()
+    if planes_T.dim() == 2:
+        planes_T = planes_T.unsqueeze(0)
+    planes = planes_T.transpose(1, 2).contiguous()              # [Mp, L*K, d]
+    if causal:
+        scale = math.sqrt(d)                                    # misc/race.py:67
+        dlt = 0.0
+    else:
+        scale = float(torch.tensor(logit_temp).exp().clamp(1e-2, 20.0))   # misc/vit.py:923
+        dlt = float(ace.logit_temp.grad)
+    return dict(
+        q=q.detach().float().numpy(), k=k.detach().float().numpy(),
+        v=v.detach().float().numpy(), planes=planes.float().numpy(),
+        dout=dout.float().numpy(), out=out.detach().numpy(),
+        dq=q.grad.numpy(), dk=k.grad.numpy(), dv=v.grad.numpy(),
+        scale=np.float64(scale), dlogit_temp=np.float64(dlt),
+        meta=np.array([M, B, T, H, d, K, L, int(share_planes), int(causal)], np.int64),
+    )
+
+
+CASES = [
+    # name, causal, M, B, T, H, d, K, L, share_planes, logit_temp
+    ("nc_k2l5_t64", False, 1, 1, 64, 2, 64, 2, 5, False, 0.0),
+    ("nc_k3l3_t37_m2", False, 2, 2, 37, 1, 64, 3, 3, False, math.log(0.5)),
+    ("nc_k2l4_t33_d32_shared", False, 2, 1, 33, 2, 32, 2, 4, True, math.log(3.0)),
+    ("c_k2l5_t48", True, 1, 1, 48, 2, 64, 2, 5, True, 0.0),
+    ("c_k3l2_t29_m2_indep", True, 2, 1, 29, 2, 64, 3, 2, False, 0.0),
+    ("c_k1l8_t17_d32", True, 1, 2, 17, 1, 32, 1, 8, True, 0.0),
+]
+
+
+def main(ref_root: str):
+    vit_cls = load_class(os.path.join(ref_root, "misc/vit.py"), "BatchedACE")
+    race_cls = load_class(os.path.join(ref_root, "misc/race.py"), "BatchedACE")
+    for i, (name, causal, M, B, T, H, d, K, L, sp, lt) in enumerate(CASES):
+        cls = race_cls if causal else vit_cls
+        res = run_case(cls, causal=causal, M=M, B=B, T=T, H=H, d=d, K=K, L=L,
+                       share_planes=sp, logit_temp=lt, seed=i)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **res)
+        print("wrote", path, os.path.getsize(path))
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -1,0 +1,89 @@
+"""The oracle (oracle/race_oracle.py) reproduces the reference's torch modules.
+
+Golden vectors come from the reference's own ``BatchedACE`` classes run under
+autograd in float64 (tests/golden/make_golden.py).  These tests pin the oracle
+before any GPU test trusts it.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import race_oracle as O
+from tests import golden_util as G
+
+
+@pytest.mark.parametrize("path", G.golden_files(), ids=lambda p: p.split("/")[-1][:-4])
+def test_oracle_matches_reference_modules(path):
+    g = G.load(path)
+    q, k, v = G.inputs_as_streams(g)
+    P = G.stream_planes(g)
+    M, B, H = g["M"], g["B"], g["H"]
+    scale = float(g["scale"])
+    out = O.forward(q, k, v, P, g["K"], g["L"], scale, g["causal"])
+    np.testing.assert_allclose(G.from_streams(out, M, B, H), g["out"], rtol=1e-10, atol=1e-12)
+
+    dout = G.to_streams(g["dout"])
+    dq, dk, dv, dscale = O.backward(q, k, v, P, g["K"], g["L"], scale, g["causal"], dout)
+    # the reference expands q/k/v over M ensembles, so its gradients are sums over m
+    red = lambda x: G.from_streams(x, M, B, H).sum(0)
+    np.testing.assert_allclose(red(dq), g["dq"], rtol=1e-9, atol=1e-11)
+    np.testing.assert_allclose(red(dk), g["dk"], rtol=1e-9, atol=1e-11)
+    np.testing.assert_allclose(red(dv), g["dv"], rtol=1e-9, atol=1e-11)
+    if not g["causal"]:
+        # d logit_temp = d scale * scale while exp(logit_temp) is inside the clamp
+        assert math.isclose(dscale * scale, float(g["dlogit_temp"]), rel_tol=1e-9, abs_tol=1e-12)
+
+
+def test_causal_last_token_equals_noncausal():
+    rng = np.random.default_rng(0)
+    N, T, D, K, L = 2, 19, 16, 2, 3
+    q, k, v = (rng.standard_normal((N, T, D)) for _ in range(3))
+    P = rng.standard_normal((N, K * L, D))
+    c = O.causal_forward(q, k, v, P, K, L, 1.3)
+    nc = O.noncausal_forward(q, k, v, P, K, L, 1.3)[0]
+    np.testing.assert_allclose(c[:, -1], nc[:, -1], rtol=1e-12)
+
+
+def test_backward_matches_finite_differences():
+    rng = np.random.default_rng(1)
+    N, T, D, K, L = 1, 7, 8, 2, 2
+    q, k, v = (rng.standard_normal((N, T, D)) for _ in range(3))
+    P = rng.standard_normal((N, K * L, D))
+    dout = rng.standard_normal((N, T, D))
+    for causal in (False, True):
+        f = lambda q_, k_, v_, s_: float((O.forward(q_, k_, v_, P, K, L, s_, causal) * dout).sum())
+        dq, dk, dv, ds = O.backward(q, k, v, P, K, L, 0.7, causal, dout)
+        h = 1e-6
+        for arr, grad, which in ((q, dq, 0), (k, dk, 1), (v, dv, 2)):
+            idx = (0, 3, 5)
+            a1, a2 = arr.copy(), arr.copy()
+            a1[idx] += h
+            a2[idx] -= h
+            args1 = [q, k, v]
+            args2 = [q, k, v]
+            args1[which], args2[which] = a1, a2
+            num = (f(*args1, 0.7) - f(*args2, 0.7)) / (2 * h)
+            assert math.isclose(num, grad[idx], rel_tol=1e-5, abs_tol=1e-7)
+        num = (f(q, k, v, 0.7 + h) - f(q, k, v, 0.7 - h)) / (2 * h)
+        assert math.isclose(num, ds, rel_tol=1e-5, abs_tol=1e-7)
+
+
+def test_oracle_prefix_mean_matches_reference_cpp():
+    """Pin the causal restatement on the reference's own compiled C++ kernel."""
+    from oracle.ref_loader import load_race_pref
+    rp = load_race_pref()
+    if rp is None:
+        pytest.skip("oracle/_ref/race_pref not built (make -C oracle)")
+    import torch
+    g = torch.Generator().manual_seed(0)
+    NS, T, D = 12, 300, 16
+    w = torch.rand(NS, T, generator=g)
+    V = torch.randn(NS, T, D, generator=g)
+    gE = torch.randn(NS, T, D, generator=g)
+    E = rp.race_prefix_mean_flat(w, V, 1e-6)
+    np.testing.assert_allclose(E.numpy(), O.prefix_mean_flat(w.numpy(), V.numpy()), rtol=2e-6, atol=2e-6)
+    gw, gV = rp.race_prefix_mean_flat_bw(w, V, gE, 1e-6)
+    ow, oV = O.prefix_mean_flat_backward(w.numpy(), V.numpy(), gE.numpy())
+    assert O.rel_l2(gw.numpy(), ow) < 1e-6
+    assert O.rel_l2(gV.numpy(), oV) < 1e-6
