@@ -1,0 +1,443 @@
+#!/usr/bin/env python
+"""RACE attention fwd+bwd throughput on B200 (tokens/s) and % of HBM roofline.
+
+Workload (the reference's long-context scaling config): B=1, H=1, d=64, K=2,
+L=5, 2^20 tokens per GPU, q/k/v/dO ~ N(0,1) from seed 0, one sequence
+sharded along the tokens over the GPUs (weak scaling: every GPU holds 2^20
+tokens; bucket states are all-reduced over NCCL).  The headline line is the
+non-causal float32 layer; causal and bfloat16 variants are measured in the
+same run and reported under "variants".
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one forward + backward of the layer over the resident inputs.
+Inputs (256 MiB per tensor in fp32) are larger than the 126 MB L2, so no L2
+flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D, K, L = 64, 2, 5
+S = L << K
+TOKENS = 1 << 20
+METRIC = "RACE attn fwd+bwd tokens/s at N=1M (d=64, K=2, L=5)"
+CPU_SAMPLE_TOKENS = 1 << 16
+
+
+# --------------------------------------------------------------------------- helpers
+def load_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# --------------------------------------------------------------------------- our arm
+class Layer:
+    """Preallocated buffers + the C-ABI calls of one fwd+bwd step."""
+
+    def __init__(self, causal, dtype, tokens, group, device, seed):
+        from race_attention_b200 import _lib
+        from race_attention_b200.functional import Buffers, make_desc, query
+        self.lib = _lib.load()
+        self.causal, self.dtype, self.group = causal, dtype, group
+        g = torch.Generator(device=device).manual_seed(seed)
+        shape = (1, 1, tokens, 1, D)
+        rnd = lambda: torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(dtype)
+        self.q, self.k, self.v, self.dout = rnd(), rnd(), rnd(), rnd()
+        g0 = torch.Generator(device=device).manual_seed(0)   # identical planes on every rank
+        self.planes = torch.randn((1, K * L, D), generator=g0, device=device)
+        self.scale = torch.tensor(1.0, device=device)
+        self.desc = make_desc(shape, dtype, K, L, causal, 1e-6, 0, True)
+        self.sizes = query(self.desc)
+        self.buf = Buffers(self.sizes, device)
+        self.out = torch.empty(shape, dtype=dtype, device=device)
+        self.dq, self.dk, self.dv = (torch.empty(shape, dtype=dtype, device=device) for _ in range(3))
+        self.dscale = torch.empty((), device=device)
+        self.state = self.buf.floats(self.sizes.state_bytes)
+        self.gstate = self.buf.floats(self.sizes.gstate_bytes)
+        self.ws = self.buf.workspace()
+        self.tokens = tokens
+
+    def phases(self):
+        """The step as its four C-ABI phases (+ collectives when sharded)."""
+        from race_attention_b200._lib import check
+        from race_attention_b200.functional import _ptr, _rt, _stream
+        from race_attention_b200 import sequence_parallel as sp
+        lib, d = self.lib, self.desc
+        q, k, v, o = _rt(self.q), _rt(self.k), _rt(self.v), _rt(self.out)
+        P, sc, st, gs, ws, n = (_ptr(self.planes), _ptr(self.scale), _ptr(self.state),
+                                _ptr(self.gstate), _ptr(self.ws), self.ws.numel())
+        total = self.buf.floats(self.sizes.total_bytes) if self.causal else None
+        gtotal = self.buf.floats(self.sizes.total_bytes) if self.causal else None
+
+        def f_reduce():
+            check(lib.race_forward_reduce(d, k, v, P, sc, st, _ptr(total), ws, n, _stream()))
+            if self.group is not None:
+                add = lambda off: check(lib.race_add_offset(d, st, _ptr(off), 0, _stream()))
+                sp.exchange_forward_state(self.state, total, self.causal, self.group, add)
+
+        def f_readout():
+            check(lib.race_forward_readout(d, q, k, v, P, sc, st, o, ws, n, _stream()))
+
+        def b_q():
+            check(lib.race_backward_q(d, q, k, v, P, sc, st, _rt(self.dout), _rt(self.dq),
+                                      _ptr(self.dscale), gs, _ptr(gtotal), ws, n, _stream()))
+            if self.group is not None:
+                slots = self.gstate[: self.state.numel()] if self.causal else self.gstate
+                add = lambda off: check(lib.race_add_offset(d, gs, _ptr(off), 1, _stream()))
+                sp.exchange_backward_state(slots, gtotal, self.causal, self.group, add)
+
+        def b_kv():
+            check(lib.race_backward_kv(d, q, k, v, P, sc, st, gs, _rt(self.dout), _rt(self.dk),
+                                       _rt(self.dv), _ptr(self.dscale), ws, n, _stream()))
+            if self.group is not None:
+                torch.distributed.all_reduce(self.dscale, group=self.group)
+
+        return [("forward_reduce", f_reduce), ("forward_readout", f_readout),
+                ("backward_q", b_q), ("backward_kv", b_kv)]
+
+    def step(self):
+        for _, fn in self.phases():
+            fn()
+
+    def kernels_per_step(self):
+        # nc: reduce+sum, readout, bwd_q+sum+dscale, bwd_kv+dscale
+        # causal: totals+scan, fwd, bwd_q+scan+dscale, bwd_kv+dscale
+        n = 8
+        if self.group is not None and self.causal:
+            n += 2   # the two offset adds
+        return n
+
+    def phase_bytes(self):
+        """Algorithmic HBM bytes per token of each phase (I/O of the function)."""
+        e = torch.tensor([], dtype=self.dtype).element_size() * D
+        if self.causal:
+            return {"forward_reduce": 2 * e, "forward_readout": 4 * e, "backward_q": 5 * e,
+                    "backward_kv": 6 * e}
+        return {"forward_reduce": 2 * e, "forward_readout": 2 * e, "backward_q": 3 * e,
+                "backward_kv": 4 * e}
+
+
+def timed(fn, steps, warmup, group, device):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    if group is not None:
+        torch.distributed.barrier(group)
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1)
+    if group is not None:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
+        ms = float(t.item())
+        torch.distributed.barrier(group)
+    return ms / steps
+
+
+def phase_times(layer, steps, device):
+    """Average per-phase device time (CUDA events on the launching stream)."""
+    stream = torch.cuda.current_stream(device)
+    names = [n for n, _ in layer.phases()]
+    acc = {n: 0.0 for n in names}
+    for _ in range(steps):
+        evs = []
+        for name, fn in layer.phases():
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            evs.append((name, a, b))
+        torch.cuda.synchronize(device)
+        for name, a, b in evs:
+            acc[name] += a.elapsed_time(b)
+    return {n: acc[n] / steps for n in names}
+
+
+def e2e_rate(causal, dtype, tokens, steps, device):
+    """Same metric through the public autograd API with pinned HOST buffers:
+    H2D of q, k, v, dO and D2H of out, dq, dk, dv inside the timed region."""
+    from race_attention_b200 import race_attention
+    g = torch.Generator().manual_seed(1)
+    shape = (1, tokens, 1, D)
+    host = [torch.randn(shape, generator=g).to(dtype).pin_memory() for _ in range(4)]
+    outs = [torch.empty(shape, dtype=dtype).pin_memory() for _ in range(4)]
+    planes = torch.randn((1, K * L, D), generator=torch.Generator().manual_seed(0)).to(device)
+    lt = torch.zeros((), device=device, requires_grad=True)
+
+    def step():
+        q, k, v, do = (h.to(device, non_blocking=True) for h in host)
+        for t in (q, k, v):
+            t.requires_grad_(True)
+        out = race_attention(q, k, v, planes, K, L, lt.exp().clamp(1e-2, 20.0), causal=causal)
+        out.backward(do)
+        for dst, src in zip(outs, (out, q.grad, k.grad, v.grad)):
+            dst.copy_(src.detach(), non_blocking=True)
+        lt.grad = None
+
+    step()
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize(device)
+    dt = (time.perf_counter() - t0) / steps
+    nbytes = tokens * D * torch.tensor([], dtype=dtype).element_size() * 4
+    return {"value": tokens / dt, "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
+            "d2h_bytes_per_step": nbytes, "steps": steps}
+
+
+def cpu_rate(causal, tokens, budget_s=10.0, iters_max=50):
+    """Reference op sequence on the host cores (float32, all threads)."""
+    from oracle import torch_ref
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(1, tokens, D, generator=g).requires_grad_(True) for _ in range(3))
+    dout = torch.randn(1, tokens, D, generator=g)
+    planes_T = torch.randn(K * L, D, generator=g).T
+    protos = torch_ref.protos_T(K)
+    scale = torch.tensor(1.0)
+    torch_ref.fwd_bwd(q, k, v, planes_T, K, L, scale, protos, dout, causal)   # warm-up
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < iters_max and (time.perf_counter() - t_start) < budget_s:
+        t0 = time.perf_counter()
+        torch_ref.fwd_bwd(q, k, v, planes_T, K, L, scale, protos, dout, causal)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": tokens / med, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{'causal' if causal else 'non-causal'} fp32 fwd+bwd, B1 H1 T={tokens} "
+                      f"d{D} K{K} L{L}, torch CPU restatement of the reference op sequence, "
+                      f"median of {len(times)}"}
+
+
+def run_ours(args):
+    world, rank, local = dist_env()
+    group = None
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+        group = torch.distributed.group.WORLD
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+    peak, peak_kind = load_peak()
+
+    configs = [(False, torch.float32), (True, torch.float32), (False, torch.bfloat16),
+               (True, torch.bfloat16)]
+    results = []
+    head = None
+    clocks = None
+    for i, (causal, dtype) in enumerate(configs):
+        layer = Layer(causal, dtype, args.tokens, group, device, seed=1000 + rank)
+        sampler = ClockSampler(device.index) if (i == 0 and rank == 0) else None
+        if sampler:
+            sampler.__enter__()
+        ms = timed(layer.step, args.steps, args.warmup, group, device)
+        if sampler:
+            sampler.__exit__()
+            clocks = sampler.summary()
+        total_tokens = args.tokens * world
+        esize = torch.tensor([], dtype=dtype).element_size()
+        rec = {"causal": causal, "dtype": "f32" if dtype == torch.float32 else "bf16",
+               "value": total_tokens / (ms / 1e3), "ms_per_step": ms,
+               "step_roofline_frac": (args.tokens * 11 * D * esize / (ms / 1e3) / 1e9) / peak}
+        if world == 1:
+            ph = phase_times(layer, max(3, args.steps // 2), device)
+            pb = layer.phase_bytes()
+            rec["phases_ms"] = ph
+            dom = max(ph, key=ph.get)
+            ach = pb[dom] * args.tokens / (ph[dom] / 1e3) / 1e9
+            rec["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak,
+                               "unit": "GB/s", "frac": ach / peak, "traffic": None,
+                               "peak_kind": peak_kind}
+        rec["gpu_launches_per_step"] = layer.kernels_per_step()
+        results.append(rec)
+        if i == 0:
+            head = (layer, rec)
+        else:
+            del layer
+        torch.cuda.empty_cache()
+
+    layer, rec = head
+    line = {
+        "metric": METRIC, "value": rec["value"], "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": rec["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: q,k,v,dO ~ N(0,1), hyperplanes ~ N(0,1), seed 0",
+        "config": {"workload": "single non-causal RACE layer fwd+bwd, sequence-sharded",
+                   "batch": 1, "heads": 1, "tokens_per_gpu": args.tokens,
+                   "tokens_total": args.tokens * world, "head_dim": D, "K": K, "L": L,
+                   "temperature": 1.0, "parallelism": f"seq{world}",
+                   "l2": "inputs larger than L2 (q,k,v,dO 256 MiB each in fp32), no flush"},
+        "gpu_launches": rec["gpu_launches_per_step"] * args.steps,
+        "clocks": clocks,
+        "variants": results[1:],
+        "step_roofline_frac": rec["step_roofline_frac"],
+    }
+    if world == 1:
+        line["roofline"] = rec["roofline"]
+        line["phases_ms"] = rec["phases_ms"]
+    del layer
+    torch.cuda.empty_cache()
+    if rank == 0 and not args.no_e2e:
+        line["e2e"] = e2e_rate(False, torch.float32, args.tokens, args.e2e_steps, device)
+    if world > 1:
+        torch.distributed.barrier()
+    if rank == 0 and not args.no_cpu and world == 1:
+        line["cpu_baseline"] = cpu_rate(False, CPU_SAMPLE_TOKENS)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    tokens = CPU_SAMPLE_TOKENS
+    from oracle import torch_ref
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(1, tokens, D, generator=g).requires_grad_(True) for _ in range(3))
+    dout = torch.randn(1, tokens, D, generator=g)
+    planes_T = torch.randn(K * L, D, generator=g).T
+    protos = torch_ref.protos_T(K)
+    scale = torch.tensor(1.0)
+    for _ in range(args.warmup):
+        torch_ref.fwd_bwd(q, k, v, planes_T, K, L, scale, protos, dout, False)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        torch_ref.fwd_bwd(q, k, v, planes_T, K, L, scale, protos, dout, False)
+    dt = (time.perf_counter() - t0) / args.steps
+    val = tokens / dt
+    sample = (f"non-causal fp32 fwd+bwd, B1 H1 T={tokens} (bounded sample of the 2^20-token "
+              f"workload) d{D} K{K} L{L}: torch CPU restatement of the reference op sequence")
+    line = {
+        "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+        "data": "synthetic: q,k,v,dO ~ N(0,1), seed 0",
+        "config": {"workload": "single non-causal RACE layer fwd+bwd, sequence-sharded",
+                   "batch": 1, "heads": 1, "tokens_per_gpu": args.tokens, "head_dim": D,
+                   "K": K, "L": L, "parallelism": f"seq{world}",
+                   "l2": "host run"},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+/*
+ * race_b200.h -- C ABI of the B200 (sm_100a) RACE attention library.
+ *
+ * RACE attention soft-hashes queries and keys onto L tables of K seeded random
+ * hyperplanes (R = 2^K buckets per table, S = L*R buckets in all), aggregates
+ * the values into per-bucket [V | 1] states and reads them back out per query.
+ * Both the non-causal form and the causal per-bucket prefix-mean form are
+ * provided, forward and backward (the backward recomputes the bucket
+ * probabilities instead of storing them).
+ *
+ * Conventions
+ *   - All pointers are device pointers unless stated otherwise.  Nothing in
+ *     this library allocates device memory: the caller passes every buffer,
+ *     sized by race_query().
+ *   - Work is stream-ordered on the cudaStream_t the caller passes.  Entry
+ *     points return a race_status_t; they never throw or abort.
+ *   - Streams of the computation (one per ensemble m, batch b, head h) are
+ *     numbered n = (m * B + b) * H + h.  q/k/v/out and every gradient are
+ *     addressed through race_tensor_t strides, so [B,T,H,d] activations (the
+ *     layout of a Linear output viewed per head) are consumed in place and the
+ *     ensemble dimension may have stride 0 (an expanded view).
+ *   - Planes are float32 [Mp][L*K][d] (Mp = 1 when shared by all ensembles,
+ *     else M), i.e. the transpose of the reference's planes_T buffer.
+ *   - `scale` is a device pointer to the float32 temperature divisor (the
+ *     reference's exp(logit_temp).clamp(...) or sqrt(d)), so a learnable
+ *     temperature never forces a host synchronisation.
+ *
+ * State buffers
+ *   A "slot" is the [S][d] bucket sum B followed by the [S] bucket mass A,
+ *   padded to a multiple of 4 floats (race_sizes_t.slot_floats).
+ *   non-causal: state  = N slots (totals over this rank's tokens, then over
+ *                all ranks after the caller's all-reduce);
+ *               gstate = N slots of dE = sum_t pQ(t) dO(t).
+ *   causal:     state  = N * num_chunks slots holding the EXCLUSIVE prefix at
+ *                the start of every chunk; gstate = N * num_chunks gradient
+ *                slots (exclusive suffix sums) followed by per-token alpha.
+ *
+ * Single GPU: race_forward() then race_backward().  Sequence-sharded multi-GPU
+ * (each rank holds a contiguous token range of every stream): the split entry
+ * points below, with the caller's collective in between (see each comment).
+ */
+#ifndef RACE_B200_H
+#define RACE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RACE_ABI_VERSION 1
+
+typedef enum {
+  RACE_OK = 0,
+  RACE_ERR_INVALID = 1,      /* bad descriptor field or null pointer            */
+  RACE_ERR_UNSUPPORTED = 2,  /* shape outside what the kernels are built for    */
+  RACE_ERR_ALIGN = 3,        /* pointer or stride breaks the vector alignment   */
+  RACE_ERR_WORKSPACE = 4,    /* workspace smaller than race_query() asked for   */
+  RACE_ERR_CUDA = 5          /* a CUDA launch failed (see race_last_cuda_error) */
+} race_status_t;
+
+typedef enum { RACE_F32 = 0, RACE_BF16 = 1 } race_dtype_t;
+
+/* One activation tensor: element strides of the (m, b, h, t) axes; the head
+ * dimension is contiguous. */
+typedef struct {
+  void* data;
+  int64_t stride_m, stride_b, stride_h, stride_t;
+} race_tensor_t;
+
+typedef struct {
+  int32_t dtype;          /* race_dtype_t of q, k, v, out and all gradients     */
+  int32_t causal;         /* 0: non-causal (misc/vit.py), 1: prefix mean         */
+  int32_t head_dim;       /* d: 32 or 64                                         */
+  int32_t num_bits;       /* K hyperplanes per table (R = 2^K)                   */
+  int32_t num_tables;     /* L tables; S = L * 2^K <= 32, L*K <= 16              */
+  int32_t ensembles;      /* M                                                   */
+  int32_t batch;          /* B                                                   */
+  int32_t heads;          /* H                                                   */
+  int64_t tokens;         /* T held by this rank                                 */
+  int32_t chunk;          /* causal chunk length, 0 = chosen by the library      */
+  int32_t shared_planes;  /* 1: planes [1][L*K][d]; 0: planes [M][L*K][d]        */
+  float eps;              /* added to the bucket mass (reference: 1e-6)          */
+} race_desc_t;
+
+typedef struct {
+  size_t state_bytes;      /* forward -> backward saved state                   */
+  size_t gstate_bytes;     /* backward_q -> backward_kv gradient state          */
+  size_t workspace_bytes;  /* scratch, contents not preserved between calls     */
+  size_t total_bytes;      /* one [N] slot array (causal rank totals/offsets)   */
+  int32_t slot_floats;     /* floats per state slot                             */
+  int32_t chunk;           /* causal chunk length in use                        */
+  int64_t num_chunks;      /* causal chunks per stream                          */
+} race_sizes_t;
+
+const char* race_version(void);
+const char* race_strerror(int status);
+/* Text of the last CUDA error seen by this library on the calling thread. */
+const char* race_last_cuda_error(void);
+
+/* Validates the descriptor and reports the buffer sizes for it. */
+int race_query(const race_desc_t* desc, race_sizes_t* sizes);
+
+/* Full forward on one GPU.  Replaces the reference's BatchedACE.forward
+ * (misc/vit.py:918-978 non-causal; misc/race.py:63-142 causal) and the
+ * unbound host function race_fused_fwd (kernels/gpu/forward_kernel.cu:64-96).
+ * Writes out and the saved state. */
+int race_forward(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
+                 race_tensor_t v, const float* planes, const float* scale,
+                 race_tensor_t out, float* state, void* workspace,
+                 size_t workspace_bytes, cudaStream_t stream);
+
+/* Full backward on one GPU.  Replaces autograd through BatchedACE.forward and
+ * the reference's race_bwd_kq_noscan / race_bwd_v_noscan
+ * (kernels/gpu/backward_kernels.cu:145-255) and race_prefix_mean_flat_bw
+ * (kernels/cpu/race_pref.cpp:104-220).  Writes dq, dk, dv and the gradient of
+ * the temperature divisor into *dscale (device float). */
+int race_backward(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
+                  race_tensor_t v, const float* planes, const float* scale,
+                  const float* state, race_tensor_t dout, race_tensor_t dq,
+                  race_tensor_t dk, race_tensor_t dv, float* dscale,
+                  float* gstate, void* workspace, size_t workspace_bytes,
+                  cudaStream_t stream);
+
+/* ---- split phases for sequence-sharded runs ------------------------------
+ * forward:  race_forward_reduce -> [caller collective] -> race_forward_readout
+ *   non-causal: state holds this rank's bucket sums; the caller all-reduces
+ *               the whole state buffer (sum) before the readout.
+ *   causal:     state holds rank-local chunk prefixes and `total` (N slots)
+ *               the rank's totals; the caller gathers all ranks' totals, sums
+ *               those of LOWER ranks into an offset (N slots) and calls
+ *               race_add_offset(state, offset) before the readout.
+ * backward: race_backward_q -> [caller collective] -> race_backward_kv
+ *   non-causal: gstate holds this rank's dE; the caller all-reduces it.
+ *   causal:     gstate holds rank-local chunk suffixes and `total` the rank's
+ *               gradient totals; the caller sums those of HIGHER ranks into
+ *               an offset and calls race_add_offset(gstate, offset).
+ *   race_backward_q overwrites *dscale with the query-side part;
+ *   race_backward_kv adds the key-side part.  Each rank's *dscale covers its
+ *   own tokens (sum it across ranks like any parameter gradient). */
+int race_forward_reduce(const race_desc_t* desc, race_tensor_t k,
+                        race_tensor_t v, const float* planes,
+                        const float* scale, float* state, float* total,
+                        void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream);
+int race_forward_readout(const race_desc_t* desc, race_tensor_t q,
+                         race_tensor_t k, race_tensor_t v, const float* planes,
+                         const float* scale, const float* state,
+                         race_tensor_t out, void* workspace,
+                         size_t workspace_bytes, cudaStream_t stream);
+int race_backward_q(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
+                    race_tensor_t v, const float* planes, const float* scale,
+                    const float* state, race_tensor_t dout, race_tensor_t dq,
+                    float* dscale, float* gstate, float* total,
+                    void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream);
+int race_backward_kv(const race_desc_t* desc, race_tensor_t q,
+                     race_tensor_t k, race_tensor_t v, const float* planes,
+                     const float* scale, const float* state,
+                     const float* gstate, race_tensor_t dout, race_tensor_t dk,
+                     race_tensor_t dv, float* dscale, void* workspace,
+                     size_t workspace_bytes, cudaStream_t stream);
+/* Causal only: adds offset (N slots) to every chunk slot of `slots`
+ * (state or gstate).  Gradient slots also carry the per-chunk key mass,
+ * which the offset does not touch. */
+int race_add_offset(const race_desc_t* desc, float* slots, const float* offset,
+                    int is_gradient, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RACE_B200_H */

@@ -1,0 +1,103 @@
+"""ctypes binding of librace_b200.so (the C ABI declared in include/race_b200.h).
+
+The library is the only compute path: if it is missing or cannot be loaded
+the error propagates; there is no CPU or PyTorch fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "librace_b200.so")
+
+RACE_OK = 0
+RACE_F32 = 0
+RACE_BF16 = 1
+
+SYMBOLS = (
+    "race_version", "race_strerror", "race_last_cuda_error", "race_query",
+    "race_forward", "race_backward", "race_forward_reduce", "race_forward_readout",
+    "race_backward_q", "race_backward_kv", "race_add_offset",
+)
+
+
+class RaceTensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("stride_m", ctypes.c_int64),
+                ("stride_b", ctypes.c_int64), ("stride_h", ctypes.c_int64),
+                ("stride_t", ctypes.c_int64)]
+
+
+class RaceDesc(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("causal", ctypes.c_int32),
+                ("head_dim", ctypes.c_int32), ("num_bits", ctypes.c_int32),
+                ("num_tables", ctypes.c_int32), ("ensembles", ctypes.c_int32),
+                ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("tokens", ctypes.c_int64), ("chunk", ctypes.c_int32),
+                ("shared_planes", ctypes.c_int32), ("eps", ctypes.c_float)]
+
+
+class RaceSizes(ctypes.Structure):
+    _fields_ = [("state_bytes", ctypes.c_size_t), ("gstate_bytes", ctypes.c_size_t),
+                ("workspace_bytes", ctypes.c_size_t), ("total_bytes", ctypes.c_size_t),
+                ("slot_floats", ctypes.c_int32), ("chunk", ctypes.c_int32),
+                ("num_chunks", ctypes.c_int64)]
+
+
+class RaceError(RuntimeError):
+    pass
+
+
+_lib = None
+_lock = threading.Lock()
+
+_T = RaceTensor
+_P = ctypes.c_void_p
+_SIGS = {
+    "race_version": ([], ctypes.c_char_p),
+    "race_strerror": ([ctypes.c_int], ctypes.c_char_p),
+    "race_last_cuda_error": ([], ctypes.c_char_p),
+    "race_query": ([ctypes.POINTER(RaceDesc), ctypes.POINTER(RaceSizes)], ctypes.c_int),
+    "race_forward": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _T, _P, _P, ctypes.c_size_t, _P],
+                     ctypes.c_int),
+    "race_backward": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _P, _T, _T, _T, _T, _P, _P, _P,
+                       ctypes.c_size_t, _P], ctypes.c_int),
+    "race_forward_reduce": ([ctypes.POINTER(RaceDesc), _T, _T, _P, _P, _P, _P, _P, ctypes.c_size_t,
+                             _P], ctypes.c_int),
+    "race_forward_readout": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _P, _T, _P,
+                              ctypes.c_size_t, _P], ctypes.c_int),
+    "race_backward_q": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _P, _T, _T, _P, _P, _P, _P,
+                         ctypes.c_size_t, _P], ctypes.c_int),
+    "race_backward_kv": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _P, _P, _T, _T, _T, _P, _P,
+                          ctypes.c_size_t, _P], ctypes.c_int),
+    "race_add_offset": ([ctypes.POINTER(RaceDesc), _P, _P, ctypes.c_int, _P], ctypes.c_int),
+}
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load (once) and return the library with its prototypes set."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RaceError(
+                f"{path} is not built; run `python -m race_attention_b200.build` "
+                "(there is no CPU fallback)")
+        lib = ctypes.CDLL(path)
+        for name, (args, res) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = lib
+        return lib
+
+
+def check(rc: int) -> None:
+    if rc != RACE_OK:
+        lib = load()
+        msg = lib.race_strerror(rc).decode()
+        if rc == 5:
+            msg += ": " + lib.race_last_cuda_error().decode()
+        raise RaceError(f"race_b200 error {rc}: {msg}")

@@ -1,0 +1,566 @@
+// race_capi.cu -- the extern "C" boundary of librace_b200.so plus the small
+// fixed-order reduction / scan kernels that sit between the streaming passes.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "race_b200.h"
+#include "race_launch.h"
+
+namespace race {
+namespace {
+
+thread_local char g_cuda_err[256] = "";
+
+int cuda_fail(cudaError_t e) {
+  std::snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", cudaGetErrorName(e),
+                cudaGetErrorString(e));
+  return RACE_ERR_CUDA;
+}
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
+
+// ------------------------------------------------------------ small kernels
+}  // namespace
+
+// out[n][e] = sum_p part[n][p][e] for e < SS, summed in a fixed order.
+__global__ void __launch_bounds__(1024) k_sum_partials(const float* __restrict__ part, int P, int SS,
+                                                       float* __restrict__ out) {
+  __shared__ float red[32][33];
+  const int e = blockIdx.x * 32 + threadIdx.x;
+  const int n = blockIdx.y;
+  float acc = 0.f;
+  if (e < SS)
+    for (int p = threadIdx.y; p < P; p += 32) acc += part[((size_t)n * P + p) * SS + e];
+  red[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && e < SS) {
+    float t = 0.f;
+    for (int i = 0; i < 32; ++i) t += red[i][threadIdx.x];
+    out[(size_t)n * SS + e] = t;
+  }
+}
+
+namespace {
+
+// Exclusive scan over the chunk axis of slots[n][chunk][0..width):
+// forward (prefix over earlier chunks) or reverse (suffix over later chunks).
+// Optionally writes the per-stream totals to total[n][0..width).  One block
+// per (32 columns, stream); warp w owns a contiguous segment of chunks.
+// Running sums are kept in float64.
+__global__ void __launch_bounds__(1024) k_chunk_scan(float* __restrict__ slots, int64_t NC, int SS,
+                                                     int width, int reverse,
+                                                     float* __restrict__ total) {
+  __shared__ double seg_sum[32][33];
+  const int col = blockIdx.x * 32 + threadIdx.x;
+  const int n = blockIdx.y;
+  const int w = threadIdx.y;
+  const int64_t seg = (NC + 31) / 32;
+  const int64_t c0 = min(NC, (int64_t)w * seg), c1 = min(NC, c0 + seg);
+  float* base = slots + (size_t)n * NC * SS + col;
+  const bool live = col < width;
+  double s = 0.0;
+  if (live)
+    for (int64_t ch = c0; ch < c1; ++ch) s += (double)base[(size_t)ch * SS];
+  seg_sum[w][threadIdx.x] = s;
+  __syncthreads();
+  if (w == 0) {
+    double run = 0.0;
+    if (!reverse) {
+      for (int i = 0; i < 32; ++i) {
+        const double x = seg_sum[i][threadIdx.x];
+        seg_sum[i][threadIdx.x] = run;
+        run += x;
+      }
+    } else {
+      for (int i = 31; i >= 0; --i) {
+        const double x = seg_sum[i][threadIdx.x];
+        seg_sum[i][threadIdx.x] = run;
+        run += x;
+      }
+    }
+    if (total != nullptr && live) total[(size_t)n * SS + col] = (float)run;
+  }
+  __syncthreads();
+  if (!live) return;
+  double run = seg_sum[w][threadIdx.x];
+  constexpr int kB = 8;
+  if (!reverse) {
+    for (int64_t ch = c0; ch < c1; ch += kB) {
+      float x[kB];
+#pragma unroll
+      for (int i = 0; i < kB; ++i) x[i] = ch + i < c1 ? base[(size_t)(ch + i) * SS] : 0.f;
+#pragma unroll
+      for (int i = 0; i < kB; ++i)
+        if (ch + i < c1) {
+          base[(size_t)(ch + i) * SS] = (float)run;
+          run += (double)x[i];
+        }
+    }
+  } else {
+    for (int64_t ch = c1 - 1; ch >= c0; ch -= kB) {
+      float x[kB];
+#pragma unroll
+      for (int i = 0; i < kB; ++i) x[i] = ch - i >= c0 ? base[(size_t)(ch - i) * SS] : 0.f;
+#pragma unroll
+      for (int i = 0; i < kB; ++i)
+        if (ch - i >= c0) {
+          base[(size_t)(ch - i) * SS] = (float)run;
+          run += (double)x[i];
+        }
+    }
+  }
+}
+
+// slots[n][chunk][e] += offset[n][e] for e < width.
+__global__ void k_add_offset(float* __restrict__ slots, const float* __restrict__ offset,
+                             int64_t NC, int SS, int width, int64_t total) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i % width;
+    const int64_t rest = i / width;        // n * NC + chunk
+    const int64_t n = rest / NC;
+    slots[rest * SS + e] += offset[n * SS + e];
+  }
+}
+
+// *dscale (=|+=) -(sum of partials) / scale^2, summed in a fixed order.
+__global__ void __launch_bounds__(1024) k_dscale_final(const float* __restrict__ part, int count,
+                                                       const float* __restrict__ scale,
+                                                       float* __restrict__ dscale, int accumulate) {
+  __shared__ float red[32];
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) acc += part[i];
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    const float s = *scale;
+    const float v = -t / (s * s);
+    *dscale = accumulate ? *dscale + v : v;
+  }
+}
+
+// ------------------------------------------------------------ host helpers
+struct Plan {
+  int N, S, LK, SS, width, spad, P, CL;
+  int64_t NC;
+  size_t state_floats, gstate_floats, part_floats, dscale_floats;
+};
+
+bool tensor_ok(const race_tensor_t& t, int elem_bytes) {
+  if (t.data == nullptr) return false;
+  if (reinterpret_cast<uintptr_t>(t.data) % 16 != 0) return false;
+  // each lane touches 4 consecutive elements (2 for the causal dq pass):
+  // every stride must keep 8-byte (bf16) / 16-byte (fp32) alignment
+  const int64_t q = 16 / elem_bytes / (elem_bytes == 2 ? 2 : 1);
+  return t.stride_m % q == 0 && t.stride_b % q == 0 && t.stride_h % q == 0 && t.stride_t % q == 0;
+}
+
+int make_plan(const race_desc_t* d, Plan* p) {
+  if (d == nullptr || p == nullptr) return RACE_ERR_INVALID;
+  if (d->dtype != RACE_F32 && d->dtype != RACE_BF16) return RACE_ERR_INVALID;
+  if (d->num_bits < 1 || d->num_tables < 1 || d->ensembles < 1 || d->batch < 1 || d->heads < 1 ||
+      d->tokens < 0 || d->head_dim < 1 || d->chunk < 0 || !(d->eps >= 0.f))
+    return RACE_ERR_INVALID;
+  if (d->head_dim != 32 && d->head_dim != 64) return RACE_ERR_UNSUPPORTED;
+  if (d->num_bits > 5) return RACE_ERR_UNSUPPORTED;
+  const int S = d->num_tables << d->num_bits;
+  const int LK = d->num_tables * d->num_bits;
+  if (S > 32 || LK > kLKMax) return RACE_ERR_UNSUPPORTED;
+  const int64_t N64 = (int64_t)d->ensembles * d->batch * d->heads;
+  if (N64 > 65535) return RACE_ERR_UNSUPPORTED;   // streams map to gridDim.y
+  p->N = (int)N64;
+  p->S = S;
+  p->LK = LK;
+  p->spad = spad_for(S);
+  const int D = d->head_dim;
+  p->width = S * D + S;
+  p->SS = d->causal ? round_up(S * D + 3 * S, 4) : round_up(S * D + S, 4);
+  const int sms = sm_count();
+  const int64_t T = d->tokens;
+  if (!d->causal) {
+    const int64_t target = (int64_t)sms * 4;
+    int64_t P = (target + p->N - 1) / p->N;
+    const int64_t by_len = T / 512;
+    if (P > by_len) P = by_len;
+    if (P < 1) P = 1;
+    p->P = (int)P;
+    p->CL = 0;
+    p->NC = 0;
+    p->state_floats = (size_t)p->N * p->SS;
+    p->gstate_floats = (size_t)p->N * p->SS;
+    p->part_floats = (size_t)p->N * p->P * p->SS;
+    p->dscale_floats = (size_t)p->N * p->P;
+  } else {
+    int64_t CL = d->chunk;
+    if (CL == 0) {
+      // enough chunks to give every SM two CTAs of token groups
+      const int64_t groups = (int64_t)sms * 2 * (kThreads / (D / 4));
+      CL = (N64 * T + groups - 1) / groups;
+      CL = (CL + 63) / 64 * 64;
+      if (CL < 128) CL = 128;
+      if (CL > 2048) CL = 2048;
+    }
+    if (CL > (1 << 20)) return RACE_ERR_UNSUPPORTED;
+    p->CL = (int)CL;
+    p->NC = T > 0 ? (T + CL - 1) / CL : 1;
+    p->P = 0;
+    const size_t slots = (size_t)p->N * p->NC;
+    p->state_floats = slots * p->SS;
+    p->gstate_floats = slots * p->SS + (size_t)p->N * T * S;
+    p->part_floats = 0;
+    // largest causal grid: C = 2 kernels have the fewest groups per CTA
+    const int64_t g2 = kThreads / (D / 2);
+    p->dscale_floats = (size_t)((slots + g2 - 1) / g2);
+  }
+  return RACE_OK;
+}
+
+size_t ws_bytes(const Plan& p) {
+  return (p.part_floats + (p.dscale_floats + 3) / 4 * 4 + 64) * sizeof(float);
+}
+
+struct Call {
+  Plan plan;
+  Params prm;
+  float* part = nullptr;
+  float* dscale_part = nullptr;
+};
+
+void fill_layout(Layout& l, const race_tensor_t& t) {
+  l.sm = t.stride_m;
+  l.sb = t.stride_b;
+  l.sh = t.stride_h;
+  l.st = t.stride_t;
+}
+
+int prepare(const race_desc_t* d, const float* planes, const float* scale, void* ws,
+            size_t ws_bytes_given, Call* c) {
+  int rc = make_plan(d, &c->plan);
+  if (rc != RACE_OK) return rc;
+  if (planes == nullptr || scale == nullptr) return RACE_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(planes) % 16 != 0) return RACE_ERR_ALIGN;
+  const size_t need = ws_bytes(c->plan);
+  if (ws == nullptr || ws_bytes_given < need) return RACE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(ws) % 16 != 0) return RACE_ERR_ALIGN;
+  c->part = static_cast<float*>(ws);
+  c->dscale_part = c->part + c->plan.part_floats;
+  Params& p = c->prm;
+  std::memset(&p, 0, sizeof(p));
+  p.N = c->plan.N;
+  p.M = d->ensembles;
+  p.B = d->batch;
+  p.H = d->heads;
+  p.T = d->tokens;
+  p.K = d->num_bits;
+  p.L = d->num_tables;
+  p.R = 1 << d->num_bits;
+  p.S = c->plan.S;
+  p.LK = c->plan.LK;
+  p.Mp = d->shared_planes ? 1 : d->ensembles;
+  p.eps = d->eps;
+  p.planes = planes;
+  p.scale = scale;
+  p.part = c->part;
+  p.dscale_part = c->dscale_part;
+  p.P = c->plan.P;
+  p.CL = c->plan.CL;
+  p.NC = c->plan.NC;
+  p.SS = c->plan.SS;
+  return RACE_OK;
+}
+
+int check_tensor(const race_desc_t* d, const race_tensor_t& t) {
+  if (t.data == nullptr) return RACE_ERR_INVALID;
+  return tensor_ok(t, d->dtype == RACE_F32 ? 4 : 2) ? RACE_OK : RACE_ERR_ALIGN;
+}
+
+int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream) {
+  KernelInfo ki;
+  const bool ok = d->dtype == RACE_F32 ? kernels_f32(d->head_dim, c.plan.spad, id, &ki)
+                                       : kernels_bf16(d->head_dim, c.plan.spad, id, &ki);
+  if (!ok) return RACE_ERR_UNSUPPORTED;
+  dim3 grid;
+  if (id == K_NC_REDUCE || id == K_NC_READOUT || id == K_NC_BWD_Q || id == K_NC_BWD_KV) {
+    grid = dim3(c.plan.P, c.plan.N, 1);
+  } else {
+    const int64_t units = (int64_t)c.plan.N * c.plan.NC;
+    grid = dim3((unsigned)((units + ki.groups - 1) / ki.groups), 1, 1);
+  }
+  Params prm = c.prm;
+  void* args[] = {&prm};
+  const cudaError_t e = cudaLaunchKernel(ki.fn, grid, dim3(kThreads), args, ki.smem_bytes, stream);
+  if (e != cudaSuccess) return cuda_fail(e);
+  return RACE_OK;
+}
+
+int post(cudaStream_t) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? RACE_OK : cuda_fail(e);
+}
+
+int sum_partials(const Call& c, float* out, cudaStream_t stream) {
+  dim3 grid((c.plan.SS + 31) / 32, c.plan.N), block(32, 32);
+  k_sum_partials<<<grid, block, 0, stream>>>(c.part, c.plan.P, c.plan.SS, out);
+  return post(stream);
+}
+
+int chunk_scan(const Call& c, float* slots, int reverse, float* total, cudaStream_t stream) {
+  dim3 grid((c.plan.width + 31) / 32, c.plan.N), block(32, 32);
+  k_chunk_scan<<<grid, block, 0, stream>>>(slots, c.plan.NC, c.plan.SS, c.plan.width, reverse,
+                                           total);
+  return post(stream);
+}
+
+int dscale_final(const Call& c, int count, float* dscale, int accumulate, cudaStream_t stream) {
+  k_dscale_final<<<1, 1024, 0, stream>>>(c.dscale_part, count, c.prm.scale, dscale, accumulate);
+  return post(stream);
+}
+
+int64_t causal_grid(const race_desc_t* d, const Call& c, int C) {
+  const int64_t g = kThreads / (d->head_dim / C);
+  const int64_t units = (int64_t)c.plan.N * c.plan.NC;
+  return (units + g - 1) / g;
+}
+
+int zero_fill(void* p, size_t bytes, cudaStream_t stream) {
+  if (bytes == 0 || p == nullptr) return RACE_OK;
+  const cudaError_t e = cudaMemsetAsync(p, 0, bytes, stream);
+  return e == cudaSuccess ? RACE_OK : cuda_fail(e);
+}
+
+#define RACE_TRY(x)                  \
+  do {                               \
+    const int rc_ = (x);             \
+    if (rc_ != RACE_OK) return rc_;  \
+  } while (0)
+
+}  // namespace
+}  // namespace race
+
+using namespace race;
+
+extern "C" {
+
+const char* race_version(void) { return "race_b200 1.0 (sm_100a)"; }
+
+const char* race_strerror(int status) {
+  switch (status) {
+    case RACE_OK: return "ok";
+    case RACE_ERR_INVALID: return "invalid argument";
+    case RACE_ERR_UNSUPPORTED: return "unsupported shape (d in {32,64}, L*2^K <= 32, L*K <= 16, K <= 5)";
+    case RACE_ERR_ALIGN: return "pointer or stride not 16-byte aligned for vector access";
+    case RACE_ERR_WORKSPACE: return "workspace missing or smaller than race_query() reported";
+    case RACE_ERR_CUDA: return "CUDA error (see race_last_cuda_error)";
+    default: return "unknown status";
+  }
+}
+
+const char* race_last_cuda_error(void) { return g_cuda_err; }
+
+int race_query(const race_desc_t* desc, race_sizes_t* sizes) {
+  if (sizes == nullptr) return RACE_ERR_INVALID;
+  Plan p;
+  RACE_TRY(make_plan(desc, &p));
+  sizes->state_bytes = p.state_floats * sizeof(float);
+  sizes->gstate_bytes = p.gstate_floats * sizeof(float);
+  sizes->workspace_bytes = ws_bytes(p);
+  sizes->total_bytes = (size_t)p.N * p.SS * sizeof(float);
+  sizes->slot_floats = p.SS;
+  sizes->chunk = p.CL;
+  sizes->num_chunks = p.NC;
+  return RACE_OK;
+}
+
+int race_forward_reduce(const race_desc_t* desc, race_tensor_t k, race_tensor_t v,
+                        const float* planes, const float* scale, float* state, float* total,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  Call c;
+  RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
+  if (state == nullptr) return RACE_ERR_INVALID;
+  if (desc->tokens == 0) {
+    RACE_TRY(zero_fill(state, c.plan.state_floats * sizeof(float), stream));
+    if (total) RACE_TRY(zero_fill(total, (size_t)c.plan.N * c.plan.SS * sizeof(float), stream));
+    return RACE_OK;
+  }
+  RACE_TRY(check_tensor(desc, k));
+  RACE_TRY(check_tensor(desc, v));
+  fill_layout(c.prm.lk, k);
+  fill_layout(c.prm.lv, v);
+  c.prm.k = k.data;
+  c.prm.v = v.data;
+  if (!desc->causal) {
+    RACE_TRY(launch(desc, c, K_NC_REDUCE, stream));
+    RACE_TRY(sum_partials(c, state, stream));
+    if (total) {
+      const cudaError_t e = cudaMemcpyAsync(total, state, (size_t)c.plan.N * c.plan.SS * 4,
+                                            cudaMemcpyDeviceToDevice, stream);
+      if (e != cudaSuccess) return cuda_fail(e);
+    }
+  } else {
+    c.prm.state_out = state;
+    RACE_TRY(launch(desc, c, K_C_TOTALS, stream));
+    RACE_TRY(chunk_scan(c, state, 0, total, stream));
+  }
+  return RACE_OK;
+}
+
+int race_forward_readout(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                         const float* planes, const float* scale, const float* state,
+                         race_tensor_t out, void* workspace, size_t workspace_bytes,
+                         cudaStream_t stream) {
+  Call c;
+  RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
+  if (state == nullptr) return RACE_ERR_INVALID;
+  if (desc->tokens == 0) return RACE_OK;
+  RACE_TRY(check_tensor(desc, q));
+  RACE_TRY(check_tensor(desc, out));
+  fill_layout(c.prm.lq, q);
+  fill_layout(c.prm.lo, out);
+  c.prm.q = q.data;
+  c.prm.out = out.data;
+  c.prm.state = state;
+  if (!desc->causal) {
+    RACE_TRY(launch(desc, c, K_NC_READOUT, stream));
+  } else {
+    RACE_TRY(check_tensor(desc, k));
+    RACE_TRY(check_tensor(desc, v));
+    fill_layout(c.prm.lk, k);
+    fill_layout(c.prm.lv, v);
+    c.prm.k = k.data;
+    c.prm.v = v.data;
+    RACE_TRY(launch(desc, c, K_C_FWD, stream));
+  }
+  return RACE_OK;
+}
+
+int race_forward(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                 const float* planes, const float* scale, race_tensor_t out, float* state,
+                 void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  RACE_TRY(race_forward_reduce(desc, k, v, planes, scale, state, nullptr, workspace,
+                               workspace_bytes, stream));
+  return race_forward_readout(desc, q, k, v, planes, scale, state, out, workspace, workspace_bytes,
+                              stream);
+}
+
+int race_backward_q(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                    const float* planes, const float* scale, const float* state,
+                    race_tensor_t dout, race_tensor_t dq, float* dscale, float* gstate,
+                    float* total, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  Call c;
+  RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
+  if (state == nullptr || gstate == nullptr || dscale == nullptr) return RACE_ERR_INVALID;
+  if (desc->tokens == 0) {
+    RACE_TRY(zero_fill(gstate, c.plan.gstate_floats * sizeof(float), stream));
+    if (total) RACE_TRY(zero_fill(total, (size_t)c.plan.N * c.plan.SS * sizeof(float), stream));
+    return zero_fill(dscale, sizeof(float), stream);
+  }
+  RACE_TRY(check_tensor(desc, q));
+  RACE_TRY(check_tensor(desc, dout));
+  RACE_TRY(check_tensor(desc, dq));
+  fill_layout(c.prm.lq, q);
+  fill_layout(c.prm.ldo, dout);
+  fill_layout(c.prm.ldq, dq);
+  c.prm.q = q.data;
+  c.prm.dout = dout.data;
+  c.prm.dq = dq.data;
+  c.prm.state = state;
+  if (!desc->causal) {
+    RACE_TRY(launch(desc, c, K_NC_BWD_Q, stream));
+    RACE_TRY(sum_partials(c, gstate, stream));
+    if (total) {
+      const cudaError_t e = cudaMemcpyAsync(total, gstate, (size_t)c.plan.N * c.plan.SS * 4,
+                                            cudaMemcpyDeviceToDevice, stream);
+      if (e != cudaSuccess) return cuda_fail(e);
+    }
+    RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 0, stream));
+  } else {
+    RACE_TRY(check_tensor(desc, k));
+    RACE_TRY(check_tensor(desc, v));
+    fill_layout(c.prm.lk, k);
+    fill_layout(c.prm.lv, v);
+    c.prm.k = k.data;
+    c.prm.v = v.data;
+    c.prm.gstate_out = gstate;
+    c.prm.alpha = gstate + (size_t)c.plan.N * c.plan.NC * c.plan.SS;
+    RACE_TRY(launch(desc, c, K_C_BWD_Q, stream));
+    RACE_TRY(chunk_scan(c, gstate, 1, total, stream));
+    RACE_TRY(dscale_final(c, (int)causal_grid(desc, c, 2), dscale, 0, stream));
+  }
+  return RACE_OK;
+}
+
+int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                     const float* planes, const float* scale, const float* state,
+                     const float* gstate, race_tensor_t dout, race_tensor_t dk, race_tensor_t dv,
+                     float* dscale, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  Call c;
+  RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
+  if (state == nullptr || gstate == nullptr || dscale == nullptr) return RACE_ERR_INVALID;
+  if (desc->tokens == 0) return RACE_OK;
+  RACE_TRY(check_tensor(desc, k));
+  RACE_TRY(check_tensor(desc, v));
+  RACE_TRY(check_tensor(desc, dk));
+  RACE_TRY(check_tensor(desc, dv));
+  fill_layout(c.prm.lk, k);
+  fill_layout(c.prm.lv, v);
+  fill_layout(c.prm.ldk, dk);
+  fill_layout(c.prm.ldv, dv);
+  c.prm.k = k.data;
+  c.prm.v = v.data;
+  c.prm.dk = dk.data;
+  c.prm.dv = dv.data;
+  c.prm.state = state;
+  c.prm.gstate_in = gstate;
+  if (!desc->causal) {
+    RACE_TRY(launch(desc, c, K_NC_BWD_KV, stream));
+    RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 1, stream));
+  } else {
+    RACE_TRY(check_tensor(desc, q));
+    RACE_TRY(check_tensor(desc, dout));
+    fill_layout(c.prm.lq, q);
+    fill_layout(c.prm.ldo, dout);
+    c.prm.q = q.data;
+    c.prm.dout = dout.data;
+    c.prm.alpha = const_cast<float*>(gstate) + (size_t)c.plan.N * c.plan.NC * c.plan.SS;
+    RACE_TRY(launch(desc, c, K_C_BWD_KV, stream));
+    RACE_TRY(dscale_final(c, (int)causal_grid(desc, c, 4), dscale, 1, stream));
+  }
+  return RACE_OK;
+}
+
+int race_backward(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                  const float* planes, const float* scale, const float* state, race_tensor_t dout,
+                  race_tensor_t dq, race_tensor_t dk, race_tensor_t dv, float* dscale,
+                  float* gstate, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  RACE_TRY(race_backward_q(desc, q, k, v, planes, scale, state, dout, dq, dscale, gstate, nullptr,
+                           workspace, workspace_bytes, stream));
+  return race_backward_kv(desc, q, k, v, planes, scale, state, gstate, dout, dk, dv, dscale,
+                          workspace, workspace_bytes, stream);
+}
+
+int race_add_offset(const race_desc_t* desc, float* slots, const float* offset, int is_gradient,
+                    cudaStream_t stream) {
+  Plan p;
+  RACE_TRY(make_plan(desc, &p));
+  (void)is_gradient;  // both slot kinds carry [S][d] sums then [S] masses up front
+  if (!desc->causal || slots == nullptr || offset == nullptr) return RACE_ERR_INVALID;
+  const int64_t total = (int64_t)p.N * p.NC * p.width;
+  if (total == 0) return RACE_OK;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4096);
+  k_add_offset<<<blocks, 256, 0, stream>>>(slots, offset, p.NC, p.SS, p.width, total);
+  return post(stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,37 @@
+// race_launch.h -- internal table of kernel instantiations (host side).
+#pragma once
+#include "race_kernels.cuh"
+
+namespace race {
+
+enum KernelId {
+  K_NC_REDUCE = 0,
+  K_NC_READOUT,
+  K_NC_BWD_Q,
+  K_NC_BWD_KV,
+  K_C_TOTALS,
+  K_C_FWD,
+  K_C_BWD_Q,
+  K_C_BWD_KV,
+  K_COUNT
+};
+
+struct KernelInfo {
+  const void* fn;   // __global__ symbol, launched with one `Params` argument
+  int groups;       // token groups per CTA
+  int smem_bytes;   // dynamic shared memory
+};
+
+// Padded bucket counts the kernels are instantiated for.
+constexpr int kSpadList[] = {8, 16, 20, 24, 32};
+
+inline int spad_for(int S) {
+  for (int s : kSpadList)
+    if (S <= s) return s;
+  return -1;
+}
+
+bool kernels_f32(int D, int spad, KernelId id, KernelInfo* info);
+bool kernels_bf16(int D, int spad, KernelId id, KernelInfo* info);
+
+}  // namespace race

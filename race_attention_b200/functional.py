@@ -1,0 +1,203 @@
+"""Autograd entry point of RACE attention on B200.
+
+``race_attention`` takes q, k, v in the reference's [M, B, T, H, d] layout
+(``BatchedACE.forward`` inputs, misc/vit.py:918 and misc/race.py:63) -- any
+strided view whose head dimension is contiguous, including the stride-0
+ensemble expansion the reference's ``RACEAttention`` builds -- and returns the
+[M, B, T, H, d] output.  Gradients flow to q, k, v and to the temperature
+divisor ``scale``; the hyperplanes are a buffer (misc/vit.py:906-908) and get
+none.  The bucket probabilities are recomputed in the backward pass, never
+stored.
+
+The role of the reference's ``RACEPrefixMeanFlatFn`` (misc/race.py:9-24:
+save the inputs and eps, call the kernel forward / backward) is played by
+``_RaceFunction`` here, one level higher so the hash is fused in.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import RaceDesc, RaceSizes, RaceTensor, check
+
+_SUPPORTED = (torch.float32, torch.bfloat16)
+
+
+def _aligned(x: torch.Tensor) -> bool:
+    if x.stride(-1) != 1 or x.data_ptr() % 16 != 0:
+        return False
+    return all(s % 4 == 0 for s in x.stride()[:-1])
+
+
+def _prep(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    if x.dtype != dtype:
+        x = x.to(dtype)
+    if not _aligned(x):
+        x = x.contiguous()
+        if not _aligned(x):
+            raise ValueError("RACE attention needs head_dim % 4 == 0 and 16-byte aligned storage")
+    return x
+
+
+def _rt(x: Optional[torch.Tensor]) -> RaceTensor:
+    """[M,B,T,H,d] view -> race_tensor_t (strides in (m, b, h, t) order)."""
+    if x is None:
+        return RaceTensor(None, 0, 0, 0, 0)
+    s = x.stride()
+    return RaceTensor(x.data_ptr(), s[0], s[1], s[3], s[2])
+
+
+def _ptr(x: Optional[torch.Tensor]):
+    return None if x is None else x.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def make_desc(shape, dtype, K, L, causal, eps, chunk, shared_planes) -> RaceDesc:
+    M, B, T, H, d = shape
+    return RaceDesc(
+        dtype=_lib.RACE_F32 if dtype == torch.float32 else _lib.RACE_BF16,
+        causal=int(bool(causal)), head_dim=d, num_bits=K, num_tables=L, ensembles=M,
+        batch=B, heads=H, tokens=T, chunk=int(chunk), shared_planes=int(bool(shared_planes)),
+        eps=float(eps))
+
+
+def query(desc: RaceDesc) -> RaceSizes:
+    lib = _lib.load()
+    sz = RaceSizes()
+    check(lib.race_query(desc, sz))
+    return sz
+
+
+class Buffers:
+    """Device buffers one call needs, sized by race_query()."""
+
+    def __init__(self, sizes: RaceSizes, device):
+        self.sizes = sizes
+        self.device = device
+
+    def floats(self, nbytes: int) -> torch.Tensor:
+        return torch.empty(max(1, nbytes // 4), dtype=torch.float32, device=self.device)
+
+    def workspace(self) -> torch.Tensor:
+        return torch.empty(max(16, self.sizes.workspace_bytes), dtype=torch.uint8,
+                           device=self.device)
+
+
+def _scale_tensor(scale, device) -> torch.Tensor:
+    if isinstance(scale, torch.Tensor):
+        return scale
+    return torch.tensor(float(scale), dtype=torch.float32, device=device)
+
+
+class _RaceFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, planes, scale, K, L, causal, eps, chunk, shared_planes, group):
+        if not q.is_cuda:
+            raise RuntimeError("race_attention runs on CUDA devices only (no CPU fallback)")
+        ctx.in_dtypes = (q.dtype, k.dtype, v.dtype)
+        dtype = q.dtype if q.dtype in _SUPPORTED else torch.float32
+        q, k, v = (_prep(t, dtype) for t in (q, k, v))
+        planes = planes.detach().to(torch.float32).contiguous()
+        scale_d = scale.detach().to(torch.float32).reshape(()).contiguous()
+        desc = make_desc(tuple(q.shape), dtype, K, L, causal, eps, chunk, shared_planes)
+        sizes = query(desc)
+        buf = Buffers(sizes, q.device)
+        lib = _lib.load()
+        out = torch.empty(q.shape, dtype=dtype, device=q.device)
+        state = buf.floats(sizes.state_bytes)
+        ws = buf.workspace()
+        if group is None:
+            check(lib.race_forward(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale_d),
+                                   _rt(out), _ptr(state), _ptr(ws), ws.numel(), _stream()))
+        else:
+            from .sequence_parallel import sharded_forward
+            sharded_forward(lib, desc, sizes, buf, q, k, v, planes, scale_d, out, state, ws, group)
+        ctx.save_for_backward(q, k, v, planes, scale_d, state)
+        ctx.desc = desc
+        ctx.group = group
+        ctx.scale_shape = scale.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, planes, scale_d, state = ctx.saved_tensors
+        desc = ctx.desc
+        dtype = q.dtype
+        dout = _prep(dout, dtype)
+        sizes = query(desc)
+        buf = Buffers(sizes, q.device)
+        lib = _lib.load()
+        shape = tuple(q.shape)
+        dq = torch.empty(shape, dtype=dtype, device=q.device)
+        dk = torch.empty(shape, dtype=dtype, device=q.device)
+        dv = torch.empty(shape, dtype=dtype, device=q.device)
+        dscale = torch.empty((), dtype=torch.float32, device=q.device)
+        gstate = buf.floats(sizes.gstate_bytes)
+        ws = buf.workspace()
+        if ctx.group is None:
+            check(lib.race_backward(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale_d),
+                                    _ptr(state), _rt(dout), _rt(dq), _rt(dk), _rt(dv),
+                                    _ptr(dscale), _ptr(gstate), _ptr(ws), ws.numel(), _stream()))
+        else:
+            from .sequence_parallel import sharded_backward
+            sharded_backward(lib, desc, sizes, buf, q, k, v, planes, scale_d, state, dout,
+                             dq, dk, dv, dscale, gstate, ws, ctx.group)
+        dq, dk, dv = (g.to(t) for g, t in zip((dq, dk, dv), ctx.in_dtypes))
+        return (dq, dk, dv, None, dscale.reshape(ctx.scale_shape), None, None, None, None, None,
+                None, None)
+
+
+def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: torch.Tensor,
+                   num_bits: int, num_tables: int, scale=1.0, causal: bool = False,
+                   eps: float = 1e-6, chunk: int = 0, shared_planes: Optional[bool] = None,
+                   group=None) -> torch.Tensor:
+    """RACE attention forward (autograd-aware) on [M, B, T, H, d] inputs.
+
+    Args:
+      q, k, v: [M, B, T, H, d] (4-D [B, T, H, d] is taken as M = 1), float32
+        or bfloat16 (other float types compute in float32).
+      planes: hyperplanes [Mp, L*K, d] (Mp = 1 shared, or M), float32.
+      num_bits: K hyperplanes per table; num_tables: L tables.
+      scale: temperature divisor -- a tensor (learnable: gets a gradient) or a
+        float.  The reference uses exp(logit_temp).clamp(1e-2, 20) for the
+        non-causal module (misc/vit.py:923) and sqrt(d) for the causal one
+        (misc/race.py:67).
+      causal: per-bucket prefix mean (misc/race.py:108-138) instead of the
+        full-sequence bucket mean (misc/vit.py:967-975).
+      eps: added to the bucket mass.
+      chunk: causal work-chunk length (0 = chosen by the library); results do
+        not depend on it beyond float rounding.
+      group: torch.distributed process group across which the token axis is
+        sharded (contiguous ranges in rank order), or None.
+    """
+    squeeze = False
+    if q.dim() == 4:
+        q, k, v = q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0)
+        squeeze = True
+    if q.dim() != 5 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must share one [M, B, T, H, d] shape")
+    M = q.shape[0]
+    if planes.dim() == 2:
+        planes = planes.unsqueeze(0)
+    if shared_planes is None:
+        shared_planes = planes.shape[0] == 1
+    LK = num_bits * num_tables
+    if planes.shape[-2:] != (LK, q.shape[-1]):
+        raise ValueError(f"planes must be [Mp, {LK}, {q.shape[-1]}], got {tuple(planes.shape)}")
+    if not shared_planes and planes.shape[0] != M:
+        raise ValueError("per-ensemble planes need one set per ensemble")
+    scale_t = _scale_tensor(scale, q.device)
+    out = _RaceFunction.apply(q, k, v, planes, scale_t, int(num_bits), int(num_tables),
+                              bool(causal), float(eps), int(chunk), bool(shared_planes), group)
+    return out.squeeze(0) if squeeze else out
+
+
+def default_causal_scale(head_dim: int) -> float:
+    """Fixed divisor of the causal module (misc/race.py:67)."""
+    return math.sqrt(head_dim)

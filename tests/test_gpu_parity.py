@@ -1,0 +1,116 @@
+"""CUDA path vs the oracle and the golden vectors (needs a B200).
+
+Tolerances (relative L2, from the path's specification): 1e-4 for float32
+inputs, 2e-2 for bfloat16 inputs (the oracle then sees the same
+bf16-rounded inputs).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import race_oracle as O
+from tests import golden_util as G
+from tests.cuda_util import bf16_round, run_streams
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-4, torch.bfloat16: 2e-2}
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from race_attention_b200 import _lib
+    _lib.load()   # fails loudly when the extension is missing
+
+
+@pytest.mark.parametrize("path", G.golden_files(), ids=lambda p: p.split("/")[-1][:-4])
+def test_golden(path):
+    """Reference modules' own fp64 outputs/gradients on the same inputs."""
+    from race_attention_b200 import race_attention
+    g = G.load(path)
+    M, B, T, H, d, K, L = (g[x] for x in ("M", "B", "T", "H", "d", "K", "L"))
+    dev = "cuda"
+    q, k, v = (torch.tensor(g[x], device=dev, requires_grad=True) for x in ("q", "k", "v"))
+    pack = lambda z: z.unsqueeze(0).expand(M, -1, -1, -1, -1)
+    planes = torch.tensor(g["planes"], device=dev)
+    if g["causal"]:
+        scale = torch.tensor(float(g["scale"]), device=dev)
+        out = race_attention(pack(q), pack(k), pack(v), planes, K, L, scale, causal=True,
+                             shared_planes=g["share"])
+    else:
+        lt = torch.tensor(math.log(float(g["scale"])), device=dev, requires_grad=True)
+        scale = lt.exp().clamp(1e-2, 20.0)
+        out = race_attention(pack(q), pack(k), pack(v), planes, K, L, scale, causal=False,
+                             shared_planes=g["share"])
+    out.backward(torch.tensor(g["dout"], device=dev))
+    c = lambda t: t.detach().double().cpu().numpy()
+    assert O.rel_l2(c(out), g["out"]) < 1e-4
+    assert O.rel_l2(c(q.grad), g["dq"]) < 1e-4
+    assert O.rel_l2(c(k.grad), g["dk"]) < 1e-4
+    assert O.rel_l2(c(v.grad), g["dv"]) < 1e-4
+    if not g["causal"]:
+        assert math.isclose(float(lt.grad), float(g["dlogit_temp"]), rel_tol=1e-4, abs_tol=1e-6)
+
+
+CASES = [
+    # N, T, d, K, L, causal, chunk
+    (2, 1, 64, 2, 5, False, 0),
+    (3, 7, 64, 2, 5, False, 0),
+    (2, 127, 64, 2, 5, True, 0),
+    (2, 129, 64, 2, 5, True, 64),
+    (1, 785, 64, 4, 2, False, 0),
+    (1, 785, 64, 4, 2, True, 128),
+    (4, 1000, 32, 1, 8, True, 128),
+    (2, 3000, 64, 3, 3, False, 0),
+    (2, 3000, 64, 3, 3, True, 0),
+    (3, 2049, 32, 5, 1, False, 0),
+    (1, 4096, 64, 2, 5, True, 256),
+    (4, 4096, 64, 2, 5, False, 0),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("N,T,d,K,L,causal,chunk", CASES)
+def test_vs_oracle(N, T, d, K, L, causal, chunk, dtype):
+    rng = np.random.default_rng(N * 7919 + T * 31 + d + K * 3 + L)
+    q, k, v, dout = (rng.standard_normal((N, T, d)).astype(np.float32) for _ in range(4))
+    planes = rng.standard_normal((1, K * L, d)).astype(np.float32)
+    scale = 0.8 if causal else 1.3
+    if dtype == torch.bfloat16:
+        q, k, v, dout = (bf16_round(a) for a in (q, k, v, dout))
+    got = run_streams(q, k, v, planes, K, L, scale, causal, dout, dtype=dtype, chunk=chunk)
+    P = np.broadcast_to(planes, (N,) + planes.shape[1:])
+    ref_out = O.forward(q, k, v, P, K, L, scale, causal)
+    dq, dk, dv, ds = O.backward(q, k, v, P, K, L, scale, causal, dout)
+    tol = TOL[dtype]
+    for name, a, b in zip(("out", "dq", "dk", "dv"), got[:4], (ref_out, dq, dk, dv)):
+        assert O.rel_l2(a, b) < tol, (name, O.rel_l2(a, b))
+    assert math.isclose(got[4], ds, rel_tol=10 * tol, abs_tol=1e-3 * tol)
+
+
+def test_deterministic():
+    rng = np.random.default_rng(5)
+    N, T, d, K, L = 2, 5000, 64, 2, 5
+    q, k, v, dout = (rng.standard_normal((N, T, d)).astype(np.float32) for _ in range(4))
+    planes = rng.standard_normal((1, K * L, d)).astype(np.float32)
+    for causal in (False, True):
+        a = run_streams(q, k, v, planes, K, L, 1.0, causal, dout)
+        b = run_streams(q, k, v, planes, K, L, 1.0, causal, dout)
+        for x, y in zip(a[:4], b[:4]):
+            assert np.array_equal(x, y)
+        assert a[4] == b[4]
+
+
+def test_chunk_length_independent():
+    rng = np.random.default_rng(9)
+    N, T, d, K, L = 1, 6000, 64, 2, 5
+    q, k, v, dout = (rng.standard_normal((N, T, d)).astype(np.float32) for _ in range(4))
+    planes = rng.standard_normal((1, K * L, d)).astype(np.float32)
+    a = run_streams(q, k, v, planes, K, L, 1.0, True, dout, chunk=128)
+    b = run_streams(q, k, v, planes, K, L, 1.0, True, dout, chunk=1024)
+    for x, y in zip(a[:4], b[:4]):
+        assert O.rel_l2(x, y) < 1e-5
