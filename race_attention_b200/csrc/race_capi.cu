@@ -190,9 +190,10 @@ int make_plan(const race_desc_t* d, Plan* p) {
   const int sms = sm_count();
   const int64_t T = d->tokens;
   if (!d->causal) {
-    const int64_t target = (int64_t)sms * 4;
+    // one resident wave of 2 CTAs per SM, each walking >= 4 tiles of 64 tokens
+    const int64_t target = (int64_t)sms * 2;
     int64_t P = (target + p->N - 1) / p->N;
-    const int64_t by_len = T / 512;
+    const int64_t by_len = (T + 255) / 256;
     if (P > by_len) P = by_len;
     if (P < 1) P = 1;
     p->P = (int)P;
@@ -300,6 +301,11 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
   }
   Params prm = c.prm;
   void* args[] = {&prm};
+  if (ki.smem_bytes > 48 * 1024) {
+    const cudaError_t ea =
+        cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem_bytes);
+    if (ea != cudaSuccess) return cuda_fail(ea);
+  }
   const cudaError_t e = cudaLaunchKernel(ki.fn, grid, dim3(kThreads), args, ki.smem_bytes, stream);
   if (e != cudaSuccess) return cuda_fail(e);
   return RACE_OK;
@@ -535,7 +541,7 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
     c.prm.dout = dout.data;
     c.prm.alpha = const_cast<float*>(gstate) + (size_t)c.plan.N * c.plan.NC * c.plan.SS;
     RACE_TRY(launch(desc, c, K_C_BWD_KV, stream));
-    RACE_TRY(dscale_final(c, (int)causal_grid(desc, c, 4), dscale, 1, stream));
+    RACE_TRY(dscale_final(c, (int)causal_grid(desc, c, 2), dscale, 1, stream));
   }
   return RACE_OK;
 }

@@ -410,294 +410,9 @@ __device__ __forceinline__ void token_range(int64_t T, int P, int part, int64_t&
   t1 = (T * (part + 1)) / P;
 }
 
-// F1 (non-causal): per-CTA partial bucket sums of p_K v^T and p_K.
-template <typename T, int D, int C, int SPAD>
-__global__ void __launch_bounds__(kThreads) k_nc_reduce(const Params prm) {
-  RACE_KERNEL_PROLOGUE
-  const int n = blockIdx.y, part = blockIdx.x;
-  int64_t t0, t1;
-  token_range(prm.T, prm.P, part, t0, t1);
-  const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
-  const float* pl = prm.planes + (size_t)m * prm.LK * D;
-  const T* kb = static_cast<const T*>(prm.k) + stream_offset(prm.lk, n, prm.B, prm.H) + c * C;
-  const T* vb = static_cast<const T*>(prm.v) + stream_offset(prm.lv, n, prm.B, prm.H) + c * C;
-
-  float acc[SPAD][C];
-#pragma unroll
-  for (int s = 0; s < SPAD; ++s)
-#pragma unroll
-    for (int i = 0; i < C; ++i) acc[s][i] = 0.f;
-  float amass[Gm::KS];
-#pragma unroll
-  for (int i = 0; i < Gm::KS; ++i) amass[i] = 0.f;
-
-  const int64_t iters = (t1 - t0 + Gm::G - 1) / Gm::G;
-  float xk[C] = {}, xv[C] = {}, nk[C] = {}, nv[C] = {};
-  {
-    const int64_t t = t0 + g;
-    if (t < t1) {
-      ld_row<T, C>(kb + t * prm.lk.st, xk);
-      ld_row<T, C>(vb + t * prm.lv.st, xv);
-    }
-  }
-  for (int64_t it = 0; it < iters; ++it) {
-    const int64_t t = t0 + it * Gm::G + g;
-    const bool valid = t < t1;
-    const int64_t tn = t + Gm::G;
-    if (tn < t1) {
-      ld_row<T, C>(kb + tn * prm.lk.st, nk);
-      ld_row<T, C>(vb + tn * prm.lv.st, nv);
-    }
-    float pm[Gm::KS], hk[Gm::KH];
-    soft_hash<D, C, SPAD>(xk, pl, sh, inv_scale, c, scr, valid, pm, hk);
-#pragma unroll
-    for (int i = 0; i < Gm::KS; ++i) amass[i] += pm[i];
-    float p[SPAD];
-    ld_buckets<SPAD>(scr + Gm::P_OFF, p);
-#pragma unroll
-    for (int s = 0; s < SPAD; ++s)
-#pragma unroll
-      for (int i = 0; i < C; ++i) acc[s][i] = fmaf(p[s], xv[i], acc[s][i]);
-#pragma unroll
-    for (int i = 0; i < C; ++i) { xk[i] = nk[i]; xv[i] = nv[i]; }
-  }
-  cta_reduce_slots<D, C, SPAD>(acc, red, c);
-  cta_reduce_mine<D, C, SPAD>(amass, red + SPAD * D, c);
-  float* dst = prm.part + ((size_t)n * prm.P + part) * prm.SS;
-  for (int e = threadIdx.x; e < prm.S * D; e += kThreads) dst[e] = red[e];
-  for (int s = threadIdx.x; s < prm.S; s += kThreads) dst[prm.S * D + s] = red[SPAD * D + s];
-}
-
 // Sums P partial slots per stream in a fixed order: out[n] = sum_p part[n][p].
 __global__ void __launch_bounds__(1024) k_sum_partials(const float* __restrict__ part, int P, int SS,
                                                        float* __restrict__ out);
-
-// F2 (non-causal): out = sum_s pQ_s E_s with E = B / (A + eps) in registers.
-template <typename T, int D, int C, int SPAD>
-__global__ void __launch_bounds__(kThreads) k_nc_readout(const Params prm) {
-  RACE_KERNEL_PROLOGUE
-  const int n = blockIdx.y, part = blockIdx.x;
-  int64_t t0, t1;
-  token_range(prm.T, prm.P, part, t0, t1);
-  const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
-  const float* pl = prm.planes + (size_t)m * prm.LK * D;
-  const float* st = prm.state + (size_t)n * prm.SS;
-  float E[SPAD][C];
-#pragma unroll
-  for (int s = 0; s < SPAD; ++s) {
-    if (s < sh.S) {
-      float b[C];
-      ld_f<C>(st + s * D + c * C, b);
-      const float inv = 1.f / (st[sh.S * D + s] + prm.eps);
-#pragma unroll
-      for (int i = 0; i < C; ++i) E[s][i] = b[i] * inv;
-    } else {
-#pragma unroll
-      for (int i = 0; i < C; ++i) E[s][i] = 0.f;
-    }
-  }
-  const T* qb = static_cast<const T*>(prm.q) + stream_offset(prm.lq, n, prm.B, prm.H) + c * C;
-  T* ob = static_cast<T*>(prm.out) + stream_offset(prm.lo, n, prm.B, prm.H) + c * C;
-  const int64_t iters = (t1 - t0 + Gm::G - 1) / Gm::G;
-  float xq[C] = {}, nq[C] = {};
-  if (t0 + g < t1) ld_row<T, C>(qb + (t0 + g) * prm.lq.st, xq);
-  for (int64_t it = 0; it < iters; ++it) {
-    const int64_t t = t0 + it * Gm::G + g;
-    const bool valid = t < t1;
-    const int64_t tn = t + Gm::G;
-    if (tn < t1) ld_row<T, C>(qb + tn * prm.lq.st, nq);
-    float pm[Gm::KS], hq[Gm::KH];
-    soft_hash<D, C, SPAD>(xq, pl, sh, inv_scale, c, scr, valid, pm, hq);
-    float p[SPAD];
-    ld_buckets<SPAD>(scr + Gm::P_OFF, p);
-    float o[C];
-#pragma unroll
-    for (int i = 0; i < C; ++i) o[i] = 0.f;
-#pragma unroll
-    for (int s = 0; s < SPAD; ++s)
-#pragma unroll
-      for (int i = 0; i < C; ++i) o[i] = fmaf(p[s], E[s][i], o[i]);
-    if (valid) st_row<T, C>(ob + t * prm.lo.st, o);
-#pragma unroll
-    for (int i = 0; i < C; ++i) xq[i] = nq[i];
-  }
-}
-
-// B1 (non-causal): dq, per-CTA partial dE = sum_t pQ dO^T, dscale partial.
-template <typename T, int D, int C, int SPAD>
-__global__ void __launch_bounds__(kThreads) k_nc_bwd_q(const Params prm) {
-  RACE_KERNEL_PROLOGUE
-  const int n = blockIdx.y, part = blockIdx.x;
-  int64_t t0, t1;
-  token_range(prm.T, prm.P, part, t0, t1);
-  const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
-  const float* pl = prm.planes + (size_t)m * prm.LK * D;
-  const float* st = prm.state + (size_t)n * prm.SS;
-  // E table in shared memory (each lane reads its own columns per bucket)
-  for (int e = threadIdx.x; e < SPAD * D; e += kThreads) {
-    const int s = e / D;
-    tab[e] = s < sh.S ? st[e] / (st[sh.S * D + s] + prm.eps) : 0.f;
-  }
-  __syncthreads();
-  const T* qb = static_cast<const T*>(prm.q) + stream_offset(prm.lq, n, prm.B, prm.H) + c * C;
-  const T* gb = static_cast<const T*>(prm.dout) + stream_offset(prm.ldo, n, prm.B, prm.H) + c * C;
-  T* dqb = static_cast<T*>(prm.dq) + stream_offset(prm.ldq, n, prm.B, prm.H) + c * C;
-  float acc[SPAD][C];
-#pragma unroll
-  for (int s = 0; s < SPAD; ++s)
-#pragma unroll
-    for (int i = 0; i < C; ++i) acc[s][i] = 0.f;
-  float ds = 0.f;
-  const int64_t iters = (t1 - t0 + Gm::G - 1) / Gm::G;
-  float xq[C] = {}, xg[C] = {}, nq[C] = {}, ng[C] = {};
-  if (t0 + g < t1) {
-    ld_row<T, C>(qb + (t0 + g) * prm.lq.st, xq);
-    ld_row<T, C>(gb + (t0 + g) * prm.ldo.st, xg);
-  }
-  for (int64_t it = 0; it < iters; ++it) {
-    const int64_t t = t0 + it * Gm::G + g;
-    const bool valid = t < t1;
-    const int64_t tn = t + Gm::G;
-    if (tn < t1) {
-      ld_row<T, C>(qb + tn * prm.lq.st, nq);
-      ld_row<T, C>(gb + tn * prm.ldo.st, ng);
-    }
-    if (!valid) {
-#pragma unroll
-      for (int i = 0; i < C; ++i) xg[i] = 0.f;
-    }
-    float pm[Gm::KS], hq[Gm::KH];
-    soft_hash<D, C, SPAD>(xq, pl, sh, inv_scale, c, scr, valid, pm, hq);
-    float p[SPAD];
-    ld_buckets<SPAD>(scr + Gm::P_OFF, p);
-    float dpv[Gm::SPV];
-#pragma unroll
-    for (int s = 0; s < Gm::SPV; ++s) dpv[s] = 0.f;
-#pragma unroll
-    for (int s = 0; s < SPAD; ++s) {
-      float e[C];
-      ld_f<C>(tab + s * D + c * C, e);
-      float d = 0.f;
-#pragma unroll
-      for (int i = 0; i < C; ++i) {
-        acc[s][i] = fmaf(p[s], xg[i], acc[s][i]);
-        d = fmaf(xg[i], e[i], d);
-      }
-      dpv[s] = d;
-    }
-    group_reduce<Gm::SPV, Gm::W>(dpv, c);
-#pragma unroll
-    for (int i = 0; i < Gm::KS; ++i) scr[Gm::DP_OFF + c * Gm::KS + i] = dpv[i];
-    __syncwarp();
-    float dx[C];
-    soft_hash_backward<D, C, SPAD>(pl, sh, inv_scale, c, scr, valid, hq, ds, dx);
-    if (valid) st_row<T, C>(dqb + t * prm.ldq.st, dx);
-#pragma unroll
-    for (int i = 0; i < C; ++i) { xq[i] = nq[i]; xg[i] = ng[i]; }
-  }
-  cta_reduce_slots<D, C, SPAD>(acc, red, c);
-  float* dst = prm.part + ((size_t)n * prm.P + part) * prm.SS;
-  for (int e = threadIdx.x; e < prm.S * D; e += kThreads) dst[e] = red[e];
-  const float tot = cta_sum(ds, red32);
-  if (threadIdx.x == 0) prm.dscale_part[(size_t)n * prm.P + part] = tot;
-}
-
-// B2 (non-causal): dk, dv from dB = dE / (A + eps), dA = -<dB, E>.
-template <typename T, int D, int C, int SPAD>
-__global__ void __launch_bounds__(kThreads) k_nc_bwd_kv(const Params prm) {
-  RACE_KERNEL_PROLOGUE
-  const int n = blockIdx.y, part = blockIdx.x;
-  int64_t t0, t1;
-  token_range(prm.T, prm.P, part, t0, t1);
-  const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
-  const float* pl = prm.planes + (size_t)m * prm.LK * D;
-  const float* st = prm.state + (size_t)n * prm.SS;
-  const float* gs = prm.gstate_in + (size_t)n * prm.SS;
-  // dA_s = -sum_d dE_sd B_sd / (A_s + eps)^2, one warp per bucket
-  float* dA = red;  // SPV floats
-  for (int s = threadIdx.x >> 5; s < Gm::SPV; s += kWarps) {
-    float a = 0.f;
-    if (s < sh.S) {
-      for (int d = lane; d < D; d += 32) a = fmaf(gs[s * D + d], st[s * D + d], a);
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      const float inv = 1.f / (st[sh.S * D + s] + prm.eps);
-      a = -a * inv * inv;
-    }
-    if (lane == 0) dA[s] = a;
-  }
-  __syncthreads();
-  float dB[SPAD][C];
-#pragma unroll
-  for (int s = 0; s < SPAD; ++s) {
-    if (s < sh.S) {
-      float b[C];
-      ld_f<C>(gs + s * D + c * C, b);
-      const float inv = 1.f / (st[sh.S * D + s] + prm.eps);
-#pragma unroll
-      for (int i = 0; i < C; ++i) dB[s][i] = b[i] * inv;
-    } else {
-#pragma unroll
-      for (int i = 0; i < C; ++i) dB[s][i] = 0.f;
-    }
-  }
-  float dAm[Gm::KS];
-#pragma unroll
-  for (int i = 0; i < Gm::KS; ++i) dAm[i] = dA[c * Gm::KS + i];
-
-  const T* kb = static_cast<const T*>(prm.k) + stream_offset(prm.lk, n, prm.B, prm.H) + c * C;
-  const T* vb = static_cast<const T*>(prm.v) + stream_offset(prm.lv, n, prm.B, prm.H) + c * C;
-  T* dkb = static_cast<T*>(prm.dk) + stream_offset(prm.ldk, n, prm.B, prm.H) + c * C;
-  T* dvb = static_cast<T*>(prm.dv) + stream_offset(prm.ldv, n, prm.B, prm.H) + c * C;
-  float ds = 0.f;
-  const int64_t iters = (t1 - t0 + Gm::G - 1) / Gm::G;
-  float xk[C] = {}, xv[C] = {}, nk[C] = {}, nv[C] = {};
-  if (t0 + g < t1) {
-    ld_row<T, C>(kb + (t0 + g) * prm.lk.st, xk);
-    ld_row<T, C>(vb + (t0 + g) * prm.lv.st, xv);
-  }
-  for (int64_t it = 0; it < iters; ++it) {
-    const int64_t t = t0 + it * Gm::G + g;
-    const bool valid = t < t1;
-    const int64_t tn = t + Gm::G;
-    if (tn < t1) {
-      ld_row<T, C>(kb + tn * prm.lk.st, nk);
-      ld_row<T, C>(vb + tn * prm.lv.st, nv);
-    }
-    float pm[Gm::KS], hk[Gm::KH];
-    soft_hash<D, C, SPAD>(xk, pl, sh, inv_scale, c, scr, valid, pm, hk);
-    float p[SPAD];
-    ld_buckets<SPAD>(scr + Gm::P_OFF, p);
-    float dvv[C];
-#pragma unroll
-    for (int i = 0; i < C; ++i) dvv[i] = 0.f;
-    float dpv[Gm::SPV];
-#pragma unroll
-    for (int s = 0; s < Gm::SPV; ++s) dpv[s] = 0.f;
-#pragma unroll
-    for (int s = 0; s < SPAD; ++s) {
-      float d = 0.f;
-#pragma unroll
-      for (int i = 0; i < C; ++i) {
-        dvv[i] = fmaf(p[s], dB[s][i], dvv[i]);
-        d = fmaf(xv[i], dB[s][i], d);
-      }
-      dpv[s] = d;
-    }
-    if (valid) st_row<T, C>(dvb + t * prm.ldv.st, dvv);
-    group_reduce<Gm::SPV, Gm::W>(dpv, c);
-#pragma unroll
-    for (int i = 0; i < Gm::KS; ++i) scr[Gm::DP_OFF + c * Gm::KS + i] = dpv[i] + dAm[i];
-    __syncwarp();
-    float dx[C];
-    soft_hash_backward<D, C, SPAD>(pl, sh, inv_scale, c, scr, valid, hk, ds, dx);
-    if (valid) st_row<T, C>(dkb + t * prm.ldk.st, dx);
-#pragma unroll
-    for (int i = 0; i < C; ++i) { xk[i] = nk[i]; xv[i] = nv[i]; }
-  }
-  const float tot = cta_sum(ds, red32);
-  if (threadIdx.x == 0) prm.dscale_part[(size_t)n * prm.P + part] = tot;
-}
 
 // ---------------------------------------------------------------- causal
 // Work unit = one chunk of CL consecutive tokens of one stream, walked in
@@ -986,6 +701,11 @@ __global__ void __launch_bounds__(kThreads) k_c_bwd_q(const Params prm) {
   if (threadIdx.x == 0) prm.dscale_part[blockIdx.x] = tot;
 }
 
+// CB2 is instantiated with the same column split as CB1 (C = 2) so both walks
+// hash every key to bit-identical probabilities: the key mass A_s(t) is
+// rebuilt here by subtracting them from CB1's chunk total, and for the first
+// tokens of a sequence A_s(t) can be ~1e-5, where two differently rounded
+// hashes would disagree by 1e-3 relative.
 // CB2: reverse walk of the chunk from its exclusive gradient suffix:
 //   beta_s += W_s dO, alpha_suf_s += alpha_s, dv = sum_s pK_s beta_s,
 //   dpK_s = alpha_suf_s + <beta_s, v>  -> dk.
