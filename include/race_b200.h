@@ -58,7 +58,8 @@ typedef enum {
   RACE_ERR_UNSUPPORTED = 2,  /* shape outside what the kernels are built for    */
   RACE_ERR_ALIGN = 3,        /* pointer or stride breaks the vector alignment   */
   RACE_ERR_WORKSPACE = 4,    /* workspace smaller than race_query() asked for   */
-  RACE_ERR_CUDA = 5          /* a CUDA launch failed (see race_last_cuda_error) */
+  RACE_ERR_CUDA = 5,         /* a CUDA launch failed (see race_last_cuda_error) */
+  RACE_ERR_TOO_LARGE = 6     /* shape needs more than the static scratch holds  */
 } race_status_t;
 
 typedef enum { RACE_F32 = 0, RACE_BF16 = 1 } race_dtype_t;
@@ -167,6 +168,27 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q,
  * which the offset does not touch. */
 int race_add_offset(const race_desc_t* desc, float* slots, const float* offset,
                     int is_gradient, cudaStream_t stream);
+
+/* Forward without any device allocation: for callers that cannot call
+ * cudaMalloc or own a caching allocator -- e.g. code running inside another
+ * runtime's memory pool, a plugin host that forbids allocation after start-up,
+ * or an inference loop with a fixed memory budget.  No counterpart exists in
+ * the reference.  The caller passes only inputs and `out`; the bucket state and
+ * all scratch live in one library-owned static device array of
+ * RACE_STATIC_SCRATCH_BYTES (8 MiB), which every GPU that loads the library
+ * keeps until process exit.  Shapes whose state + scratch exceed it return
+ * RACE_ERR_TOO_LARGE (see race_query: state_bytes + workspace_bytes).
+ * The first call on a device looks up that array's device address (once per
+ * device, on the current device), so make the first call before any stream
+ * capture.  All calls share the array: two calls that overlap on the GPU
+ * (different streams, or different host threads) race and corrupt each other;
+ * serialize them.  Every value a call reads from the array is written earlier
+ * in the same call, so nothing is cleared between calls.  No saved state is
+ * returned, so there is no matching backward: use race_forward for training. */
+#define RACE_STATIC_SCRATCH_BYTES (8u << 20)
+int race_forward_static(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
+                        race_tensor_t v, const float* planes, const float* scale,
+                        race_tensor_t out, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -13,13 +13,14 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "librace_b200.so")
 
 RACE_OK = 0
+RACE_ERR_TOO_LARGE = 6
 RACE_F32 = 0
 RACE_BF16 = 1
 
 SYMBOLS = (
     "race_version", "race_strerror", "race_last_cuda_error", "race_query",
     "race_forward", "race_backward", "race_forward_reduce", "race_forward_readout",
-    "race_backward_q", "race_backward_kv", "race_add_offset",
+    "race_backward_q", "race_backward_kv", "race_add_offset", "race_forward_static",
 )
 
 
@@ -72,6 +73,7 @@ _SIGS = {
     "race_backward_kv": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _P, _P, _T, _T, _T, _P, _P,
                           ctypes.c_size_t, _P], ctypes.c_int),
     "race_add_offset": ([ctypes.POINTER(RaceDesc), _P, _P, ctypes.c_int, _P], ctypes.c_int),
+    "race_forward_static": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _T, _P], ctypes.c_int),
 }
 
 

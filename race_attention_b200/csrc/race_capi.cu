@@ -369,6 +369,8 @@ const char* race_strerror(int status) {
     case RACE_ERR_ALIGN: return "pointer or stride not 16-byte aligned for vector access";
     case RACE_ERR_WORKSPACE: return "workspace missing or smaller than race_query() reported";
     case RACE_ERR_CUDA: return "CUDA error (see race_last_cuda_error)";
+    case RACE_ERR_TOO_LARGE:
+      return "state + scratch exceed RACE_STATIC_SCRATCH_BYTES (use race_forward with caller buffers)";
     default: return "unknown status";
   }
 }
@@ -570,3 +572,49 @@ int race_add_offset(const race_desc_t* desc, float* slots, const float* offset, 
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ allocation-free forward
+// Library-owned scratch for race_forward_static: the bucket state followed by
+// the workspace.  In host code `g_static_scratch` is only a symbol handle; its
+// device address is fetched per device with cudaGetSymbolAddress.
+namespace race {
+namespace {
+constexpr size_t kStaticFloats = RACE_STATIC_SCRATCH_BYTES / sizeof(float);
+static __device__ __align__(256) float g_static_scratch[kStaticFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+float* g_static_ptr[kMaxDevices] = {};
+
+int static_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return RACE_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (g_static_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_static_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_static_ptr[dev];
+  return RACE_OK;
+}
+}  // namespace
+}  // namespace race
+
+extern "C" int race_forward_static(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
+                                   race_tensor_t v, const float* planes, const float* scale,
+                                   race_tensor_t out, cudaStream_t stream) {
+  race_sizes_t sz;
+  RACE_TRY(race_query(desc, &sz));
+  const size_t state_bytes = (sz.state_bytes + 255) / 256 * 256;
+  if (state_bytes + sz.workspace_bytes > RACE_STATIC_SCRATCH_BYTES) return RACE_ERR_TOO_LARGE;
+  float* base = nullptr;
+  RACE_TRY(static_scratch(&base));
+  float* state = base;
+  void* ws = reinterpret_cast<char*>(base) + state_bytes;
+  return race_forward(desc, q, k, v, planes, scale, out, state, ws,
+                      RACE_STATIC_SCRATCH_BYTES - state_bytes, stream);
+}

@@ -35,7 +35,7 @@ def test_exports_every_declared_symbol(lib):
 
 def test_version_and_errors(lib):
     assert b"sm_100a" in lib.race_version()
-    for rc in range(6):
+    for rc in range(7):
         assert lib.race_strerror(rc)
 
 
