@@ -18,7 +18,6 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "librace_b200.so")
 SOURCES = ["race_capi.cu", "race_f32.cu", "race_bf16.cu"]
-DEPS = SOURCES + ["race_kernels.cuh", "race_launch.h", "race_instances.inc"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
@@ -36,7 +35,8 @@ def _stale() -> bool:
         return True
     t = os.path.getmtime(OUT)
     hdr = os.path.join(ROOT, "include", "race_b200.h")
-    return any(os.path.getmtime(p) > t for p in [os.path.join(CSRC, f) for f in DEPS] + [hdr])
+    deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)] + [hdr, os.path.abspath(__file__)]
+    return any(os.path.getmtime(p) > t for p in deps)
 
 
 def build(force: bool = False, verbose: bool = False) -> str:

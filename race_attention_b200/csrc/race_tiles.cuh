@@ -38,7 +38,12 @@ template <int D, int SPAD, bool BF = false>
 struct Lay {
   static constexpr int NSTAGE = BF ? 1 : 2;   // fp32 tile stages (bf16 stages raw rows)
   static constexpr int RS = D + 4;       // fp32 row stride of X / Y / PL / TAB
-  static constexpr int PS = SPAD + 4;    // row stride of P / DP  [t][s]
+  // row stride of P / DP [t][s]; 16 makes the float4 reads of one table by a
+  // quarter-warp (2 tokens x 4 tables) conflict-free; SPAD + 4 for wider rows
+  // (at most 2-way conflicts) keeps two CTAs' shared memory within the SM
+  static constexpr int PS = SPAD <= 16 ? 16 : SPAD + 4;
+  // largest power of two <= SPAD: bound on buckets per table
+  static constexpr int RM = SPAD >= 32 ? 32 : SPAD >= 16 ? 16 : 8;
   static constexpr int TS = TT + 4;      // row stride of PT / DJT [k][t]
   static constexpr int SQ = SPAD / 4;    // buckets per rowdot thread
   static constexpr int XS = 0;                       // [NSTAGE][TT][RS]
@@ -173,16 +178,19 @@ __device__ __forceinline__ void hash_tile(const float* __restrict__ X, float* sm
   float* Hrow = sm + LY::H + t * (LKP + 1);
   float* Prow = sm + LY::P + t * LY::PS;
   float* PT = sm + LY::PT;
+  // park the projections in the token's H row (quarter q writes j = q mod 4),
+  // so the table owners can pick theirs without indexing a register array
+#pragma unroll
+  for (int j = 0; j < LKP; ++j)
+    if ((j & 3) == q && j < sh.LK) Hrow[j] = acc[j];
+  __syncwarp();
   for (int l = q; l < sh.L; l += 4) {
     float sp[5], sn[5];   // sigmoid(+2u), sigmoid(-2u) per plane of the table (K <= 5)
 #pragma unroll
     for (int k = 0; k < 5; ++k) {
       sp[k] = sn[k] = 1.f;
       if (k < sh.K) {
-        float a = 0.f;
-#pragma unroll
-        for (int j = 0; j < LKP; ++j)
-          if (j == l * sh.K + k) a = acc[j];
+        const float a = Hrow[l * sh.K + k];
         const float h = tanh_exp(a);
         Hrow[l * sh.K + k] = h;
         const float u = h * inv_scale;
@@ -205,10 +213,13 @@ __device__ __forceinline__ void hash_tile(const float* __restrict__ X, float* sm
 }
 
 // Softmax / corner / tanh backward in the hash layout: reads P, DP (+dA when
-// given), H; writes DJT[j][t] = dL/dproj_j and accumulates sum_j du_j h_j.
-template <class LY>
+// HAS_DA), H; writes DJT[j][t] = dL/dproj_j and accumulates sum_j du_j h_j.
+// A thread loads its table's R probabilities and gradients once (vector
+// loads), forms g_r = p_r (dp_r - sum p dp) and the K plane sums from them.
+template <class LY, bool HAS_DA>
 __device__ __forceinline__ void hash_backward(float* sm, const Shape& sh, float inv_scale,
                                               const float* dA, float& ds) {
+  constexpr int RM = LY::RM;
   const int lane = threadIdx.x & 31;
   const int t = (threadIdx.x >> 5) * 8 + (lane >> 2);
   const int q = lane & 3;
@@ -218,23 +229,61 @@ __device__ __forceinline__ void hash_backward(float* sm, const Shape& sh, float 
   float* DJT = sm + LY::DJT;
   for (int l = q; l < sh.L; l += 4) {
     const int s0 = l * sh.R;
+    float g[RM];
     float pbar = 0.f;
-    for (int r = 0; r < sh.R; ++r) {
-      const float d = Drow[s0 + r] + (dA ? dA[s0 + r] : 0.f);
-      pbar = fmaf(Prow[s0 + r], d, pbar);
-    }
-    for (int k = 0; k < sh.K; ++k) {
-      const int bit = sh.K - 1 - k;
-      float du = 0.f;
-      for (int r = 0; r < sh.R; ++r) {
-        const float d = Drow[s0 + r] + (dA ? dA[s0 + r] : 0.f);
-        const float g = Prow[s0 + r] * (d - pbar);
-        du += ((r >> bit) & 1) ? g : -g;
+    if (sh.R >= 4) {
+#pragma unroll
+      for (int c = 0; c < RM / 4; ++c) {
+        if (4 * c < sh.R) {
+          const float4 pp = *reinterpret_cast<const float4*>(Prow + s0 + 4 * c);
+          float4 dd = *reinterpret_cast<const float4*>(Drow + s0 + 4 * c);
+          if (HAS_DA) {
+            const float4 aa = *reinterpret_cast<const float4*>(dA + s0 + 4 * c);
+            dd.x += aa.x; dd.y += aa.y; dd.z += aa.z; dd.w += aa.w;
+          }
+          g[4 * c] = pp.x; g[4 * c + 1] = pp.y; g[4 * c + 2] = pp.z; g[4 * c + 3] = pp.w;
+          pbar = fmaf(pp.x, dd.x, fmaf(pp.y, dd.y, fmaf(pp.z, dd.z, fmaf(pp.w, dd.w, pbar))));
+        }
       }
-      const int j = l * sh.K + k;
-      const float h = Hrow[j];
-      ds = fmaf(du, h, ds);
-      DJT[j * LY::TS + t] = du * inv_scale * (1.f - h * h);
+      // second pass: g_r = p_r (dp_r - pbar) (re-read dp; p is in registers)
+#pragma unroll
+      for (int c = 0; c < RM / 4; ++c) {
+        if (4 * c < sh.R) {
+          float4 dd = *reinterpret_cast<const float4*>(Drow + s0 + 4 * c);
+          if (HAS_DA) {
+            const float4 aa = *reinterpret_cast<const float4*>(dA + s0 + 4 * c);
+            dd.x += aa.x; dd.y += aa.y; dd.z += aa.z; dd.w += aa.w;
+          }
+          g[4 * c] *= dd.x - pbar;
+          g[4 * c + 1] *= dd.y - pbar;
+          g[4 * c + 2] *= dd.z - pbar;
+          g[4 * c + 3] *= dd.w - pbar;
+        }
+      }
+    } else {   // R == 2
+      const float2 pp = *reinterpret_cast<const float2*>(Prow + s0);
+      float2 dd = *reinterpret_cast<const float2*>(Drow + s0);
+      if (HAS_DA) {
+        const float2 aa = *reinterpret_cast<const float2*>(dA + s0);
+        dd.x += aa.x; dd.y += aa.y;
+      }
+      pbar = fmaf(pp.x, dd.x, pp.y * dd.y);
+      g[0] = pp.x * (dd.x - pbar);
+      g[1] = pp.y * (dd.y - pbar);
+    }
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      if (k < sh.K) {
+        const int bit = sh.K - 1 - k;
+        float du = 0.f;
+#pragma unroll
+        for (int r = 0; r < RM; ++r)
+          if (r < sh.R) du += ((r >> bit) & 1) ? g[r] : -g[r];
+        const int j = l * sh.K + k;
+        const float h = Hrow[j];
+        ds = fmaf(du, h, ds);
+        DJT[j * LY::TS + t] = du * inv_scale * (1.f - h * h);
+      }
     }
   }
 }
@@ -293,7 +342,7 @@ __device__ __forceinline__ void store_readout(T* base, int64_t st, int64_t tile0
   }
 }
 
-// DP[t][s] = sum_d X[t][d] TAB[s][d] for t in {16w + 2p, +1}, s = sq + 4j.
+// DP[t][s] = sum_d X[t][d] TAB[s][d] for t in {16w + p, 16w + p + 8}, s = sq + 4j.
 // Uses 4 warps (warp0 .. warp0+3), 16 tokens each.
 template <class LY>
 __device__ __forceinline__ void rowdot(const float* __restrict__ X, const float* __restrict__ TAB,
@@ -303,7 +352,7 @@ __device__ __forceinline__ void rowdot(const float* __restrict__ X, const float*
   const int lane = threadIdx.x & 31;
   const int w = (threadIdx.x >> 5) - warp0;
   const int p = lane >> 2, sq = lane & 3;
-  const int t = w * 16 + 2 * p;
+  const int t = w * 16 + p;
   float acc[2][SQ];
 #pragma unroll
   for (int i = 0; i < 2; ++i)
@@ -312,7 +361,7 @@ __device__ __forceinline__ void rowdot(const float* __restrict__ X, const float*
 #pragma unroll 4
   for (int d = 0; d < D; d += 4) {
     const float4 x0 = *reinterpret_cast<const float4*>(X + t * LY::RS + d);
-    const float4 x1 = *reinterpret_cast<const float4*>(X + (t + 1) * LY::RS + d);
+    const float4 x1 = *reinterpret_cast<const float4*>(X + (t + 8) * LY::RS + d);
 #pragma unroll
     for (int j = 0; j < SQ; ++j) {
       const float4 e = *reinterpret_cast<const float4*>(TAB + (sq + 4 * j) * LY::RS + d);
@@ -323,7 +372,7 @@ __device__ __forceinline__ void rowdot(const float* __restrict__ X, const float*
 #pragma unroll
   for (int j = 0; j < SQ; ++j) {
     DP[t * LY::PS + sq + 4 * j] = acc[0][j];
-    DP[(t + 1) * LY::PS + sq + 4 * j] = acc[1][j];
+    DP[(t + 8) * LY::PS + sq + 4 * j] = acc[1][j];
   }
 }
 
@@ -420,24 +469,34 @@ __device__ __forceinline__ TileRange tile_range(int64_t T, int P, int part) {
   return r;
 }
 
-// Pipelined walk over the tiles: stage tile i+1 while computing tile i.
-// body(X, Y, tile0) computes one tile from the fp32 shared-memory tiles.
-template <typename T, class LY, bool TWO, typename Body>
-__device__ __forceinline__ void walk_tiles(float* sm, const T* xb, int64_t xst, const T* yb,
-                                           int64_t yst, const TileRange& tr, Body&& body) {
-  constexpr int D = LY::Dv;
-  constexpr bool BF = sizeof(T) == 2;
-  auto fx = [&](int st) { return sm + LY::XS + (BF ? 0 : st * TT * LY::RS); };
-  auto fy = [&](int st) { return sm + LY::YS + (BF ? 0 : st * TT * LY::RS); };
-  auto rx = [&](int st) { return (void*)(sm + LY::RAW + (st * 2 + 0) * (TT * D / 2)); };
-  auto ry = [&](int st) { return (void*)(sm + LY::RAW + (st * 2 + 1) * (TT * D / 2)); };
-  if (tr.ntiles <= 0) return;
-  stage_tile<T, D>(fx(0), rx(0), xb, xst, tr.t0, tr.t1);
-  if (TWO) stage_tile<T, D>(fy(0), ry(0), yb, yst, tr.t0, tr.t1);
-  cp_commit();
-  for (int i = 0; i < tr.ntiles; ++i) {
+// Pipelined walk over the tiles: tile i+1 is staged while tile i is
+// computed.  Usage:
+//   TilePipe<T, LY, TWO> pipe{...};  pipe.start();
+//   for (i < ntiles) { pipe.acquire(i, X, Y, tile0); ...compute...; __syncthreads(); }
+//   pipe.finish();
+template <typename T, class LY, bool TWO>
+struct TilePipe {
+  static constexpr int D = LY::Dv;
+  static constexpr bool BF = sizeof(T) == 2;
+  float* sm;
+  const T* xb;
+  int64_t xst;
+  const T* yb;
+  int64_t yst;
+  TileRange tr;
+  __device__ __forceinline__ float* fx(int st) const { return sm + LY::XS + (BF ? 0 : st * TT * LY::RS); }
+  __device__ __forceinline__ float* fy(int st) const { return sm + LY::YS + (BF ? 0 : st * TT * LY::RS); }
+  __device__ __forceinline__ void* rx(int st) const { return sm + LY::RAW + (st * 2 + 0) * (TT * D / 2); }
+  __device__ __forceinline__ void* ry(int st) const { return sm + LY::RAW + (st * 2 + 1) * (TT * D / 2); }
+  __device__ __forceinline__ void start() const {
+    if (tr.ntiles <= 0) return;
+    stage_tile<T, D>(fx(0), rx(0), xb, xst, tr.t0, tr.t1);
+    if (TWO) stage_tile<T, D>(fy(0), ry(0), yb, yst, tr.t0, tr.t1);
+    cp_commit();
+  }
+  __device__ __forceinline__ void acquire(int i, float*& X, float*& Y, int64_t& tile0) const {
     const int st = i & 1;
-    const int64_t tile0 = tr.t0 + (int64_t)i * TT;
+    tile0 = tr.t0 + (int64_t)i * TT;
     if (i + 1 < tr.ntiles) {
       stage_tile<T, D>(fx(st ^ 1), rx(st ^ 1), xb, xst, tile0 + TT, tr.t1);
       if (TWO) stage_tile<T, D>(fy(st ^ 1), ry(st ^ 1), yb, yst, tile0 + TT, tr.t1);
@@ -450,11 +509,11 @@ __device__ __forceinline__ void walk_tiles(float* sm, const T* xb, int64_t xst, 
       if (TWO) convert_tile<D>(fy(0), ry(st));
       __syncthreads();
     }
-    body(fx(st), fy(st), tile0);
-    __syncthreads();
+    X = fx(st);
+    Y = fy(st);
   }
-  cp_wait<0>();
-}
+  __device__ __forceinline__ void finish() const { cp_wait<0>(); }
+};
 
 #define RACE_TILE_PROLOGUE                                                        \
   using LY = Lay<D, SPAD, sizeof(T) == 2>;                                        \
@@ -481,8 +540,12 @@ __global__ void __launch_bounds__(NT, 2) k_tile_reduce(const Params prm) {
   agg.zero();
   float amass = 0.f;   // thread (s = tid/8, part = tid%8): bucket mass partial
   const int w = threadIdx.x >> 5;
-  walk_tiles<T, LY, true>(sm, kb, prm.lk.st, vb, prm.lv.st, tr,
-                          [&](float* X, float* Y, int64_t tile0) {
+  TilePipe<T, LY, true> pipe{sm, kb, prm.lk.st, vb, prm.lv.st, tr};
+  pipe.start();
+  for (int it = 0; it < tr.ntiles; ++it) {
+    float *X, *Y;
+    int64_t tile0;
+    pipe.acquire(it, X, Y, tile0);
     hash_tile<LY>(X, sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
     agg.add_tile(sm + LY::P, Y, w * 8, w * 8 + 8);
@@ -493,7 +556,9 @@ __global__ void __launch_bounds__(NT, 2) k_tile_reduce(const Params prm) {
       const float4 b = *reinterpret_cast<const float4*>(row + 4);
       amass += ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
     }
-  });
+    __syncthreads();
+  }
+  pipe.finish();
   amass += __shfl_xor_sync(0xffffffffu, amass, 1);
   amass += __shfl_xor_sync(0xffffffffu, amass, 2);
   amass += __shfl_xor_sync(0xffffffffu, amass, 4);
@@ -516,15 +581,21 @@ __global__ void __launch_bounds__(NT, 2) k_tile_readout(const Params prm) {
   const T* qb = static_cast<const T*>(prm.q) + stream_offset(prm.lq, n, prm.B, prm.H);
   T* ob = static_cast<T*>(prm.out) + stream_offset(prm.lo, n, prm.B, prm.H);
   __syncthreads();
-  walk_tiles<T, LY, false>(sm, qb, prm.lq.st, qb, prm.lq.st, tr,
-                           [&](float* X, float*, int64_t tile0) {
+  TilePipe<T, LY, false> pipe{sm, qb, prm.lq.st, qb, prm.lq.st, tr};
+  pipe.start();
+  for (int it = 0; it < tr.ntiles; ++it) {
+    float *X, *Y;
+    int64_t tile0;
+    pipe.acquire(it, X, Y, tile0);
     hash_tile<LY>(X, sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
     float o[2][8];
     int t, c;
     readout<LY>(sm + LY::PT, sm + LY::TAB, sh.S, 0, o, t, c);
     store_readout<T, D>(ob, prm.lo.st, tile0, tr.t1, t, c, o);
-  });
+    __syncthreads();
+  }
+  pipe.finish();
 }
 
 // B1: dq and the per-CTA partial dE = sum_t pQ dO^T (warps 4-7), dp = dO E^T
@@ -542,20 +613,26 @@ __global__ void __launch_bounds__(NT, 2) k_tile_bwd_q(const Params prm) {
   agg.zero();
   float ds = 0.f;
   const int w = threadIdx.x >> 5;
-  walk_tiles<T, LY, true>(sm, qb, prm.lq.st, gb, prm.ldo.st, tr,
-                          [&](float* X, float* Y, int64_t tile0) {
+  TilePipe<T, LY, true> pipe{sm, qb, prm.lq.st, gb, prm.ldo.st, tr};
+  pipe.start();
+  for (int it = 0; it < tr.ntiles; ++it) {
+    float *X, *Y;
+    int64_t tile0;
+    pipe.acquire(it, X, Y, tile0);
     hash_tile<LY>(X, sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
     if (w < 4) rowdot<LY>(Y, sm + LY::TAB, sm + LY::DP, 0);
     else agg.add_tile(sm + LY::P, Y, (w - 4) * 16, (w - 4) * 16 + 16);
     __syncthreads();
-    hash_backward<LY>(sm, sh, inv_scale, nullptr, ds);
+    hash_backward<LY, false>(sm, sh, inv_scale, nullptr, ds);
     __syncthreads();
     float o[2][8];
     int t, c;
     readout<LY>(sm + LY::DJT, sm + LY::PL, sh.LK, 0, o, t, c);
     store_readout<T, D>(dqb, prm.ldq.st, tile0, tr.t1, t, c, o);
-  });
+    __syncthreads();
+  }
+  pipe.finish();
   float* red = sm + LY::XS;
   __syncthreads();
   agg.reduce(red, 4, 4);
@@ -596,8 +673,12 @@ __global__ void __launch_bounds__(NT, 2) k_tile_bwd_kv(const Params prm) {
   __syncthreads();
   float ds = 0.f;
   const int w = threadIdx.x >> 5;
-  walk_tiles<T, LY, true>(sm, kb, prm.lk.st, vb, prm.lv.st, tr,
-                          [&](float* X, float* Y, int64_t tile0) {
+  TilePipe<T, LY, true> pipe{sm, kb, prm.lk.st, vb, prm.lv.st, tr};
+  pipe.start();
+  for (int it = 0; it < tr.ntiles; ++it) {
+    float *X, *Y;
+    int64_t tile0;
+    pipe.acquire(it, X, Y, tile0);
     hash_tile<LY>(X, sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
     if (w < 4) {
@@ -612,13 +693,15 @@ __global__ void __launch_bounds__(NT, 2) k_tile_bwd_kv(const Params prm) {
       }
     }
     __syncthreads();
-    hash_backward<LY>(sm, sh, inv_scale, dA, ds);
+    hash_backward<LY, true>(sm, sh, inv_scale, dA, ds);
     __syncthreads();
     float o[2][8];
     int t, c;
     readout<LY>(sm + LY::DJT, sm + LY::PL, sh.LK, 0, o, t, c);
     store_readout<T, D>(dkb, prm.ldk.st, tile0, tr.t1, t, c, o);
-  });
+    __syncthreads();
+  }
+  pipe.finish();
   const float tot = cta_sum(ds, sm + LY::MISC + 32);
   if (threadIdx.x == 0) prm.dscale_part[(size_t)n * prm.P + part] = tot;
 }
