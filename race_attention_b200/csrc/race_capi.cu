@@ -289,8 +289,12 @@ int check_tensor(const race_desc_t* d, const race_tensor_t& t) {
 
 int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream) {
   KernelInfo ki;
-  const bool ok = d->dtype == RACE_F32 ? kernels_f32(d->head_dim, c.plan.spad, id, &ki)
-                                       : kernels_bf16(d->head_dim, c.plan.spad, id, &ki);
+  const int K = d->num_bits, sp = c.plan.spad;
+  bool ok;
+  if (d->dtype == RACE_F32)
+    ok = d->head_dim == 32 ? kernels_f32_d32(sp, K, id, &ki) : kernels_f32_d64(sp, K, id, &ki);
+  else
+    ok = d->head_dim == 32 ? kernels_bf16_d32(sp, K, id, &ki) : kernels_bf16_d64(sp, K, id, &ki);
   if (!ok) return RACE_ERR_UNSUPPORTED;
   dim3 grid;
   if (id == K_NC_REDUCE || id == K_NC_READOUT || id == K_NC_BWD_Q || id == K_NC_BWD_KV) {

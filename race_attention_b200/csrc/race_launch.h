@@ -31,7 +31,11 @@ inline int spad_for(int S) {
   return -1;
 }
 
-bool kernels_f32(int D, int spad, KernelId id, KernelInfo* info);
-bool kernels_bf16(int D, int spad, KernelId id, KernelInfo* info);
+// One table per (element type, head dim); K selects the non-causal tile
+// kernels' compile-time hyperplane count (the causal kernels take it at run time).
+bool kernels_f32_d32(int spad, int K, KernelId id, KernelInfo* info);
+bool kernels_f32_d64(int spad, int K, KernelId id, KernelInfo* info);
+bool kernels_bf16_d32(int spad, int K, KernelId id, KernelInfo* info);
+bool kernels_bf16_d64(int spad, int K, KernelId id, KernelInfo* info);
 
 }  // namespace race

@@ -42,8 +42,6 @@ struct Lay {
   // quarter-warp (2 tokens x 4 tables) conflict-free; SPAD + 4 for wider rows
   // (at most 2-way conflicts) keeps two CTAs' shared memory within the SM
   static constexpr int PS = SPAD <= 16 ? 16 : SPAD + 4;
-  // largest power of two <= SPAD: bound on buckets per table
-  static constexpr int RM = SPAD >= 32 ? 32 : SPAD >= 16 ? 16 : 8;
   static constexpr int TS = TT + 4;      // row stride of PT / DJT [k][t]
   static constexpr int SQ = SPAD / 4;    // buckets per rowdot thread
   static constexpr int XS = 0;                       // [NSTAGE][TT][RS]
@@ -139,87 +137,83 @@ __device__ __forceinline__ void convert_tile(float* fdst, const void* rawsrc) {
 // ------------------------------------------------------------------ hash
 // Thread (token t = 8*warp + lane/4, quarter q = lane%4).  The quarter owns the
 // 16-byte column chunks {2q, 2q+1, 2q+8, 2q+9} (D=64; {2q, 2q+1} for D=32),
-// which keeps each quarter-warp's row reads on distinct banks.  After the
-// shuffles every quarter holds all projections of its token.  Writes H[t][j]
-// for the planes of its tables, P[t][s] and PT[s][t] for their buckets.
-template <class LY>
+// which keeps each quarter-warp's row reads on distinct banks.  For every
+// table l the four quarters form partial dot products with its K planes and
+// combine them with two xor-shuffles; quarter l%4 owns the table and turns the
+// projections into tanh (kept in H[t][l*K+k]), the sigmoids and the 2^K corner
+// probabilities (P[t][s] and PT[s][t]).  K is a compile-time constant, so the
+// corner products and the per-table loops carry no guards.
+template <class LY, int K>
 __device__ __forceinline__ void hash_tile(const float* __restrict__ X, float* sm, const Shape& sh,
                                           float inv_scale, int64_t valid_rows) {
   constexpr int D = LY::Dv;
+  constexpr int R = 1 << K;
+  constexpr int NCH = D / 16;  // chunks per quarter
   const int lane = threadIdx.x & 31;
   const int t = (threadIdx.x >> 5) * 8 + (lane >> 2);
   const int q = lane & 3;
-  constexpr int NCH = D / 16;  // chunks per quarter
-  float acc[LKP];
-#pragma unroll
-  for (int j = 0; j < LKP; ++j) acc[j] = 0.f;
+  float x[NCH][4];
   const float* xr = X + t * LY::RS;
-  const float* pl = sm + LY::PL;
 #pragma unroll
   for (int i = 0; i < NCH; ++i) {
     const int ch = 2 * q + (i & 1) + 8 * (i >> 1);
-    const float4 x = *reinterpret_cast<const float4*>(xr + ch * 4);
-#pragma unroll
-    for (int j = 0; j < LKP; ++j) {
-      if (j < sh.LK) {
-        const float4 w = *reinterpret_cast<const float4*>(pl + j * LY::RS + ch * 4);
-        acc[j] = fmaf(x.x, w.x, fmaf(x.y, w.y, fmaf(x.z, w.z, fmaf(x.w, w.w, acc[j]))));
-      }
-    }
+    const float4 v = *reinterpret_cast<const float4*>(xr + ch * 4);
+    x[i][0] = v.x; x[i][1] = v.y; x[i][2] = v.z; x[i][3] = v.w;
   }
-#pragma unroll
-  for (int j = 0; j < LKP; ++j) {
-    if (j < sh.LK) {
-      acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 1);
-      acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 2);
-    }
-  }
-  const bool valid = t < valid_rows;
+  const float pv = t < valid_rows ? 1.f : 0.f;
   float* Hrow = sm + LY::H + t * (LKP + 1);
   float* Prow = sm + LY::P + t * LY::PS;
   float* PT = sm + LY::PT;
-  // park the projections in the token's H row (quarter q writes j = q mod 4),
-  // so the table owners can pick theirs without indexing a register array
+  const float* pl = sm + LY::PL;
+  for (int l = 0; l < sh.L; ++l) {
+    float acc[K];
 #pragma unroll
-  for (int j = 0; j < LKP; ++j)
-    if ((j & 3) == q && j < sh.LK) Hrow[j] = acc[j];
-  __syncwarp();
-  for (int l = q; l < sh.L; l += 4) {
-    float sp[5], sn[5];   // sigmoid(+2u), sigmoid(-2u) per plane of the table (K <= 5)
+    for (int k = 0; k < K; ++k) {
+      const float* row = pl + (l * K + k) * LY::RS;
+      float a = 0.f;
 #pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      sp[k] = sn[k] = 1.f;
-      if (k < sh.K) {
-        const float a = Hrow[l * sh.K + k];
-        const float h = tanh_exp(a);
-        Hrow[l * sh.K + k] = h;
+      for (int i = 0; i < NCH; ++i) {
+        const int ch = 2 * q + (i & 1) + 8 * (i >> 1);
+        const float4 w = *reinterpret_cast<const float4*>(row + ch * 4);
+        a = fmaf(x[i][0], w.x, fmaf(x[i][1], w.y, fmaf(x[i][2], w.z, fmaf(x[i][3], w.w, a))));
+      }
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      a += __shfl_xor_sync(0xffffffffu, a, 2);
+      acc[k] = a;
+    }
+    if ((l & 3) == q) {
+      float sp[K], sn[K];   // sigmoid(+2u), sigmoid(-2u) per plane of the table
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const float h = tanh_exp(acc[k]);
+        Hrow[l * K + k] = h;
         const float u = h * inv_scale;
         const float e = __expf(-2.f * fabsf(u));
         const float r = __frcp_rn(1.f + e);
         sp[k] = u >= 0.f ? r : e * r;
         sn[k] = u >= 0.f ? e * r : r;
       }
-    }
-    for (int r = 0; r < sh.R; ++r) {
-      float p = valid ? 1.f : 0.f;
 #pragma unroll
-      for (int k = 0; k < 5; ++k)
-        if (k < sh.K) p *= ((r >> (sh.K - 1 - k)) & 1) ? sp[k] : sn[k];
-      const int s = l * sh.R + r;
-      Prow[s] = p;
-      PT[s * LY::TS + t] = p;
+      for (int r = 0; r < R; ++r) {
+        float p = pv;
+#pragma unroll
+        for (int k = 0; k < K; ++k) p *= ((r >> (K - 1 - k)) & 1) ? sp[k] : sn[k];
+        const int s = l * R + r;
+        Prow[s] = p;
+        PT[s * LY::TS + t] = p;
+      }
     }
   }
 }
 
 // Softmax / corner / tanh backward in the hash layout: reads P, DP (+dA when
 // HAS_DA), H; writes DJT[j][t] = dL/dproj_j and accumulates sum_j du_j h_j.
-// A thread loads its table's R probabilities and gradients once (vector
-// loads), forms g_r = p_r (dp_r - sum p dp) and the K plane sums from them.
-template <class LY, bool HAS_DA>
+// The owner quarter of each table loads its R probabilities and gradients
+// once, forms g_r = p_r (dp_r - sum p dp) and the K plane sums from them.
+template <class LY, int K, bool HAS_DA>
 __device__ __forceinline__ void hash_backward(float* sm, const Shape& sh, float inv_scale,
                                               const float* dA, float& ds) {
-  constexpr int RM = LY::RM;
+  constexpr int R = 1 << K;
   const int lane = threadIdx.x & 31;
   const int t = (threadIdx.x >> 5) * 8 + (lane >> 2);
   const int q = lane & 3;
@@ -228,62 +222,43 @@ __device__ __forceinline__ void hash_backward(float* sm, const Shape& sh, float 
   const float* Drow = sm + LY::DP + t * LY::PS;
   float* DJT = sm + LY::DJT;
   for (int l = q; l < sh.L; l += 4) {
-    const int s0 = l * sh.R;
-    float g[RM];
-    float pbar = 0.f;
-    if (sh.R >= 4) {
+    const int s0 = l * R;
+    float p[R], d[R];
+    if constexpr (R >= 4) {
 #pragma unroll
-      for (int c = 0; c < RM / 4; ++c) {
-        if (4 * c < sh.R) {
-          const float4 pp = *reinterpret_cast<const float4*>(Prow + s0 + 4 * c);
-          float4 dd = *reinterpret_cast<const float4*>(Drow + s0 + 4 * c);
-          if (HAS_DA) {
-            const float4 aa = *reinterpret_cast<const float4*>(dA + s0 + 4 * c);
-            dd.x += aa.x; dd.y += aa.y; dd.z += aa.z; dd.w += aa.w;
-          }
-          g[4 * c] = pp.x; g[4 * c + 1] = pp.y; g[4 * c + 2] = pp.z; g[4 * c + 3] = pp.w;
-          pbar = fmaf(pp.x, dd.x, fmaf(pp.y, dd.y, fmaf(pp.z, dd.z, fmaf(pp.w, dd.w, pbar))));
+      for (int c = 0; c < R / 4; ++c) {
+        const float4 pp = *reinterpret_cast<const float4*>(Prow + s0 + 4 * c);
+        const float4 dd = *reinterpret_cast<const float4*>(Drow + s0 + 4 * c);
+        p[4 * c] = pp.x; p[4 * c + 1] = pp.y; p[4 * c + 2] = pp.z; p[4 * c + 3] = pp.w;
+        d[4 * c] = dd.x; d[4 * c + 1] = dd.y; d[4 * c + 2] = dd.z; d[4 * c + 3] = dd.w;
+        if constexpr (HAS_DA) {
+          const float4 aa = *reinterpret_cast<const float4*>(dA + s0 + 4 * c);
+          d[4 * c] += aa.x; d[4 * c + 1] += aa.y; d[4 * c + 2] += aa.z; d[4 * c + 3] += aa.w;
         }
       }
-      // second pass: g_r = p_r (dp_r - pbar) (re-read dp; p is in registers)
-#pragma unroll
-      for (int c = 0; c < RM / 4; ++c) {
-        if (4 * c < sh.R) {
-          float4 dd = *reinterpret_cast<const float4*>(Drow + s0 + 4 * c);
-          if (HAS_DA) {
-            const float4 aa = *reinterpret_cast<const float4*>(dA + s0 + 4 * c);
-            dd.x += aa.x; dd.y += aa.y; dd.z += aa.z; dd.w += aa.w;
-          }
-          g[4 * c] *= dd.x - pbar;
-          g[4 * c + 1] *= dd.y - pbar;
-          g[4 * c + 2] *= dd.z - pbar;
-          g[4 * c + 3] *= dd.w - pbar;
-        }
-      }
-    } else {   // R == 2
+    } else {
       const float2 pp = *reinterpret_cast<const float2*>(Prow + s0);
-      float2 dd = *reinterpret_cast<const float2*>(Drow + s0);
-      if (HAS_DA) {
+      const float2 dd = *reinterpret_cast<const float2*>(Drow + s0);
+      p[0] = pp.x; p[1] = pp.y; d[0] = dd.x; d[1] = dd.y;
+      if constexpr (HAS_DA) {
         const float2 aa = *reinterpret_cast<const float2*>(dA + s0);
-        dd.x += aa.x; dd.y += aa.y;
+        d[0] += aa.x; d[1] += aa.y;
       }
-      pbar = fmaf(pp.x, dd.x, pp.y * dd.y);
-      g[0] = pp.x * (dd.x - pbar);
-      g[1] = pp.y * (dd.y - pbar);
     }
+    float pbar = 0.f;
 #pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      if (k < sh.K) {
-        const int bit = sh.K - 1 - k;
-        float du = 0.f;
+    for (int r = 0; r < R; ++r) pbar = fmaf(p[r], d[r], pbar);
 #pragma unroll
-        for (int r = 0; r < RM; ++r)
-          if (r < sh.R) du += ((r >> bit) & 1) ? g[r] : -g[r];
-        const int j = l * sh.K + k;
-        const float h = Hrow[j];
-        ds = fmaf(du, h, ds);
-        DJT[j * LY::TS + t] = du * inv_scale * (1.f - h * h);
-      }
+    for (int r = 0; r < R; ++r) p[r] *= d[r] - pbar;   // p now holds g_r
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float du = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) du += ((r >> (K - 1 - k)) & 1) ? p[r] : -p[r];
+      const int j = l * K + k;
+      const float h = Hrow[j];
+      ds = fmaf(du, h, ds);
+      DJT[j * LY::TS + t] = du * inv_scale * (1.f - h * h);
     }
   }
 }
@@ -530,7 +505,7 @@ struct TilePipe {
   }
 
 // F1: per-CTA partial [V|1] bucket sums of the key side.
-template <typename T, int D, int SPAD>
+template <typename T, int D, int SPAD, int K>
 __global__ void __launch_bounds__(NT, 2) k_tile_reduce(const Params prm) {
   RACE_TILE_PROLOGUE
   const T* kb = static_cast<const T*>(prm.k) + stream_offset(prm.lk, n, prm.B, prm.H);
@@ -546,7 +521,7 @@ __global__ void __launch_bounds__(NT, 2) k_tile_reduce(const Params prm) {
     float *X, *Y;
     int64_t tile0;
     pipe.acquire(it, X, Y, tile0);
-    hash_tile<LY>(X, sm, sh, inv_scale, tr.t1 - tile0);
+    hash_tile<LY, K>(X, sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
     agg.add_tile(sm + LY::P, Y, w * 8, w * 8 + 8);
     if (threadIdx.x < SPAD * 8) {
@@ -573,7 +548,7 @@ __global__ void __launch_bounds__(NT, 2) k_tile_reduce(const Params prm) {
 }
 
 // F2: out = sum_s pQ_s E_s.
-template <typename T, int D, int SPAD>
+template <typename T, int D, int SPAD, int K>
 __global__ void __launch_bounds__(NT, 2) k_tile_readout(const Params prm) {
   RACE_TILE_PROLOGUE
   const float* st = prm.state + (size_t)n * prm.SS;
@@ -587,7 +562,7 @@ __global__ void __launch_bounds__(NT, 2) k_tile_readout(const Params prm) {
     float *X, *Y;
     int64_t tile0;
     pipe.acquire(it, X, Y, tile0);
-    hash_tile<LY>(X, sm, sh, inv_scale, tr.t1 - tile0);
+    hash_tile<LY, K>(X, sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
     float o[2][8];
     int t, c;
@@ -600,7 +575,7 @@ __global__ void __launch_bounds__(NT, 2) k_tile_readout(const Params prm) {
 
 // B1: dq and the per-CTA partial dE = sum_t pQ dO^T (warps 4-7), dp = dO E^T
 // (warps 0-3), then the hash backward and dq = dproj . planes.
-template <typename T, int D, int SPAD>
+template <typename T, int D, int SPAD, int K>
 __global__ void __launch_bounds__(NT, 2) k_tile_bwd_q(const Params prm) {
   RACE_TILE_PROLOGUE
   const float* st = prm.state + (size_t)n * prm.SS;
@@ -619,12 +594,12 @@ __global__ void __launch_bounds__(NT, 2) k_tile_bwd_q(const Params prm) {
     float *X, *Y;
     int64_t tile0;
     pipe.acquire(it, X, Y, tile0);
-    hash_tile<LY>(X, sm, sh, inv_scale, tr.t1 - tile0);
+    hash_tile<LY, K>(X, sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
     if (w < 4) rowdot<LY>(Y, sm + LY::TAB, sm + LY::DP, 0);
     else agg.add_tile(sm + LY::P, Y, (w - 4) * 16, (w - 4) * 16 + 16);
     __syncthreads();
-    hash_backward<LY, false>(sm, sh, inv_scale, nullptr, ds);
+    hash_backward<LY, K, false>(sm, sh, inv_scale, nullptr, ds);
     __syncthreads();
     float o[2][8];
     int t, c;
@@ -643,7 +618,7 @@ __global__ void __launch_bounds__(NT, 2) k_tile_bwd_q(const Params prm) {
 }
 
 // B2: dv = pK . dB (warps 4-7), dpK = v . dB^T + dA (warps 0-3), then dk.
-template <typename T, int D, int SPAD>
+template <typename T, int D, int SPAD, int K>
 __global__ void __launch_bounds__(NT, 2) k_tile_bwd_kv(const Params prm) {
   RACE_TILE_PROLOGUE
   const float* st = prm.state + (size_t)n * prm.SS;
@@ -679,7 +654,7 @@ __global__ void __launch_bounds__(NT, 2) k_tile_bwd_kv(const Params prm) {
     float *X, *Y;
     int64_t tile0;
     pipe.acquire(it, X, Y, tile0);
-    hash_tile<LY>(X, sm, sh, inv_scale, tr.t1 - tile0);
+    hash_tile<LY, K>(X, sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
     if (w < 4) {
       rowdot<LY>(Y, sm + LY::TAB, sm + LY::DP, 0);
@@ -693,7 +668,7 @@ __global__ void __launch_bounds__(NT, 2) k_tile_bwd_kv(const Params prm) {
       }
     }
     __syncthreads();
-    hash_backward<LY, true>(sm, sh, inv_scale, dA, ds);
+    hash_backward<LY, K, true>(sm, sh, inv_scale, dA, ds);
     __syncthreads();
     float o[2][8];
     int t, c;
