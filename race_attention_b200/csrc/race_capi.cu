@@ -190,7 +190,7 @@ int make_plan(const race_desc_t* d, Plan* p) {
   const int sms = sm_count();
   const int64_t T = d->tokens;
   if (!d->causal) {
-    // one resident wave of 2 CTAs per SM, each walking >= 4 tiles of 64 tokens
+    // one resident wave (two CTAs per SM), each walking several tiles
     const int64_t target = (int64_t)sms * 2;
     int64_t P = (target + p->N - 1) / p->N;
     const int64_t by_len = (T + 255) / 256;
@@ -310,7 +310,7 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
         cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem_bytes);
     if (ea != cudaSuccess) return cuda_fail(ea);
   }
-  const cudaError_t e = cudaLaunchKernel(ki.fn, grid, dim3(kThreads), args, ki.smem_bytes, stream);
+  const cudaError_t e = cudaLaunchKernel(ki.fn, grid, dim3(ki.threads), args, ki.smem_bytes, stream);
   if (e != cudaSuccess) return cuda_fail(e);
   return RACE_OK;
 }

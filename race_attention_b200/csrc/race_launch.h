@@ -20,6 +20,7 @@ struct KernelInfo {
   const void* fn;   // __global__ symbol, launched with one `Params` argument
   int groups;       // token groups per CTA
   int smem_bytes;   // dynamic shared memory
+  int threads;      // threads per CTA
 };
 
 // Padded bucket counts the kernels are instantiated for.

@@ -89,13 +89,13 @@ __device__ __forceinline__ float tanh_exp(float x) {
 // shared memory: fp32 rows go straight into the padded fp32 tile, bf16 rows
 // into the unpadded raw buffer (converted later by convert_tile).  Rows past
 // the range are zero-filled.
-template <typename T, int D>
+template <typename T, int D, int NTH = NT, int TTL = TT>
 __device__ __forceinline__ void stage_tile(float* fdst, void* rawdst, const T* base, int64_t st,
                                            int64_t t0, int64_t t1) {
   constexpr int RS = D + 4;
   if constexpr (sizeof(T) == 4) {
     constexpr int CPR = D / 4;  // 16-byte chunks per row
-    for (int i = threadIdx.x; i < TT * CPR; i += NT) {
+    for (int i = threadIdx.x; i < TTL * CPR; i += NTH) {
       const int r = i / CPR, ch = i % CPR;
       const int64_t t = t0 + r;
       const bool ok = t < t1;
@@ -105,7 +105,7 @@ __device__ __forceinline__ void stage_tile(float* fdst, void* rawdst, const T* b
   } else {
     constexpr int CPR = D / 8;
     __nv_bfloat16* raw = static_cast<__nv_bfloat16*>(rawdst);
-    for (int i = threadIdx.x; i < TT * CPR; i += NT) {
+    for (int i = threadIdx.x; i < TTL * CPR; i += NTH) {
       const int r = i / CPR, ch = i % CPR;
       const int64_t t = t0 + r;
       const bool ok = t < t1;
@@ -115,11 +115,11 @@ __device__ __forceinline__ void stage_tile(float* fdst, void* rawdst, const T* b
   }
 }
 
-template <int D>
+template <int D, int NTH = NT, int TTL = TT>
 __device__ __forceinline__ void convert_tile(float* fdst, const void* rawsrc) {
   constexpr int RS = D + 4;
   const __nv_bfloat16* raw = static_cast<const __nv_bfloat16*>(rawsrc);
-  for (int i = threadIdx.x; i < TT * D / 8; i += NT) {
+  for (int i = threadIdx.x; i < TTL * D / 8; i += NTH) {
     const int r = i / (D / 8), ch = i % (D / 8);
     const uint4 u = *reinterpret_cast<const uint4*>(raw + r * D + ch * 8);
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -434,12 +434,13 @@ struct TileRange {
   int64_t t0, t1;
   int ntiles;
 };
+template <int TTL = TT>
 __device__ __forceinline__ TileRange tile_range(int64_t T, int P, int part) {
-  const int64_t tiles = (T + TT - 1) / TT;
+  const int64_t tiles = (T + TTL - 1) / TTL;
   const int64_t a = tiles * part / P, b = tiles * (part + 1) / P;
   TileRange r;
-  r.t0 = a * TT;
-  r.t1 = min(T, b * TT);
+  r.t0 = a * TTL;
+  r.t1 = min(T, b * TTL);
   r.ntiles = (int)(b - a);
   return r;
 }
@@ -449,7 +450,7 @@ __device__ __forceinline__ TileRange tile_range(int64_t T, int P, int part) {
 //   TilePipe<T, LY, TWO> pipe{...};  pipe.start();
 //   for (i < ntiles) { pipe.acquire(i, X, Y, tile0); ...compute...; __syncthreads(); }
 //   pipe.finish();
-template <typename T, class LY, bool TWO>
+template <typename T, class LY, bool TWO, int NTH = NT, int TTL = TT>
 struct TilePipe {
   static constexpr int D = LY::Dv;
   static constexpr bool BF = sizeof(T) == 2;
@@ -459,29 +460,29 @@ struct TilePipe {
   const T* yb;
   int64_t yst;
   TileRange tr;
-  __device__ __forceinline__ float* fx(int st) const { return sm + LY::XS + (BF ? 0 : st * TT * LY::RS); }
-  __device__ __forceinline__ float* fy(int st) const { return sm + LY::YS + (BF ? 0 : st * TT * LY::RS); }
-  __device__ __forceinline__ void* rx(int st) const { return sm + LY::RAW + (st * 2 + 0) * (TT * D / 2); }
-  __device__ __forceinline__ void* ry(int st) const { return sm + LY::RAW + (st * 2 + 1) * (TT * D / 2); }
+  __device__ __forceinline__ float* fx(int st) const { return sm + LY::XS + (BF ? 0 : st * TTL * LY::RS); }
+  __device__ __forceinline__ float* fy(int st) const { return sm + LY::YS + (BF ? 0 : st * TTL * LY::RS); }
+  __device__ __forceinline__ void* rx(int st) const { return sm + LY::RAW + (st * 2 + 0) * (TTL * D / 2); }
+  __device__ __forceinline__ void* ry(int st) const { return sm + LY::RAW + (st * 2 + 1) * (TTL * D / 2); }
   __device__ __forceinline__ void start() const {
     if (tr.ntiles <= 0) return;
-    stage_tile<T, D>(fx(0), rx(0), xb, xst, tr.t0, tr.t1);
-    if (TWO) stage_tile<T, D>(fy(0), ry(0), yb, yst, tr.t0, tr.t1);
+    stage_tile<T, D, NTH, TTL>(fx(0), rx(0), xb, xst, tr.t0, tr.t1);
+    if (TWO) stage_tile<T, D, NTH, TTL>(fy(0), ry(0), yb, yst, tr.t0, tr.t1);
     cp_commit();
   }
   __device__ __forceinline__ void acquire(int i, float*& X, float*& Y, int64_t& tile0) const {
     const int st = i & 1;
-    tile0 = tr.t0 + (int64_t)i * TT;
+    tile0 = tr.t0 + (int64_t)i * TTL;
     if (i + 1 < tr.ntiles) {
-      stage_tile<T, D>(fx(st ^ 1), rx(st ^ 1), xb, xst, tile0 + TT, tr.t1);
-      if (TWO) stage_tile<T, D>(fy(st ^ 1), ry(st ^ 1), yb, yst, tile0 + TT, tr.t1);
+      stage_tile<T, D, NTH, TTL>(fx(st ^ 1), rx(st ^ 1), xb, xst, tile0 + TTL, tr.t1);
+      if (TWO) stage_tile<T, D, NTH, TTL>(fy(st ^ 1), ry(st ^ 1), yb, yst, tile0 + TTL, tr.t1);
     }
     cp_commit();
     cp_wait<1>();
     __syncthreads();
     if constexpr (BF) {
-      convert_tile<D>(fx(0), rx(st));
-      if (TWO) convert_tile<D>(fy(0), ry(st));
+      convert_tile<D, NTH, TTL>(fx(0), rx(st));
+      if (TWO) convert_tile<D, NTH, TTL>(fy(0), ry(st));
       __syncthreads();
     }
     X = fx(st);
