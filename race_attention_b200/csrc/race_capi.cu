@@ -161,9 +161,9 @@ struct Plan {
 bool tensor_ok(const race_tensor_t& t, int elem_bytes) {
   if (t.data == nullptr) return false;
   if (reinterpret_cast<uintptr_t>(t.data) % 16 != 0) return false;
-  // each lane touches 4 consecutive elements (2 for the causal dq pass):
-  // every stride must keep 8-byte (bf16) / 16-byte (fp32) alignment
-  const int64_t q = 16 / elem_bytes / (elem_bytes == 2 ? 2 : 1);
+  // rows are moved by 16-byte vector loads and bulk copies: every row must
+  // start on a 16-byte boundary (strides in multiples of 16 bytes)
+  const int64_t q = 16 / elem_bytes;
   return t.stride_m % q == 0 && t.stride_b % q == 0 && t.stride_h % q == 0 && t.stride_t % q == 0;
 }
 
@@ -275,6 +275,8 @@ int prepare(const race_desc_t* d, const float* planes, const float* scale, void*
   p.scale = scale;
   p.part = c->part;
   p.dscale_part = c->dscale_part;
+  // the last 16 floats of the workspace hold the sticky device error word
+  p.err = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + ws_bytes(c->plan) - 64);
   p.P = c->plan.P;
   p.CL = c->plan.CL;
   p.NC = c->plan.NC;

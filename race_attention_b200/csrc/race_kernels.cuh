@@ -63,6 +63,7 @@ struct Params {
   int CL;                // causal chunk length
   int64_t NC;            // causal chunks per stream
   int SS;                // floats per slot
+  unsigned* err;         // sticky device error word (workspace tail), 0 = ok
 };
 
 __host__ __device__ constexpr int round_up(int a, int b) { return (a + b - 1) / b * b; }

@@ -63,13 +63,15 @@ struct Lay {
   static constexpr int DJ2 = PT2 + 2 * SM16 * PT2S;     // float2 [TT][DJ2S]
   static constexpr int DP = DJ2 + 2 * TT * DJ2S;        // [TT][PS]; PROJ aliases it
   static constexpr int PROJ = DP;                       // [TT][JS]
-  static constexpr int MISC = DP + (PS > JS ? TT * PS : TT * JS);  // 64 floats
-  static constexpr int RAW = MISC + 64;
+  static constexpr int MISC = DP + (PS > JS ? TT * PS : TT * JS);  // 64 floats, then 2 mbarriers
+  static constexpr int BAR = MISC + 64;                 // 2 x uint64 mbarriers
+  static constexpr int RAW = BAR + 4;
   static constexpr int RAW_FLOATS = BF ? 2 * 2 * TT * D / 2 : 0;
   static constexpr int FLOATS = RAW + RAW_FLOATS;
   static constexpr int Dv = D;
   static constexpr int Sv = SPAD;
   static_assert(S8 <= 32, "bucket count above 32");
+  static_assert(BAR % 2 == 0 && RAW % 4 == 0 && (XS + YS) % 4 == 0, "alignment");
   static_assert(PLB % 2 == 0 && TABB % 2 == 0 && P2 % 2 == 0, "float2 alignment");
 };
 

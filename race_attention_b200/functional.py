@@ -27,9 +27,11 @@ _SUPPORTED = (torch.float32, torch.bfloat16)
 
 
 def _aligned(x: torch.Tensor) -> bool:
+    """Rows must start on 16-byte boundaries (vector loads and bulk copies)."""
     if x.stride(-1) != 1 or x.data_ptr() % 16 != 0:
         return False
-    return all(s % 4 == 0 for s in x.stride()[:-1])
+    q = 16 // x.element_size()
+    return all(s % q == 0 for s in x.stride()[:-1])
 
 
 def _prep(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
@@ -38,7 +40,7 @@ def _prep(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     if not _aligned(x):
         x = x.contiguous()
         if not _aligned(x):
-            raise ValueError("RACE attention needs head_dim % 4 == 0 and 16-byte aligned storage")
+            raise ValueError("RACE attention needs 16-byte aligned rows (head_dim * element size % 16 == 0)")
     return x
 
 
