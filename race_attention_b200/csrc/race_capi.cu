@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(1024) k_dscale_final(const float* __restrict__
 struct Plan {
   int N, S, LK, SS, width, spad, P, CL;
   int64_t NC;
-  size_t state_floats, gstate_floats, part_floats, dscale_floats;
+  size_t state_floats, gstate_floats, part_floats, dscale_floats, tile_doubles;
 };
 
 bool tensor_ok(const race_tensor_t& t, int elem_bytes) {
@@ -186,44 +186,37 @@ int make_plan(const race_desc_t* d, Plan* p) {
   p->spad = spad_for(S);
   const int D = d->head_dim;
   p->width = S * D + S;
-  p->SS = d->causal ? round_up(S * D + 3 * S, 4) : round_up(S * D + S, 4);
+  p->SS = round_up(S * D + S, 4);
   const int sms = sm_count();
   const int64_t T = d->tokens;
+  // contiguous token ranges, one CTA each: one resident wave of two CTAs per
+  // SM, every range at least a few 32-token tiles long
+  const int64_t target = (int64_t)sms * 2;
+  int64_t P = (target + p->N - 1) / p->N;
+  const int64_t by_len = (T + 127) / 128;
+  if (P > by_len) P = by_len;
+  if (P < 1) P = 1;
+  p->P = (int)P;
+  p->dscale_floats = (size_t)p->N * p->P;
   if (!d->causal) {
-    // one resident wave (two CTAs per SM), each walking several tiles
-    const int64_t target = (int64_t)sms * 2;
-    int64_t P = (target + p->N - 1) / p->N;
-    const int64_t by_len = (T + 255) / 256;
-    if (P > by_len) P = by_len;
-    if (P < 1) P = 1;
-    p->P = (int)P;
     p->CL = 0;
     p->NC = 0;
     p->state_floats = (size_t)p->N * p->SS;
     p->gstate_floats = (size_t)p->N * p->SS;
     p->part_floats = (size_t)p->N * p->P * p->SS;
-    p->dscale_floats = (size_t)p->N * p->P;
+    p->tile_doubles = 0;
   } else {
-    int64_t CL = d->chunk;
-    if (CL == 0) {
-      // enough chunks to give every SM two CTAs of token groups
-      const int64_t groups = (int64_t)sms * 2 * (kThreads / (D / 4));
-      CL = (N64 * T + groups - 1) / groups;
-      CL = (CL + 63) / 64 * 64;
-      if (CL < 128) CL = 128;
-      if (CL > 2048) CL = 2048;
-    }
-    if (CL > (1 << 20)) return RACE_ERR_UNSUPPORTED;
-    p->CL = (int)CL;
-    p->NC = T > 0 ? (T + CL - 1) / CL : 1;
-    p->P = 0;
-    const size_t slots = (size_t)p->N * p->NC;
+    // state: exclusive prefix slot of every range; gstate: exclusive suffix
+    // slot of every range, then alpha [N][T][S], then the float64 key mass at
+    // every 32-token tile start [N][tiles][S8]
+    p->CL = 32;
+    p->NC = p->P;
+    const size_t slots = (size_t)p->N * p->P;
+    const int64_t tiles = (T + 31) / 32;
     p->state_floats = slots * p->SS;
-    p->gstate_floats = slots * p->SS + (size_t)p->N * T * S;
+    p->tile_doubles = (size_t)p->N * tiles * round_up(S, 8);
+    p->gstate_floats = slots * p->SS + (size_t)p->N * T * S + 2 * p->tile_doubles + 2;
     p->part_floats = 0;
-    // largest causal grid: C = 2 kernels have the fewest groups per CTA
-    const int64_t g2 = kThreads / (D / 2);
-    p->dscale_floats = (size_t)((slots + g2 - 1) / g2);
   }
   return RACE_OK;
 }
@@ -298,13 +291,7 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
   else
     ok = d->head_dim == 32 ? kernels_bf16_d32(sp, K, id, &ki) : kernels_bf16_d64(sp, K, id, &ki);
   if (!ok) return RACE_ERR_UNSUPPORTED;
-  dim3 grid;
-  if (id == K_NC_REDUCE || id == K_NC_READOUT || id == K_NC_BWD_Q || id == K_NC_BWD_KV) {
-    grid = dim3(c.plan.P, c.plan.N, 1);
-  } else {
-    const int64_t units = (int64_t)c.plan.N * c.plan.NC;
-    grid = dim3((unsigned)((units + ki.groups - 1) / ki.groups), 1, 1);
-  }
+  const dim3 grid(c.plan.P, c.plan.N, 1);
   Params prm = c.prm;
   void* args[] = {&prm};
   if (ki.smem_bytes > 48 * 1024) {
@@ -340,10 +327,12 @@ int dscale_final(const Call& c, int count, float* dscale, int accumulate, cudaSt
   return post(stream);
 }
 
-int64_t causal_grid(const race_desc_t* d, const Call& c, int C) {
-  const int64_t g = kThreads / (d->head_dim / C);
-  const int64_t units = (int64_t)c.plan.N * c.plan.NC;
-  return (units + g - 1) / g;
+// alpha and the per-tile key mass live behind the gradient slots
+void causal_scratch(Call& c, float* gstate) {
+  const size_t slot_floats = (size_t)c.plan.N * c.plan.P * c.plan.SS;
+  c.prm.alpha = gstate + slot_floats;
+  const size_t off = slot_floats + (size_t)c.plan.N * c.prm.T * c.prm.S;
+  c.prm.tilemass = reinterpret_cast<double*>(gstate + ((off + 1) & ~size_t(1)));
 }
 
 int zero_fill(void* p, size_t bytes, cudaStream_t stream) {
@@ -423,8 +412,9 @@ int race_forward_reduce(const race_desc_t* desc, race_tensor_t k, race_tensor_t 
       if (e != cudaSuccess) return cuda_fail(e);
     }
   } else {
-    c.prm.state_out = state;
-    RACE_TRY(launch(desc, c, K_C_TOTALS, stream));
+    // range totals straight into the state slots, then the exclusive scan
+    c.prm.part = state;
+    RACE_TRY(launch(desc, c, K_NC_REDUCE, stream));
     RACE_TRY(chunk_scan(c, state, 0, total, stream));
   }
   return RACE_OK;
@@ -507,10 +497,10 @@ int race_backward_q(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, r
     c.prm.k = k.data;
     c.prm.v = v.data;
     c.prm.gstate_out = gstate;
-    c.prm.alpha = gstate + (size_t)c.plan.N * c.plan.NC * c.plan.SS;
+    causal_scratch(c, gstate);
     RACE_TRY(launch(desc, c, K_C_BWD_Q, stream));
     RACE_TRY(chunk_scan(c, gstate, 1, total, stream));
-    RACE_TRY(dscale_final(c, (int)causal_grid(desc, c, 2), dscale, 0, stream));
+    RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 0, stream));
   }
   return RACE_OK;
 }
@@ -547,9 +537,9 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
     fill_layout(c.prm.ldo, dout);
     c.prm.q = q.data;
     c.prm.dout = dout.data;
-    c.prm.alpha = const_cast<float*>(gstate) + (size_t)c.plan.N * c.plan.NC * c.plan.SS;
+    causal_scratch(c, const_cast<float*>(gstate));
     RACE_TRY(launch(desc, c, K_C_BWD_KV, stream));
-    RACE_TRY(dscale_final(c, (int)causal_grid(desc, c, 2), dscale, 1, stream));
+    RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 1, stream));
   }
   return RACE_OK;
 }

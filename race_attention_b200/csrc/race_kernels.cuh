@@ -64,6 +64,7 @@ struct Params {
   int64_t NC;            // causal chunks per stream
   int SS;                // floats per slot
   unsigned* err;         // sticky device error word (workspace tail), 0 = ok
+  double* tilemass;      // causal: key mass at every 32-token tile start [N][tiles][S8]
 };
 
 __host__ __device__ constexpr int round_up(int a, int b) { return (a + b - 1) / b * b; }

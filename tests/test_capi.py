@@ -54,8 +54,13 @@ def test_query_sizes(lib):
     assert sz.state_bytes == N * sz.slot_floats * 4
     assert sz.workspace_bytes > 0
     assert lib.race_query(desc(causal=1, tokens=1000, chunk=128), sz) == 0
-    assert sz.chunk == 128 and sz.num_chunks == 8
-    assert sz.gstate_bytes == (N * 8 * sz.slot_floats + N * 1000 * S) * 4
+    # causal: one prefix slot per token range (32-token tiles), then alpha and
+    # the float64 key mass of every tile behind the gradient slots
+    assert sz.chunk == 32 and 1 <= sz.num_chunks <= 8
+    slots = N * sz.num_chunks * sz.slot_floats
+    assert sz.state_bytes == slots * 4
+    tiles = (1000 + 31) // 32
+    assert sz.gstate_bytes == (slots + N * 1000 * S + 2 * N * tiles * 24 + 2) * 4
 
 
 @pytest.mark.parametrize("bad,code", [

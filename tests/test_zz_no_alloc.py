@@ -53,7 +53,7 @@ def test_static_forward_matches_race_forward(causal, N, T):
 
 def test_static_forward_rejects_oversized_shapes():
     lib = _lib.load()
-    shape = (1, 1, 1 << 22, 1, 64)          # causal: chunk states need > 8 MiB
-    desc = make_desc(shape, torch.float32, 2, 5, True, 1e-6, 128, True)
+    shape = (1, 6000, 1024, 1, 64)          # 6000 streams: their states need > 8 MiB
+    desc = make_desc(shape, torch.float32, 2, 5, False, 1e-6, 0, True)
     t = _lib.RaceTensor(None, 0, 0, 0, 0)
     assert lib.race_forward_static(desc, t, t, t, None, None, t, None) == _lib.RACE_ERR_TOO_LARGE
