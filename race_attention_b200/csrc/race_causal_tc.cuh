@@ -160,21 +160,56 @@ __device__ __forceinline__ void probs_to(float* sm, const Shape& sh, float inv_s
   }
 }
 
-// ACUM[t][s] = A0_s + sum_{tau<=t} pK_s(tau) (float64 running sum), and
-// A0 += the tile's key mass.  One thread per bucket.
+// ACUM[t][s] = A0_s + sum_{tau<=t} pK_s(tau) and A0 += the tile's key mass
+// (A0 in float64, the in-tile sum of <= 32 terms in float32).  Warp w scans
+// buckets s = w, w+8, ... with lane = token.  Kp holds pK split [t][s].
 template <class LY>
-__device__ __forceinline__ void key_mass(float* sm, int S) {
-  const int s = threadIdx.x;
-  if (s < S) {
-    double* A0 = reinterpret_cast<double*>(sm + LY::A0D);
-    const float2* K2 = reinterpret_cast<const float2*>(sm + LY::K2);
-    double a = A0[s];
-    for (int t = 0; t < TT; ++t) {
-      const float2 p = K2[t * LY::P2S + s];
-      a += (double)(p.x + p.y);
-      sm[LY::ACUM + t * LY::ACS + s] = (float)a;
+__device__ __forceinline__ void key_mass(float* sm, const float2* Kp, int S) {
+  const int lane = threadIdx.x & 31;
+  double* A0 = reinterpret_cast<double*>(sm + LY::A0D);
+  for (int s = threadIdx.x >> 5; s < S; s += NW) {
+    const float2 p = Kp[lane * LY::P2S + s];
+    float v = p.x + p.y;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
     }
-    A0[s] = a;
+    const double a0 = A0[s];
+    sm[LY::ACUM + lane * LY::ACS + s] = (float)(a0 + (double)v);
+    __syncwarp();
+    if (lane == 31) A0[s] = a0 + (double)v;
+  }
+}
+
+// In place: X[t][s] = base_s + sum_{tau >= t} X[tau][s] for s < S (lane = t),
+// and base_s += sum over the tile.  Returns nothing; base lives in smem.
+template <class LY>
+__device__ __forceinline__ void suffix_scan(float* X, float* base, int S) {
+  const int lane = threadIdx.x & 31;
+  for (int s = threadIdx.x >> 5; s < S; s += NW) {
+    float v = X[lane * LY::ACS + s];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float u = __shfl_down_sync(0xffffffffu, v, o);
+      if (lane + o < 32) v += u;
+    }
+    const float b = base[s];
+    X[lane * LY::ACS + s] = b + v;
+    __syncwarp();
+    if (lane == 0) base[s] = b + v;
+  }
+}
+
+// sum over the tile's tokens of X[t][s], added into acc (thread s < S holds acc).
+template <class LY>
+__device__ __forceinline__ void column_sums(const float* X, float* out, int S) {
+  const int lane = threadIdx.x & 31;
+  for (int s = threadIdx.x >> 5; s < S; s += NW) {
+    float v = X[lane * LY::ACS + s];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) out[s] += v;
   }
 }
 
@@ -216,7 +251,7 @@ __device__ __forceinline__ void refresh_state_table(float* sm) {
 
 // STF[s][d] += sum_t A^T[s][t] Y[t][d] (A^T given split [SM16][PT2S]),
 // for buckets s < S8; warp w owns (S8/16 rounded) x (D/8) tiles like AggTC.
-template <class LY>
+template <class LY, bool EX = false>
 __device__ __forceinline__ void state_add(float* sm, const float2* AT, const float* Y) {
   constexpr int D = LY::Dv;
   constexpr int NTILES = D / 8;
@@ -227,7 +262,7 @@ __device__ __forceinline__ void state_add(float* sm, const float2* AT, const flo
   const int m0 = 16 * (first / NTILES), n0 = 8 * (first % NTILES);
   float c[PER][4];
   zero(c);
-  wgemm<PER, TT / 8>(c, ASplit<LY::PT2S>{AT}, m0, BView<LY::RS, 1>{Y}, n0);
+  wgemm<PER, TT / 8>(c, ASplit<LY::PT2S>{AT}, m0, BView<LY::RS, 1, EX>{Y}, n0);
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
 #pragma unroll
@@ -302,12 +337,12 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_fwd(const Params prm) {
     const float* Kx = pipe.in(1, it);
     const float* V = pipe.in(2, it);
     const int64_t valid = tr.t1 - tile0;
-    projections<LY>(Kx, sm);
+    projections<LY, sizeof(T) == 2>(Kx, sm);
     __syncthreads();
     probs_to<LY, K>(sm, sh, inv_scale, valid, K2, KT2, nullptr);
     __syncthreads();
-    key_mass<LY>(sm, prm.S);
-    projections<LY>(Q, sm);
+    key_mass<LY>(sm, K2, prm.S);
+    projections<LY, sizeof(T) == 2>(Q, sm);
     __syncthreads();
     probs_to<LY, K>(sm, sh, inv_scale, valid, reinterpret_cast<float2*>(sm + LY::P2), nullptr,
                     nullptr);
@@ -332,11 +367,11 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_fwd(const Params prm) {
       wgemm<D / 32, LY::S8 / 8>(c, ASplit<LY::P2S>{W2}, m0,
                                 BSplit<LY::B2S, 1>{reinterpret_cast<const float2*>(sm + LY::STB)}, n0);
       wgemm<D / 32, TT / 8>(c, ASplit<LY::MS>{reinterpret_cast<const float2*>(sm + LY::MM2)}, m0,
-                            BView<LY::RS, 1>{V}, n0);
+                            BView<LY::RS, 1, sizeof(T) == 2>{V}, n0);
       store_c_global<T, D / 32>(c, ob, prm.lo.st, tile0, tr.t1, m0, n0);
     }
     __syncthreads();
-    state_add<LY>(sm, KT2, V);   // B0 += pK^T V
+    state_add<LY, sizeof(T) == 2>(sm, KT2, V);   // B0 += pK^T V
     __syncthreads();
     refresh_state_table<LY>(sm);
     __syncthreads();
@@ -378,7 +413,7 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_q(const Params prm) {
   const int gfirst = (threadIdx.x >> 5) * PER;
   const bool glive = gfirst < TILES;
   const int gm0 = 16 * (glive ? gfirst / NTILES : 0), gn0 = 8 * (glive ? gfirst % NTILES : 0);
-  float ga = 0.f;   // thread s < S: range total of alpha_s
+  if (threadIdx.x < 32) sm[LY::VEC + threadIdx.x] = 0.f;   // range total of alpha_s
   float ds = 0.f;
   for (int it = 0; it < tr.ntiles; ++it) {
     const int64_t tile0 = pipe.acquire(it);
@@ -391,18 +426,18 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_q(const Params prm) {
     if (threadIdx.x < prm.S)
       tileA[((size_t)n * ntile_stream + tile0 / TT) * LY::S8 + threadIdx.x] =
           reinterpret_cast<const double*>(sm + LY::A0D)[threadIdx.x];
-    projections<LY>(Kx, sm);
+    projections<LY, sizeof(T) == 2>(Kx, sm);
     __syncthreads();
     probs_to<LY, K>(sm, sh, inv_scale, valid, K2, KT2, nullptr);
     __syncthreads();
-    key_mass<LY>(sm, prm.S);
-    projections<LY>(Q, sm);
+    key_mass<LY>(sm, K2, prm.S);
+    projections<LY, sizeof(T) == 2>(Q, sm);
     __syncthreads();
     probs_to<LY, K>(sm, sh, inv_scale, valid, reinterpret_cast<float2*>(sm + LY::P2), nullptr,
                     sm + LY::H);
     // M = dO V^T, lower-triangular (other warps' reads of PROJ are done: the
     // product only touches MM2)
-    masked_32x32<LY, true, D / 8>(sm, AView<LY::RS, 1>{G}, BView<1, LY::RS>{V});
+    masked_32x32<LY, true, D / 8>(sm, AView<LY::RS, 1, sizeof(T) == 2>{G}, BView<1, LY::RS, sizeof(T) == 2>{V});
     __syncthreads();
     {   // W and its transpose
       const int t = threadIdx.x >> 3, e = threadIdx.x & 7;
@@ -420,7 +455,7 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_q(const Params prm) {
       if (nt < LY::S8 / 8) {
         float c[1][4];
         zero(c);
-        wgemm<1, D / 8>(c, AView<LY::RS, 1>{G}, 16 * (w & 1),
+        wgemm<1, D / 8>(c, AView<LY::RS, 1, sizeof(T) == 2>{G}, 16 * (w & 1),
                         BSplit<1, LY::B2S>{reinterpret_cast<const float2*>(sm + LY::STB)}, 8 * nt);
         wgemm<1, TT / 8>(c, ASplit<LY::MS>{reinterpret_cast<const float2*>(sm + LY::MM2)},
                          16 * (w & 1), BSplit<LY::P2S, 1>{K2}, 8 * nt);
@@ -442,14 +477,10 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_q(const Params prm) {
       }
     }
     __syncthreads();
-    if (threadIdx.x < prm.S) {
-      float a = 0.f;
-      for (int t = 0; t < TT; ++t) a += sm[LY::AUX + t * LY::ACS + threadIdx.x];
-      ga += a;
-    }
+    column_sums<LY>(sm + LY::AUX, sm + LY::VEC, prm.S);   // range total of alpha
     hash_backward<LY, K, false>(sm, sh, inv_scale, nullptr, ds);
     if (glive)   // range total of W^T dO
-      wgemm<PER, TT / 8>(gb, ASplit<LY::PT2S>{WT2}, gm0, BView<LY::RS, 1>{G}, gn0);
+      wgemm<PER, TT / 8>(gb, ASplit<LY::PT2S>{WT2}, gm0, BView<LY::RS, 1, sizeof(T) == 2>{G}, gn0);
     __syncthreads();
     {
       float c[D / 32][4];
@@ -457,7 +488,7 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_q(const Params prm) {
       readout_tc<LY, true>(sm, c, m0, n0);
       store_c_global<T, D / 32>(c, dqb, prm.ldq.st, tile0, tr.t1, m0, n0);
     }
-    state_add<LY>(sm, KT2, V);
+    state_add<LY, sizeof(T) == 2>(sm, KT2, V);
     __syncthreads();
     refresh_state_table<LY>(sm);
     __syncthreads();
@@ -479,7 +510,8 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_q(const Params prm) {
         }
       }
   }
-  if (threadIdx.x < prm.S) dst[prm.S * D + threadIdx.x] = ga;
+  __syncthreads();
+  if (threadIdx.x < prm.S) dst[prm.S * D + threadIdx.x] = sm[LY::VEC + threadIdx.x];
   const float tot = cta_sum_nw(ds, sm + LY::MISC);
   if (threadIdx.x == 0) prm.dscale_part[slot] = tot;
 }
@@ -524,21 +556,13 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_kv(const Params prm) {
           threadIdx.x < prm.S
               ? tileA[((size_t)n * ntile_stream + tile0 / TT) * LY::S8 + threadIdx.x]
               : 0.0;
-    projections<LY>(Kx, sm);
+    projections<LY, sizeof(T) == 2>(Kx, sm);
     __syncthreads();
     // key probabilities into P2 (gradient side) and K2 (for key_mass); tanh into H
     probs_to<LY, K>(sm, sh, inv_scale, valid, P2, nullptr, sm + LY::H);
     __syncthreads();
-    {
-      float2* K2 = reinterpret_cast<float2*>(sm + LY::K2);
-      for (int i = threadIdx.x; i < TT * LY::S8; i += NT) {
-        const int t = i / LY::S8, s = i % LY::S8;
-        K2[t * LY::P2S + s] = P2[t * LY::P2S + s];
-      }
-    }
-    __syncthreads();
-    key_mass<LY>(sm, prm.S);
-    projections<LY>(Q, sm);
+    key_mass<LY>(sm, P2, prm.S);
+    projections<LY, sizeof(T) == 2>(Q, sm);
     __syncthreads();
     probs_to<LY, K>(sm, sh, inv_scale, valid, reinterpret_cast<float2*>(sm + LY::Q2), nullptr,
                     nullptr);
@@ -552,19 +576,17 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_kv(const Params prm) {
         W2[t * LY::P2S + s] = w;
         WT2[s * LY::PT2S + t] = w;
       }
-      if (threadIdx.x < prm.S) {
-        const int s = threadIdx.x;
-        float run = asuf[s];
-        for (int tt = TT - 1; tt >= 0; --tt) {
-          const int64_t tok = tile0 + tt;
-          if (tok < tr.t1) run += alpha[tok * prm.S + s];
-          sm[LY::AUX + tt * LY::ACS + s] = run;
-        }
+      // alpha of the tile (contiguous [t][s]) into AUX
+      for (int i = threadIdx.x; i < TT * prm.S; i += NT) {
+        const int t = i / prm.S, ss = i - t * prm.S;
+        sm[LY::AUX + t * LY::ACS + ss] = tile0 + t < tr.t1 ? alpha[tile0 * prm.S + i] : 0.f;
       }
     }
     __syncthreads();
+    suffix_scan<LY>(sm + LY::AUX, asuf, prm.S);   // asuf(t), and asuf -> the previous tile's end
+    __syncthreads();
     // Mt(t, tau) = v_t . dO_tau, kept for tau >= t
-    masked_32x32<LY, false, D / 8>(sm, AView<LY::RS, 1>{V}, BView<1, LY::RS>{G});
+    masked_32x32<LY, false, D / 8>(sm, AView<LY::RS, 1, sizeof(T) == 2>{V}, BView<1, LY::RS, sizeof(T) == 2>{G});
     __syncthreads();
     {   // dpK = asuf + V . beta^T + Mt . W  -> DP
       const int w = threadIdx.x >> 5;
@@ -572,7 +594,7 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_kv(const Params prm) {
       if (nt < LY::S8 / 8) {
         float c[1][4];
         zero(c);
-        wgemm<1, D / 8>(c, AView<LY::RS, 1>{V}, 16 * (w & 1),
+        wgemm<1, D / 8>(c, AView<LY::RS, 1, sizeof(T) == 2>{V}, 16 * (w & 1),
                         BSplit<1, LY::B2S>{reinterpret_cast<const float2*>(sm + LY::STB)}, 8 * nt);
         wgemm<1, TT / 8>(c, ASplit<LY::MS>{reinterpret_cast<const float2*>(sm + LY::MM2)},
                          16 * (w & 1), BSplit<LY::P2S, 1>{W2}, 8 * nt);
@@ -606,13 +628,12 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_kv(const Params prm) {
       wgemm<D / 32, LY::S8 / 8>(c, ASplit<LY::P2S>{P2}, m0,
                                 BSplit<LY::B2S, 1>{reinterpret_cast<const float2*>(sm + LY::STB)}, n0);
       wgemm<D / 32, TT / 8>(c, ASplit<LY::MS>{reinterpret_cast<const float2*>(sm + LY::MM2)}, m0,
-                            BView<LY::RS, 1>{G}, n0);
+                            BView<LY::RS, 1, sizeof(T) == 2>{G}, n0);
       store_c_global<T, D / 32>(c, dvb, prm.ldv.st, tile0, tr.t1, m0, n0);
     }
     __syncthreads();
     // carry the suffix states to the previous tile: beta += W^T dO, asuf = AUX[0]
-    state_add<LY>(sm, WT2, G);
-    if (threadIdx.x < prm.S) asuf[threadIdx.x] = sm[LY::AUX + threadIdx.x];
+    state_add<LY, sizeof(T) == 2>(sm, WT2, G);
     __syncthreads();
     refresh_state_table<LY>(sm);
     __syncthreads();

@@ -9,7 +9,6 @@ enum KernelId {
   K_NC_READOUT,
   K_NC_BWD_Q,
   K_NC_BWD_KV,
-  K_C_TOTALS,
   K_C_FWD,
   K_C_BWD_Q,
   K_C_BWD_KV,

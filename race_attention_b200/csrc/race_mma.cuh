@@ -1,8 +1,8 @@
 // race_mma.cuh -- non-causal RACE kernels with tensor-core tile contractions.
 //
 // A CTA of 256 threads (8 warps; two CTAs per SM) walks a contiguous range of
-// 32-token tiles of one stream; cp.async double-buffers the next tile's rows (race_tiles.cuh
-// TilePipe).  Every dense contraction of a tile runs on the tensor cores as
+// 32-token tiles of one stream; cp.async double-buffers the next tile's rows
+// (race_tiles.cuh TilePipe).  Every dense contraction of a tile runs on the tensor cores as
 // warp-level mma.sync.m16n8k8 TF32 products in "3xTF32" form: each fp32
 // operand x is split into a TF32 high part and the TF32 truncation of x - hi,
 // and lo*hi + hi*lo + hi*hi is accumulated in fp32 (relative error ~2^-19 per
@@ -95,35 +95,47 @@ __device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], 
 }
 
 // A operand: fp32 matrix in shared memory, element (r, c) at p[r*RS + c*CS].
-template <int RS, int CS>
+// EXACT: every value is a bf16 widened to fp32 (exact in TF32, lo = 0).
+template <int RS, int CS, bool EXACT = false>
 struct AView {
   const float* p;
+  static constexpr bool kExact = EXACT;
 };
 // A operand from a pre-split float2 {hi, lo} matrix, (r, c) at p2[r*RS + c].
 template <int RS>
 struct ASplit {
   const float2* p2;
+  static constexpr bool kExact = false;
 };
 // B operand from an fp32 matrix (split on the fly), (k, n) at p[k*KS + n*NS].
-template <int KS, int NS>
+template <int KS, int NS, bool EXACT = false>
 struct BView {
   const float* p;
+  static constexpr bool kExact = EXACT;
 };
 // B operand from a pre-split float2 {hi, lo} matrix, (k, n) at p2[k*KS + n*NS].
 template <int KS, int NS>
 struct BSplit {
   const float2* p2;
+  static constexpr bool kExact = false;
 };
 
-template <int RS, int CS>
-__device__ __forceinline__ void load_a(const AView<RS, CS>& A, int m0, int k0, uint32_t (&ah)[4],
+template <int RS, int CS, bool EX>
+__device__ __forceinline__ void load_a(const AView<RS, CS, EX>& A, int m0, int k0, uint32_t (&ah)[4],
                                        uint32_t (&al)[4]) {
   const int lane = threadIdx.x & 31;
   const float* b = A.p + (m0 + (lane >> 2)) * RS + (k0 + (lane & 3)) * CS;
-  split_tf32(b[0], ah[0], al[0]);
-  split_tf32(b[8 * RS], ah[1], al[1]);
-  split_tf32(b[4 * CS], ah[2], al[2]);
-  split_tf32(b[8 * RS + 4 * CS], ah[3], al[3]);
+  if constexpr (EX) {
+    ah[0] = __float_as_uint(b[0]);
+    ah[1] = __float_as_uint(b[8 * RS]);
+    ah[2] = __float_as_uint(b[4 * CS]);
+    ah[3] = __float_as_uint(b[8 * RS + 4 * CS]);
+  } else {
+    split_tf32(b[0], ah[0], al[0]);
+    split_tf32(b[8 * RS], ah[1], al[1]);
+    split_tf32(b[4 * CS], ah[2], al[2]);
+    split_tf32(b[8 * RS + 4 * CS], ah[3], al[3]);
+  }
 }
 
 template <int RS>
@@ -144,13 +156,18 @@ __device__ __forceinline__ float2 split2(float x) {
   return make_float2(__uint_as_float(h), __uint_as_float(l));
 }
 
-template <int KS, int NS>
-__device__ __forceinline__ void load_b(const BView<KS, NS>& B, int k0, int n, uint32_t& h0,
+template <int KS, int NS, bool EX>
+__device__ __forceinline__ void load_b(const BView<KS, NS, EX>& B, int k0, int n, uint32_t& h0,
                                        uint32_t& l0, uint32_t& h1, uint32_t& l1) {
   const int lane = threadIdx.x & 31;
   const float* b = B.p + (k0 + (lane & 3)) * KS + (n + (lane >> 2)) * NS;
-  split_tf32(b[0], h0, l0);
-  split_tf32(b[4 * KS], h1, l1);
+  if constexpr (EX) {
+    h0 = __float_as_uint(b[0]);
+    h1 = __float_as_uint(b[4 * KS]);
+  } else {
+    split_tf32(b[0], h0, l0);
+    split_tf32(b[4 * KS], h1, l1);
+  }
 }
 
 template <int KS, int NS>
@@ -178,8 +195,8 @@ __device__ __forceinline__ void wgemm(float (&c)[NTL][4], const VA& A, int m0, c
       if (i < ntl) {
         uint32_t h0, l0, h1, l1;
         load_b(B, ks * 8, n0 + 8 * i, h0, l0, h1, l1);
-        mma_tf32(c[i], al, h0, h1);
-        mma_tf32(c[i], ah, l0, l1);
+        if constexpr (!VA::kExact) mma_tf32(c[i], al, h0, h1);
+        if constexpr (!VB::kExact) mma_tf32(c[i], ah, l0, l1);
         mma_tf32(c[i], ah, h0, h1);
       }
     }
@@ -233,7 +250,7 @@ __device__ __forceinline__ void store_c_global(const float (&c)[NTL][4], T* base
 
 // ------------------------------------------------------------------ tile ops
 // PROJ = X . PL^T: warps 0..3 compute token rows 16(w&1).. and planes 8(w>>1)..
-template <class LY>
+template <class LY, bool EX = false>
 __device__ __forceinline__ void projections(const float* X, float* sm) {
   constexpr int D = LY::Dv;
   const int w = threadIdx.x >> 5;
@@ -241,7 +258,7 @@ __device__ __forceinline__ void projections(const float* X, float* sm) {
     float c[1][4];
     zero(c);
     const float2* plb = reinterpret_cast<const float2*>(sm + LY::PLB);
-    wgemm<1, D / 8>(c, AView<LY::RS, 1>{X}, 16 * (w & 1), BSplit<1, LY::B2S>{plb}, 8 * (w >> 1));
+    wgemm<1, D / 8>(c, AView<LY::RS, 1, EX>{X}, 16 * (w & 1), BSplit<1, LY::B2S>{plb}, 8 * (w >> 1));
     store_c_smem<1>(c, sm + LY::PROJ, LY::JS, 16 * (w & 1), 8 * (w >> 1));
   }
 }
@@ -344,7 +361,7 @@ __device__ __forceinline__ void readout_tc(const float* sm, float (&c)[LY::Dv / 
 }
 
 // DP[32][S8] = Y . TAB^T: warp w -> rows 16(w&1), bucket n-tile w>>1.
-template <class LY>
+template <class LY, bool EX = false>
 __device__ __forceinline__ void rowdot_tc(const float* Y, float* sm) {
   constexpr int D = LY::Dv;
   const int w = threadIdx.x >> 5;
@@ -353,7 +370,7 @@ __device__ __forceinline__ void rowdot_tc(const float* Y, float* sm) {
     float c[1][4];
     zero(c);
     const float2* b = reinterpret_cast<const float2*>(sm + LY::TABB);
-    wgemm<1, D / 8>(c, AView<LY::RS, 1>{Y}, 16 * (w & 1), BSplit<1, LY::B2S>{b}, 8 * nt);
+    wgemm<1, D / 8>(c, AView<LY::RS, 1, EX>{Y}, 16 * (w & 1), BSplit<1, LY::B2S>{b}, 8 * nt);
     store_c_smem<1>(c, sm + LY::DP, LY::PS, 16 * (w & 1), 8 * nt);
   }
 }
@@ -377,10 +394,11 @@ struct AggTC {
     m0 = 16 * (first / NTILES);
     n0 = 8 * (first % NTILES);
   }
+  template <bool EX = false>
   __device__ __forceinline__ void add_tile(const float* sm, const float* Y) {
     if (live)
       wgemm<PER, TT / 8>(c, ASplit<LY::PT2S>{reinterpret_cast<const float2*>(sm + LY::PT2)}, m0,
-                         BView<LY::RS, 1>{Y}, n0);
+                         BView<LY::RS, 1, EX>{Y}, n0);
   }
   __device__ __forceinline__ void write(float* dst, int S) const {
     if (!live) return;
@@ -484,11 +502,11 @@ __global__ void __launch_bounds__(NT, 2) k_tc_reduce(const Params prm) {
   agg.init();
   float amass = 0.f;   // thread (s = tid/4, quarter pp = tid%4) of the first SPAD*4
   RACE_TC_LOOP(true, kb, prm.lk.st, vb, prm.lv.st)
-    projections<LY>(X, sm);
+    projections<LY, sizeof(T) == 2>(X, sm);
     __syncthreads();
     probabilities<LY, K>(sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
-    agg.add_tile(sm, Y);
+    agg.template add_tile<sizeof(T) == 2>(sm, Y);
     if (threadIdx.x < SPAD * 4) {
       const int s = threadIdx.x >> 2, pp = threadIdx.x & 3;
       const float2* row = reinterpret_cast<const float2*>(sm + LY::PT2) + s * LY::PT2S + pp * 8;
@@ -517,7 +535,7 @@ __global__ void __launch_bounds__(NT, 2) k_tc_readout(const Params prm) {
   __syncthreads();
   RACE_TC_LOOP(false, qb, prm.lq.st, qb, prm.lq.st)
     (void)Y;
-    projections<LY>(X, sm);
+    projections<LY, sizeof(T) == 2>(X, sm);
     __syncthreads();
     probabilities<LY, K>(sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
@@ -542,12 +560,12 @@ __global__ void __launch_bounds__(NT, 2) k_tc_bwd_q(const Params prm) {
   agg.init();
   float ds = 0.f;
   RACE_TC_LOOP(true, qb, prm.lq.st, gb, prm.ldo.st)
-    projections<LY>(X, sm);
+    projections<LY, sizeof(T) == 2>(X, sm);
     __syncthreads();
     probabilities<LY, K>(sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
-    agg.add_tile(sm, Y);
-    rowdot_tc<LY>(Y, sm);
+    agg.template add_tile<sizeof(T) == 2>(sm, Y);
+    rowdot_tc<LY, sizeof(T) == 2>(Y, sm);
     __syncthreads();
     hash_backward<LY, K, false>(sm, sh, inv_scale, nullptr, ds);
     __syncthreads();
@@ -590,30 +608,25 @@ __global__ void __launch_bounds__(NT, 2) k_tc_bwd_kv(const Params prm) {
   T* dvb = static_cast<T*>(prm.dv) + stream_offset(prm.ldv, n, prm.B, prm.H);
   __syncthreads();
   float ds = 0.f;
-#ifndef RACE_ABLATE
-#define RACE_ABLATE 0
-#endif
   RACE_TC_LOOP(true, kb, prm.lk.st, vb, prm.lv.st)
-    if (!(RACE_ABLATE & 1)) projections<LY>(X, sm);
+    projections<LY, sizeof(T) == 2>(X, sm);
     __syncthreads();
-    if (!(RACE_ABLATE & 2)) probabilities<LY, K>(sm, sh, inv_scale, tr.t1 - tile0);
+    probabilities<LY, K>(sm, sh, inv_scale, tr.t1 - tile0);
     __syncthreads();
-    if (!(RACE_ABLATE & 4)) {
+    {
       float c[D / 32][4];
       int m0, n0;
       readout_tc<LY, false>(sm, c, m0, n0);
       store_c_global<T, D / 32>(c, dvb, prm.ldv.st, tile0, tr.t1, m0, n0);
     }
-    if (!(RACE_ABLATE & 8)) rowdot_tc<LY>(Y, sm);
+    rowdot_tc<LY, sizeof(T) == 2>(Y, sm);
     __syncthreads();
-    if (!(RACE_ABLATE & 16)) hash_backward<LY, K, true>(sm, sh, inv_scale, dA, ds);
+    hash_backward<LY, K, true>(sm, sh, inv_scale, dA, ds);
     __syncthreads();
-    if (!(RACE_ABLATE & 32)) {
     float c[D / 32][4];
     int m0, n0;
     readout_tc<LY, true>(sm, c, m0, n0);
     store_c_global<T, D / 32>(c, dkb, prm.ldk.st, tile0, tr.t1, m0, n0);
-    }
   RACE_TC_LOOP_END
   const float tot = cta_sum_nw(ds, sm + LY::MISC + 32);
   if (threadIdx.x == 0) prm.dscale_part[(size_t)n * prm.P + part] = tot;
