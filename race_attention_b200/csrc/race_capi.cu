@@ -189,9 +189,10 @@ int make_plan(const race_desc_t* d, Plan* p) {
   p->SS = round_up(S * D + S, 4);
   const int sms = sm_count();
   const int64_t T = d->tokens;
-  // contiguous token ranges, one CTA each: one resident wave of two CTAs per
-  // SM, every range at least a few 32-token tiles long
-  const int64_t target = (int64_t)sms * 2;
+  // contiguous token ranges, one CTA each, every range at least a few 32-token
+  // tiles long.  Non-causal kernels hold 2 (query backward) or 3 CTAs per SM:
+  // 6 ranges per SM fill both evenly.  The causal walks hold one CTA per SM.
+  const int64_t target = (int64_t)sms * (d->causal ? 2 : 6);
   int64_t P = (target + p->N - 1) / p->N;
   const int64_t by_len = (T + 127) / 128;
   if (P > by_len) P = by_len;

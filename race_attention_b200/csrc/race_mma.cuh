@@ -39,8 +39,16 @@ constexpr int NW = NT / 32;
 
 __host__ __device__ constexpr int odd4(int n) { return ((n / 4) % 2 == 1) ? n : n + 4; }
 
-template <int D, int SPAD, bool BF = false>
+// Kernel kinds and the shared-memory buffers each one touches.
+enum Kind { kReduce = 0, kReadout = 1, kBwdQ = 2, kBwdKV = 3 };
+
+template <int D, int SPAD, bool BF = false, int KIND = kBwdQ>
 struct Lay {
+  static constexpr bool kTwo = KIND != kReadout;        // X and Y staged
+  static constexpr bool kP = KIND != kReduce;           // P2  (readout / hash backward)
+  static constexpr bool kPT = KIND == kReduce || KIND == kBwdQ;   // PT2 (aggregation)
+  static constexpr bool kTab = KIND != kReduce;         // E / dB table
+  static constexpr bool kBwd = KIND >= kBwdQ;           // H, DJ2
   static constexpr int NSTAGE = BF ? 1 : 2;
   static constexpr int S8 = round_up(SPAD, 8);          // bucket extent as a k / n dim
   static constexpr int SM16 = round_up(S8, 16);         // bucket extent as an m dim
@@ -55,24 +63,26 @@ struct Lay {
   static constexpr int B2S = D + 4;                     // split table / plane rows (float2)
   static constexpr int XS = 0;
   static constexpr int YS = XS + NSTAGE * TT * RS;
-  static constexpr int PLB = YS + NSTAGE * TT * RS;     // float2 [LKP][B2S]
+  static constexpr int PLB = YS + (kTwo ? NSTAGE * TT * RS : 0);   // float2 [LKP][B2S]
   static constexpr int TABB = PLB + 2 * LKP * B2S;      // float2 [S8][B2S]
-  static constexpr int H = TABB + 2 * S8 * B2S;         // [TT][LKP+1]
-  static constexpr int P2 = H + TT * (LKP + 1) + ((TT * (LKP + 1)) & 1);  // float2 [TT][P2S]
-  static constexpr int PT2 = P2 + 2 * TT * P2S;         // float2 [SM16][PT2S]
-  static constexpr int DJ2 = PT2 + 2 * SM16 * PT2S;     // float2 [TT][DJ2S]
-  static constexpr int DP = DJ2 + 2 * TT * DJ2S;        // [TT][PS]; PROJ aliases it
+  static constexpr int H = TABB + (kTab ? 2 * S8 * B2S : 0);        // [TT][LKP+1]
+  static constexpr int HN = kBwd ? TT * (LKP + 1) + ((TT * (LKP + 1)) & 1) : 0;
+  static constexpr int P2 = H + HN;                     // float2 [TT][P2S]
+  static constexpr int PT2 = P2 + (kP ? 2 * TT * P2S : 0);          // float2 [SM16][PT2S]
+  static constexpr int DJ2 = PT2 + (kPT ? 2 * SM16 * PT2S : 0);     // float2 [TT][DJ2S]
+  static constexpr int DP = DJ2 + (kBwd ? 2 * TT * DJ2S : 0);       // [TT][PS]; PROJ aliases it
   static constexpr int PROJ = DP;                       // [TT][JS]
-  static constexpr int MISC = DP + (PS > JS ? TT * PS : TT * JS);  // 64 floats, then 2 mbarriers
-  static constexpr int BAR = MISC + 64;                 // 2 x uint64 mbarriers
-  static constexpr int RAW = BAR + 4;
+  static constexpr int MISC = DP + (kBwd && PS > JS ? TT * PS : TT * JS);  // 64 floats
+  static constexpr int RAW = MISC + 64;
+  // TilePipe addresses raw bf16 rows as [stage][X, Y]: keep both slots
   static constexpr int RAW_FLOATS = BF ? 2 * 2 * TT * D / 2 : 0;
   static constexpr int FLOATS = RAW + RAW_FLOATS;
   static constexpr int Dv = D;
   static constexpr int Sv = SPAD;
   static_assert(S8 <= 32, "bucket count above 32");
-  static_assert(BAR % 2 == 0 && RAW % 4 == 0 && (XS + YS) % 4 == 0, "alignment");
-  static_assert(PLB % 2 == 0 && TABB % 2 == 0 && P2 % 2 == 0, "float2 alignment");
+  static_assert(RAW % 4 == 0 && YS % 4 == 0, "alignment");
+  static_assert(PLB % 2 == 0 && TABB % 2 == 0 && P2 % 2 == 0 && PT2 % 2 == 0 && DJ2 % 2 == 0,
+                "float2 alignment");
 };
 
 // ------------------------------------------------------------------ MMA
@@ -280,7 +290,7 @@ __device__ __forceinline__ void probabilities(float* sm, const Shape& sh, float 
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       const float h = tiles::tanh_exp(proj[l * K + k]);
-      Hrow[l * K + k] = h;
+      if constexpr (LY::kBwd) Hrow[l * K + k] = h;
       const float u = h * inv_scale;
       const float ex = __expf(-2.f * fabsf(u));
       const float r = __frcp_rn(1.f + ex);
@@ -294,8 +304,8 @@ __device__ __forceinline__ void probabilities(float* sm, const Shape& sh, float 
       for (int k = 0; k < K; ++k) p *= ((r >> (K - 1 - k)) & 1) ? sp[k] : sn[k];
       const int s = l * R + r;
       const float2 p2 = split2(p);
-      Prow[s] = p2;
-      PT[s * LY::PT2S + t] = p2;
+      if constexpr (LY::kP) Prow[s] = p2;
+      if constexpr (LY::kPT) PT[s * LY::PT2S + t] = p2;
     }
   }
 }
@@ -450,10 +460,14 @@ template <class LY>
 __device__ __forceinline__ void clear_buckets(float* sm) {
   // bucket padding (s >= S) of P2 / PT2 and DJ2 columns >= L*K are read as
   // zeros by the 8-wide k steps; DP padding is never read
-  for (int i = threadIdx.x; i < 2 * LY::SM16 * LY::PT2S; i += NT) sm[LY::PT2 + i] = 0.f;
-  for (int i = threadIdx.x; i < 2 * TT * LY::P2S; i += NT) sm[LY::P2 + i] = 0.f;
-  for (int i = threadIdx.x; i < 2 * TT * LY::DJ2S; i += NT) sm[LY::DJ2 + i] = 0.f;
-  for (int i = threadIdx.x; i < TT * LY::PS; i += NT) sm[LY::DP + i] = 0.f;
+  if constexpr (LY::kPT)
+    for (int i = threadIdx.x; i < 2 * LY::SM16 * LY::PT2S; i += NT) sm[LY::PT2 + i] = 0.f;
+  if constexpr (LY::kP)
+    for (int i = threadIdx.x; i < 2 * TT * LY::P2S; i += NT) sm[LY::P2 + i] = 0.f;
+  if constexpr (LY::kBwd) {
+    for (int i = threadIdx.x; i < 2 * TT * LY::DJ2S; i += NT) sm[LY::DJ2 + i] = 0.f;
+    for (int i = threadIdx.x; i < TT * LY::PS; i += NT) sm[LY::DP + i] = 0.f;
+  }
 }
 
 __device__ __forceinline__ float cta_sum_nw(float x, float* red) {
@@ -468,8 +482,8 @@ __device__ __forceinline__ float cta_sum_nw(float x, float* red) {
   return t;
 }
 
-#define RACE_TC_PROLOGUE                                                          \
-  using LY = Lay<D, SPAD, sizeof(T) == 2>;                                        \
+#define RACE_TC_PROLOGUE(KIND)                                                    \
+  using LY = Lay<D, SPAD, sizeof(T) == 2, KIND>;                                  \
   extern __shared__ __align__(16) float sm[];                                     \
   const Shape sh(prm);                                                            \
   const float inv_scale = 1.f / __ldg(prm.scale);                                 \
@@ -493,8 +507,8 @@ __device__ __forceinline__ float cta_sum_nw(float x, float* red) {
 
 // F1: per-CTA partial [V|1] bucket sums of the key side.
 template <typename T, int D, int SPAD, int K>
-__global__ void __launch_bounds__(NT, 2) k_tc_reduce(const Params prm) {
-  RACE_TC_PROLOGUE
+__global__ void __launch_bounds__(NT, 3) k_tc_reduce(const Params prm) {
+  RACE_TC_PROLOGUE(kReduce)
   const T* kb = static_cast<const T*>(prm.k) + stream_offset(prm.lk, n, prm.B, prm.H);
   const T* vb = static_cast<const T*>(prm.v) + stream_offset(prm.lv, n, prm.B, prm.H);
   __syncthreads();
@@ -526,8 +540,8 @@ __global__ void __launch_bounds__(NT, 2) k_tc_reduce(const Params prm) {
 
 // F2: out = sum_s pQ_s E_s.
 template <typename T, int D, int SPAD, int K>
-__global__ void __launch_bounds__(NT, 2) k_tc_readout(const Params prm) {
-  RACE_TC_PROLOGUE
+__global__ void __launch_bounds__(NT, 3) k_tc_readout(const Params prm) {
+  RACE_TC_PROLOGUE(kReadout)
   const float* st = prm.state + (size_t)n * prm.SS;
   load_table<LY>(sm, st, st + prm.S * D, prm.S, prm.eps);
   const T* qb = static_cast<const T*>(prm.q) + stream_offset(prm.lq, n, prm.B, prm.H);
@@ -549,7 +563,7 @@ __global__ void __launch_bounds__(NT, 2) k_tc_readout(const Params prm) {
 // B1: dq, the per-CTA partial dE = sum_t pQ dO^T and the q-side dscale.
 template <typename T, int D, int SPAD, int K>
 __global__ void __launch_bounds__(NT, 2) k_tc_bwd_q(const Params prm) {
-  RACE_TC_PROLOGUE
+  RACE_TC_PROLOGUE(kBwdQ)
   const float* st = prm.state + (size_t)n * prm.SS;
   load_table<LY>(sm, st, st + prm.S * D, prm.S, prm.eps);
   const T* qb = static_cast<const T*>(prm.q) + stream_offset(prm.lq, n, prm.B, prm.H);
@@ -582,8 +596,8 @@ __global__ void __launch_bounds__(NT, 2) k_tc_bwd_q(const Params prm) {
 
 // B2: dv = pK . dB, dpK = v . dB^T + dA, then dk; the k-side dscale.
 template <typename T, int D, int SPAD, int K>
-__global__ void __launch_bounds__(NT, 2) k_tc_bwd_kv(const Params prm) {
-  RACE_TC_PROLOGUE
+__global__ void __launch_bounds__(NT, 3) k_tc_bwd_kv(const Params prm) {
+  RACE_TC_PROLOGUE(kBwdKV)
   const float* st = prm.state + (size_t)n * prm.SS;
   const float* gs = prm.gstate_in + (size_t)n * prm.SS;
   load_table<LY>(sm, gs, st + prm.S * D, prm.S, prm.eps);   // dB = dE / (A + eps)
