@@ -44,7 +44,7 @@ def soft_hash(x, planes, K, L, scale):
     x = np.asarray(x, np.float64)
     planes = np.asarray(planes, np.float64)
     N, T, D = x.shape
-    proj = np.einsum("ntd,njd->ntj", x, planes)          # misc/vit.py:943-944
+    proj = np.einsum("ntd,njd->ntj", x, planes, optimize=True)  # misc/vit.py:943-944
     h = np.tanh(proj).reshape(N, T, L, K)
     logits = (h / scale) @ corners(K).T                   # misc/vit.py:955-956
     logits = logits - logits.max(-1, keepdims=True)
@@ -68,7 +68,7 @@ def soft_hash_backward(dp, p, h, planes, K, L, scale):
     dh = du / scale
     dscale = float(-(du * h).sum() / scale / scale)
     dproj = (dh * (1.0 - h * h)).reshape(N, T, L * K)
-    dx = np.einsum("ntj,njd->ntd", dproj, np.asarray(planes, np.float64))
+    dx = np.einsum("ntj,njd->ntd", dproj, np.asarray(planes, np.float64), optimize=True)
     return dx, dscale
 
 
@@ -78,10 +78,10 @@ def noncausal_forward(q, k, v, planes, K, L, scale, eps=1e-6):
     pK, _ = soft_hash(k, planes, K, L, scale)
     pQ, _ = soft_hash(q, planes, K, L, scale)
     v = np.asarray(v, np.float64)
-    Bsum = np.einsum("nts,ntd->nsd", pK, v)               # misc/vit.py:967
+    Bsum = np.einsum("nts,ntd->nsd", pK, v, optimize=True)  # misc/vit.py:967
     A = pK.sum(1)                                         # misc/vit.py:969
     E = Bsum / (A[..., None] + eps)                       # misc/vit.py:972
-    out = np.einsum("nts,nsd->ntd", pQ, E)                # misc/vit.py:975
+    out = np.einsum("nts,nsd->ntd", pQ, E, optimize=True)  # misc/vit.py:975
     return out, A, Bsum
 
 
@@ -91,16 +91,16 @@ def noncausal_backward(q, k, v, planes, K, L, scale, dout, eps=1e-6):
     pQ, hQ = soft_hash(q, planes, K, L, scale)
     v = np.asarray(v, np.float64)
     dout = np.asarray(dout, np.float64)
-    Bsum = np.einsum("nts,ntd->nsd", pK, v)
+    Bsum = np.einsum("nts,ntd->nsd", pK, v, optimize=True)
     A = pK.sum(1)
     inv = 1.0 / (A + eps)
     E = Bsum * inv[..., None]
-    dpQ = np.einsum("ntd,nsd->nts", dout, E)
-    dE = np.einsum("nts,ntd->nsd", pQ, dout)
+    dpQ = np.einsum("ntd,nsd->nts", dout, E, optimize=True)
+    dE = np.einsum("nts,ntd->nsd", pQ, dout, optimize=True)
     dB = dE * inv[..., None]
     dA = -(dB * E).sum(-1)
-    dv = np.einsum("nts,nsd->ntd", pK, dB)
-    dpK = np.einsum("ntd,nsd->nts", v, dB) + dA[:, None, :]
+    dv = np.einsum("nts,nsd->ntd", pK, dB, optimize=True)
+    dpK = np.einsum("ntd,nsd->nts", v, dB, optimize=True) + dA[:, None, :]
     dq, dsq = soft_hash_backward(dpQ, pQ, hQ, planes, K, L, scale)
     dk, dsk = soft_hash_backward(dpK, pK, hK, planes, K, L, scale)
     return dq, dk, dv, dsq + dsk
@@ -146,7 +146,7 @@ def causal_forward(q, k, v, planes, K, L, scale, eps=1e-6):
     v = np.asarray(v, np.float64)
     A, B = _causal_states(pK, v, eps)
     E = B / (A[..., None] + eps)                                  # misc/race.py:110
-    return np.einsum("nts,ntsd->ntd", pQ, E)                      # misc/race.py:135-138
+    return np.einsum("nts,ntsd->ntd", pQ, E, optimize=True)  # misc/race.py:135-138
 
 
 def causal_backward(q, k, v, planes, K, L, scale, dout, eps=1e-6):
@@ -159,7 +159,7 @@ def causal_backward(q, k, v, planes, K, L, scale, dout, eps=1e-6):
     D = v.shape[-1]
     A, B = _causal_states(pK, v, eps)
     E = B / (A[..., None] + eps)
-    dpQ = np.einsum("ntd,ntsd->nts", dout, E)
+    dpQ = np.einsum("ntd,ntsd->nts", dout, E, optimize=True)
     # per-bucket streams, flat layout [N*S, T(, D)] as race_pref.cpp expects
     w_flat = pK.transpose(0, 2, 1).reshape(N * S, T)
     V_flat = np.broadcast_to(v[:, None], (N, S, T, D)).reshape(N * S, T, D)
@@ -170,6 +170,78 @@ def causal_backward(q, k, v, planes, K, L, scale, dout, eps=1e-6):
     dq, dsq = soft_hash_backward(dpQ, pQ, hQ, planes, K, L, scale)
     dk, dsk = soft_hash_backward(dpK, pK, hK, planes, K, L, scale)
     return dq, dk, dv, dsq + dsk
+
+
+# ------------------------------------------------------- causal, streamed in chunks
+def causal_streamed(q, k, v, planes, K, L, scale, dout=None, eps=1e-6, chunk=2048, threads=None):
+    """``causal_forward`` / ``causal_backward`` in bounded memory, for long sequences.
+
+    Same float64 quantities as the dense restatement above (misc/race.py:108-138
+    forward, kernels/cpu/race_pref.cpp:104-220 backward), but the [T, S, D]
+    prefix states are never materialised.  The token axis is cut into chunks;
+    each chunk's entering state is an exclusive scan of the chunk totals
+    (sum pK, pK^T v), after which the chunks are independent and run on a
+    thread pool.  The backward uses the identities of race_pref.cpp with
+    W = pQ / (A + eps): alpha = -W * (dout . E) (race_pref.cpp:175-181) and
+    beta = W dout, whose suffix sums (race_pref.cpp:194-199) are carried across
+    chunks the same way in reverse.
+    Returns ``out`` when ``dout`` is None, else ``(out, dq, dk, dv, dscale)``.
+    """
+    from concurrent.futures import ThreadPoolExecutor
+    import os
+
+    pK, hK = soft_hash(k, planes, K, L, scale)
+    pQ, hQ = soft_hash(q, planes, K, L, scale)
+    v = np.asarray(v, np.float64)
+    N, T, S = pK.shape
+    D = v.shape[-1]
+    spans = [(c0, min(T, c0 + chunk)) for c0 in range(0, T, chunk)]
+    pool = ThreadPoolExecutor(threads or min(32, os.cpu_count() or 1))
+    out = np.empty((N, T, D))
+    bwd = dout is not None
+    if bwd:
+        dout = np.asarray(dout, np.float64)
+        dpQ = np.empty((N, T, S))
+    A = np.cumsum(pK, axis=1)                                           # [N,T,S]
+    inv = 1.0 / (A + eps)
+    for n in range(N):
+        tot = np.stack([pK[n, c0:c1].T @ v[n, c0:c1] for c0, c1 in spans])   # [C,S,D]
+        B0 = np.cumsum(tot, axis=0) - tot                                     # entering states
+
+        def fwd_chunk(ci, n=n, B0=B0):
+            c0, c1 = spans[ci]
+            b = B0[ci] + np.cumsum(pK[n, c0:c1, :, None] * v[n, c0:c1, None, :], axis=0)
+            E = b * inv[n, c0:c1, :, None]                                    # misc/race.py:110
+            out[n, c0:c1] = np.einsum("ts,tsd->td", pQ[n, c0:c1], E, optimize=True)
+            if bwd:
+                dpQ[n, c0:c1] = np.einsum("td,tsd->ts", dout[n, c0:c1], E, optimize=True)
+
+        list(pool.map(fwd_chunk, range(len(spans))))
+    if not bwd:
+        pool.shutdown()
+        return out
+    W = pQ * inv
+    alpha = -W * dpQ                                                    # race_pref.cpp:175-181
+    a_suf = np.cumsum(alpha[:, ::-1], axis=1)[:, ::-1]                  # race_pref.cpp:194-199
+    dpK = np.empty((N, T, S))
+    dv = np.empty((N, T, D))
+    for n in range(N):
+        tot = np.stack([W[n, c0:c1].T @ dout[n, c0:c1] for c0, c1 in spans])  # [C,S,D]
+        after = tot[::-1].cumsum(axis=0)[::-1] - tot                          # later chunks
+
+        def bwd_chunk(ci, n=n, after=after):
+            c0, c1 = spans[ci]
+            beta = W[n, c0:c1, :, None] * dout[n, c0:c1, None, :]
+            b_suf = np.cumsum(beta[::-1], axis=0)[::-1] + after[ci]
+            dpK[n, c0:c1] = a_suf[n, c0:c1] + np.einsum("tsd,td->ts", b_suf, v[n, c0:c1],
+                                                        optimize=True)      # race_pref.cpp:202-208
+            dv[n, c0:c1] = np.einsum("ts,tsd->td", pK[n, c0:c1], b_suf, optimize=True)  # :210-215
+
+        list(pool.map(bwd_chunk, range(len(spans))))
+    pool.shutdown()
+    dq, dsq = soft_hash_backward(dpQ, pQ, hQ, planes, K, L, scale)
+    dk, dsk = soft_hash_backward(dpK, pK, hK, planes, K, L, scale)
+    return out, dq, dk, dv, dsq + dsk
 
 
 def forward(q, k, v, planes, K, L, scale, causal, eps=1e-6):

@@ -87,3 +87,18 @@ def test_oracle_prefix_mean_matches_reference_cpp():
     ow, oV = O.prefix_mean_flat_backward(w.numpy(), V.numpy(), gE.numpy())
     assert O.rel_l2(gw.numpy(), ow) < 1e-6
     assert O.rel_l2(gV.numpy(), oV) < 1e-6
+
+
+def test_streamed_causal_matches_dense():
+    """The chunk-streamed causal oracle (used at full sequence length) equals the dense one."""
+    rng = np.random.default_rng(5)
+    N, T, D, K, L = 2, 301, 16, 2, 3
+    q, k, v, dout = (rng.standard_normal((N, T, D)) for _ in range(4))
+    P = rng.standard_normal((N, K * L, D))
+    ref = (O.causal_forward(q, k, v, P, K, L, 0.9),) + O.causal_backward(q, k, v, P, K, L, 0.9, dout)
+    for chunk in (1, 64, 1000):
+        got = O.causal_streamed(q, k, v, P, K, L, 0.9, dout, chunk=chunk)
+        for a, b in zip(got[:4], ref[:4]):
+            np.testing.assert_allclose(a, b, rtol=1e-9, atol=1e-12)
+        assert math.isclose(got[4], ref[4], rel_tol=1e-9)
+    np.testing.assert_allclose(O.causal_streamed(q, k, v, P, K, L, 0.9, chunk=50), ref[0], rtol=1e-9, atol=1e-12)
