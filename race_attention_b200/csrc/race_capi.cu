@@ -1,6 +1,7 @@
 // race_capi.cu -- the extern "C" boundary of librace_b200.so plus the small
 // fixed-order reduction / scan kernels that sit between the streaming passes.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -284,6 +285,14 @@ int check_tensor(const race_desc_t* d, const race_tensor_t& t) {
 }
 
 int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream) {
+  // RACE_MMA_SYNC=1 selects the warp-level mma.sync generation of the
+  // non-causal readout / key-value backward (for comparisons)
+  static const bool mma_sync = [] {
+    const char* e = std::getenv("RACE_MMA_SYNC");
+    return e != nullptr && e[0] == '1';
+  }();
+  if (mma_sync && id == K_NC_READOUT) id = K_NC_READOUT_SYNC;
+  if (mma_sync && id == K_NC_BWD_KV) id = K_NC_BWD_KV_SYNC;
   KernelInfo ki;
   const int K = d->num_bits, sp = c.plan.spad;
   bool ok;
@@ -292,7 +301,12 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
   else
     ok = d->head_dim == 32 ? kernels_bf16_d32(sp, K, id, &ki) : kernels_bf16_d64(sp, K, id, &ki);
   if (!ok) return RACE_ERR_UNSUPPORTED;
-  const dim3 grid(c.plan.P, c.plan.N, 1);
+  dim3 grid(c.plan.P, c.plan.N, 1);
+  if (ki.persist > 0) {
+    const int64_t items = (int64_t)c.plan.P * c.plan.N;
+    const int64_t ctas = (int64_t)sm_count() * ki.persist;
+    grid = dim3((unsigned)(items < ctas ? items : ctas), 1, 1);
+  }
   Params prm = c.prm;
   void* args[] = {&prm};
   if (ki.smem_bytes > 48 * 1024) {

@@ -12,6 +12,8 @@ enum KernelId {
   K_C_FWD,
   K_C_BWD_Q,
   K_C_BWD_KV,
+  K_NC_READOUT_SYNC,   // warp-level mma.sync generation (comparison)
+  K_NC_BWD_KV_SYNC,
   K_COUNT
 };
 
@@ -20,6 +22,7 @@ struct KernelInfo {
   int groups;       // token groups per CTA
   int smem_bytes;   // dynamic shared memory
   int threads;      // threads per CTA
+  int persist;      // >0: persistent grid of persist CTAs per SM over (stream, range) items
 };
 
 // Padded bucket counts the kernels are instantiated for.
