@@ -284,6 +284,52 @@ int check_tensor(const race_desc_t* d, const race_tensor_t& t) {
   return tensor_ok(t, d->dtype == RACE_F32 ? 4 : 2) ? RACE_OK : RACE_ERR_ALIGN;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+  static const EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Maps a [M, B, T, H, D] tensor as 5-D (D, T, H, B, M) with boxes of 128 rows
+// x min(row, 128 B) (128-byte swizzle when the box row is 128 B), matching
+// t5::Box.  Returns false when the layout cannot be mapped (a broadcast batch
+// or head axis); the caller then uses the mma.sync kernels.
+bool encode_map(CUtensorMap* m, const void* base, const Layout& l, int dtype, const Params& p,
+                int D) {
+  const EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const int64_t es = dtype == RACE_F32 ? 4 : 2;
+  const int64_t ext[5] = {D, p.T, p.H, p.B, l.sm == 0 ? 1 : p.M};
+  const int64_t str[4] = {l.st, l.sh, l.sb, l.sm};
+  cuuint64_t dims[5], strides[4];
+  for (int i = 0; i < 5; ++i) dims[i] = (cuuint64_t)ext[i];
+  for (int i = 0; i < 4; ++i) {
+    if (str[i] == 0 && ext[i + 1] > 1) return false;
+    strides[i] = str[i] == 0 ? 16 : (cuuint64_t)(str[i] * es);
+  }
+  if (p.T >= (int64_t(1) << 31)) return false;
+  const int ib = (int)(D * es < 128 ? D * es : 128);
+  const cuuint32_t box[5] = {(cuuint32_t)(ib / es), 128, 1, 1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = fn(m, es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        5, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        ib == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream) {
   // RACE_MMA_SYNC=1 selects the warp-level mma.sync generation of the
   // non-causal readout / key-value backward (for comparisons)
@@ -308,7 +354,21 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
     grid = dim3((unsigned)(items < ctas ? items : ctas), 1, 1);
   }
   Params prm = c.prm;
-  void* args[] = {&prm};
+  TmaMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if (ki.tma > 0) {
+    bool ok_map = false;
+    if (id == K_NC_READOUT)
+      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, d->head_dim);
+    else if (id == K_NC_BWD_KV)
+      ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, d->head_dim) &&
+               encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, d->head_dim);
+    if (!ok_map) {   // layouts the copy engine cannot walk: warp-level kernels
+      const KernelId alt = id == K_NC_READOUT ? K_NC_READOUT_SYNC : K_NC_BWD_KV_SYNC;
+      return launch(d, c, alt, stream);
+    }
+  }
+  void* args[] = {&prm, &maps};
   if (ki.smem_bytes > 48 * 1024) {
     const cudaError_t ea =
         cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem_bytes);

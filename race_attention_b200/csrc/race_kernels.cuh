@@ -15,6 +15,7 @@
 // in a fixed order, so every result is bitwise reproducible run to run.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -61,6 +62,13 @@ struct Params {
 };
 
 __host__ __device__ constexpr int round_up(int a, int b) { return (a + b - 1) / b * b; }
+
+// TMA descriptors of a kernel's streamed inputs (encoded per call on the host;
+// a __grid_constant__ kernel parameter).  Each maps a [M, B, T, H, D] tensor
+// as 5-D (D, T, H, B, M) with 128-row boxes.
+struct TmaMaps {
+  CUtensorMap map[2];
+};
 
 // ---------------------------------------------------------------- row I/O
 template <typename T, int C>

@@ -23,6 +23,7 @@ struct KernelInfo {
   int smem_bytes;   // dynamic shared memory
   int threads;      // threads per CTA
   int persist;      // >0: persistent grid of persist CTAs per SM over (stream, range) items
+  int tma;          // >0: the kernel takes a TmaMaps of its streamed inputs as a second argument
 };
 
 // Padded bucket counts the kernels are instantiated for.

@@ -1,13 +1,15 @@
 // race_t5.cuh -- non-causal readout and key/value backward on the 5th-generation
 // tensor cores (tcgen05 + tensor memory).
 //
-// One thread per token: a CTA of 128 threads walks 128-token tiles; every
+// NTH threads per token: a CTA of 128 NTH threads walks 128-token tiles; every
 // token-major product (projections x.P^T, readout pQ.E, key-side dpK = v.dB^T,
 // dv = pK.dB, dk = dproj.P) is an M = 128 tcgen05.mma chain issued by one
 // thread, both operands in shared memory, fp32 accumulators in tensor memory.
-// Row t of an accumulator is TMEM lane t, so after a tcgen05.ld every thread
-// holds its own token's row and the hash arithmetic (tanh, corner
-// probabilities and their backward) runs in registers.
+// Row t of an accumulator is TMEM lane t, so after a tcgen05.ld the threads
+// of token t hold its row and the hash arithmetic (tanh, corner
+// probabilities and their backward) runs in registers: thread (t, sub) owns
+// columns [sub W, sub W + W) of every row-wise pass (W = D / NTH) and every
+// NTH-th group of buckets of the hash.
 //
 // Precision: split bf16.  Every fp32 operand x is held as two bf16 parts,
 // hi = bf16(x) and lo = bf16(x - hi) (16 significant bits; the remainder is
@@ -39,8 +41,17 @@ namespace t5 {
 
 using bf16 = __nv_bfloat16;
 
+#ifndef RACE_T5_NTH_KV
+#define RACE_T5_NTH_KV 4
+#endif
+#ifndef RACE_T5_NTH_RO
+#define RACE_T5_NTH_RO 2
+#endif
+#ifndef RACE_T5_ABL
+#define RACE_T5_ABL 0
+#endif
+
 constexpr int TT = 128;   // tokens per tile = MMA M = TMEM lanes
-constexpr int NT = 128;   // threads per CTA, one per token
 constexpr int PJ = 16;    // projection columns (L*K <= 16)
 constexpr int kWaitPolls = 1 << 22;   // bounded mbarrier polls before giving up
 constexpr unsigned kErrTimeout = 1u;  // device error bit: an MMA wait timed out
@@ -153,25 +164,34 @@ __device__ __forceinline__ void tld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-// C columns of this lane as the sum of BP column blocks [c0 + j off, c0 + j off + C)
+// C columns (C % 8 == 0) of this lane as the sum of BP column blocks
+// [taddr + j off, taddr + j off + C)
 template <int C, int BP = 2>
 __device__ __forceinline__ void tld_sum(uint32_t taddr, int off, float* out) {
+  float v[BP][C];
 #pragma unroll
-  for (int c = 0; c < C; c += 16) {
-    float a[16], b[16];
-    tld16(taddr + c, a);
-    tld16(taddr + off + c, b);
-    float e[16];
-    if constexpr (BP == 3) tld16(taddr + 2 * off + c, e);
-    tld_wait();
+  for (int j = 0; j < BP; ++j)
 #pragma unroll
-    for (int i = 0; i < 16 && c + i < C; ++i) {
-      out[c + i] = a[i] + b[i];
-      if constexpr (BP == 3) out[c + i] += e[i];
-    }
+    for (int c = 0; c < C; c += 8) tld8(taddr + j * off + c, &v[j][c]);
+  tld_wait();
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    float x = v[0][c];
+#pragma unroll
+    for (int j = 1; j < BP; ++j) x += v[j][c];
+    out[c] = x;
   }
 }
 
@@ -209,84 +229,123 @@ __device__ __forceinline__ void split3(float a, float b, uint32_t& hi, uint32_t&
   lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
-// Stages tile rows [t0, t0 + TT) of a [T][D] stream of element type T (row
-// stride st) as 16-byte chunks, chunk i of the tile at dst + 16 i -- the
-// K-major chunk order (fp32 rows: 4 columns per chunk, bf16: 8).  Rows >= t1
-// are zero-filled.
+// Tiles arrive by TMA: the host maps each streamed input as a 5-D tensor
+// (D, T, H, B, M) and a tile is NB boxes of 128 rows x IB bytes (IB = 128 with
+// the 128-byte swizzle -- 16-byte chunk c of row r stored at chunk c ^ (r % 8)
+// -- or the whole row when it is shorter).  Rows past the tensor's end are
+// zero-filled by the copy engine; rows past a range's end are read but never
+// written back or counted.
 template <typename T, int D>
-__device__ __forceinline__ void stage(void* dst, const T* base, int64_t st, int64_t t0, int64_t t1) {
-  constexpr int EPC = 16 / (int)sizeof(T);   // elements per chunk
-  constexpr int CPR = D / EPC;               // chunks per row
-  char* d = static_cast<char*>(dst);
-#pragma unroll 4
-  for (int i = threadIdx.x; i < TT * CPR; i += NT) {
-    const int g = i / (8 * CPR), j = i % (8 * CPR);
-    const int c = j >> 3, r = g * 8 + (j & 7);
-    const int64_t t = t0 + r;
-    const bool ok = t < t1;
-    tiles::cp_async16(d + 16 * i, base + (ok ? t : t0) * st + EPC * c, ok);
+struct Box {
+  static constexpr int RB = D * (int)sizeof(T);      // bytes per row
+  static constexpr int IB = RB < 128 ? RB : 128;     // bytes per box row
+  static constexpr bool SWZ = IB == 128;
+  static constexpr int NB = RB / IB;                 // boxes per tile
+  static constexpr int BYTES = TT * RB;              // bytes per tile
+};
+
+__device__ __forceinline__ void bar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load5(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                          int c3, int c4, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3, %4, %5, %6}], [%7];" ::"r"(saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+      "r"(saddr(bar))
+      : "memory");
+}
+
+// One thread: loads tile rows [t0, t0 + TT) of stream n of NTS mapped tensors
+// into their slots and arms `bar` with the byte count.
+// A tensor whose ensemble axis has stride 0 is mapped with one ensemble.
+template <typename T, int D, int NTS>
+__device__ __forceinline__ void tma_tile(const TmaMaps& maps, float* const (&dst)[NTS],
+                                         const Layout* const (&lay)[NTS], const Params& prm,
+                                         int n, int64_t t0, uint64_t* bar) {
+  using BX = Box<T, D>;
+  const int h = n % prm.H, b = (n / prm.H) % prm.B, m = n / (prm.H * prm.B);
+  fence_async_smem();
+  bar_expect_tx(bar, (uint32_t)(BX::BYTES * NTS));
+#pragma unroll
+  for (int k = 0; k < NTS; ++k)
+#pragma unroll
+    for (int x = 0; x < BX::NB; ++x)
+      tma_load5(reinterpret_cast<char*>(dst[k]) + x * TT * BX::IB, &maps.map[k],
+                x * BX::IB / (int)sizeof(T), (int)t0, h, b, lay[k]->sm == 0 ? 0 : m, bar);
+}
+
+// Columns [c0, c0 + W) (c0, W multiples of 16 bytes) of row r of a landed
+// tile, as fp32.
+template <typename T, int D, int W>
+__device__ __forceinline__ void read_cols(const void* tile, int r, int c0, float* x) {
+  using BX = Box<T, D>;
+  constexpr int EPC = 16 / (int)sizeof(T);
+  const char* base = static_cast<const char*>(tile);
+#pragma unroll
+  for (int i = 0; i < W / EPC; ++i) {
+    const int gc = c0 / EPC + i;                       // 16-byte chunk of the row
+    const int bx = gc / (BX::IB / 16), c = gc % (BX::IB / 16);
+    const int pc = BX::SWZ ? (c ^ (r & 7)) : c;
+    const uint4 u =
+        *reinterpret_cast<const uint4*>(base + bx * TT * BX::IB + r * BX::IB + pc * 16);
+    if constexpr (sizeof(T) == 4) {
+      x[4 * i] = __uint_as_float(u.x);
+      x[4 * i + 1] = __uint_as_float(u.y);
+      x[4 * i + 2] = __uint_as_float(u.z);
+      x[4 * i + 3] = __uint_as_float(u.w);
+    } else {
+      const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(hb[j]);
+        x[8 * i + 2 * j] = f.x;
+        x[8 * i + 2 * j + 1] = f.y;
+      }
+    }
   }
 }
 
-// Reads this thread's row of a staged fp32 tile (4 columns per chunk).
-template <int D>
-__device__ __forceinline__ void read_row_f32(const void* tile, float (&x)[D]) {
-  const float4* t4 = static_cast<const float4*>(tile);
-  const int r = threadIdx.x;
+// Writes W values (columns [c0, c0 + W), W and c0 multiples of 8) of row r
+// as NP bf16 parts into operands p0 (, p1, p2) with C columns (NP = 1: the
+// values are exact in bf16).
+template <int C, int W, int NP>
+__device__ __forceinline__ void put_cols(bf16* p0, bf16* p1, bf16* p2, int r, int c0,
+                                         const float* v) {
 #pragma unroll
-  for (int c4 = 0; c4 < D / 4; ++c4) {
-    const float4 v = t4[(r >> 3) * (D / 4) * 8 + c4 * 8 + (r & 7)];
-    x[4 * c4] = v.x;
-    x[4 * c4 + 1] = v.y;
-    x[4 * c4 + 2] = v.z;
-    x[4 * c4 + 3] = v.w;
-  }
-}
-
-// Writes a register row (C values) of this thread's token as bf16 hi and lo
-// operands (C columns each).
-template <int C>
-__device__ __forceinline__ void put_row(bf16* hi, bf16* lo, const float* v) {
-  uint4* h4 = reinterpret_cast<uint4*>(hi);
-  uint4* l4 = reinterpret_cast<uint4*>(lo);
-  const int r = threadIdx.x;
-#pragma unroll
-  for (int c8 = 0; c8 < C / 8; ++c8) {
-    uint4 h, l;
-    split2(v[8 * c8 + 0], v[8 * c8 + 1], h.x, l.x);
-    split2(v[8 * c8 + 2], v[8 * c8 + 3], h.y, l.y);
-    split2(v[8 * c8 + 4], v[8 * c8 + 5], h.z, l.z);
-    split2(v[8 * c8 + 6], v[8 * c8 + 7], h.w, l.w);
-    h4[chunk<C>(r, c8)] = h;
-    l4[chunk<C>(r, c8)] = l;
-  }
-}
-
-// Writes a register row as three bf16 parts (hi, mid, lo operands).
-template <int C>
-__device__ __forceinline__ void put_row3(bf16* hi, bf16* mid, bf16* lo, const float* v) {
-  uint4* h4 = reinterpret_cast<uint4*>(hi);
-  uint4* m4 = reinterpret_cast<uint4*>(mid);
-  uint4* l4 = reinterpret_cast<uint4*>(lo);
-  const int r = threadIdx.x;
-#pragma unroll
-  for (int c8 = 0; c8 < C / 8; ++c8) {
+  for (int i = 0; i < W / 8; ++i) {
+    const int q = chunk<C>(r, c0 / 8 + i);
     uint4 h, m, l;
-    split3(v[8 * c8 + 0], v[8 * c8 + 1], h.x, m.x, l.x);
-    split3(v[8 * c8 + 2], v[8 * c8 + 3], h.y, m.y, l.y);
-    split3(v[8 * c8 + 4], v[8 * c8 + 5], h.z, m.z, l.z);
-    split3(v[8 * c8 + 6], v[8 * c8 + 7], h.w, m.w, l.w);
-    h4[chunk<C>(r, c8)] = h;
-    m4[chunk<C>(r, c8)] = m;
-    l4[chunk<C>(r, c8)] = l;
+    uint32_t* hp = &h.x;
+    uint32_t* mp = &m.x;
+    uint32_t* lp = &l.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = v[8 * i + 2 * j], b = v[8 * i + 2 * j + 1];
+      if constexpr (NP == 1) {
+        const __nv_bfloat162 x = __floats2bfloat162_rn(a, b);
+        hp[j] = *reinterpret_cast<const uint32_t*>(&x);
+      } else if constexpr (NP == 2) {
+        split2(a, b, hp[j], mp[j]);
+      } else {
+        split3(a, b, hp[j], mp[j], lp[j]);
+      }
+    }
+    reinterpret_cast<uint4*>(p0)[q] = h;
+    if constexpr (NP >= 2) reinterpret_cast<uint4*>(p1)[q] = m;
+    if constexpr (NP >= 3) reinterpret_cast<uint4*>(p2)[q] = l;
   }
 }
 
 // Fills a stacked constant operand [part 0; part 1; ...] of BP*R rows and C
 // columns with the BP bf16 parts of f(r, c).
-template <int R, int C, int BP = 2, class F>
+template <int R, int C, int BP, int NTHR, class F>
 __device__ __forceinline__ void put_stack(bf16* base, F f) {
-  for (int i = threadIdx.x; i < R * C; i += NT) {
+  for (int i = threadIdx.x; i < R * C; i += NTHR) {
     const int r = i / C, c = i % C;
     float x = f(r, c);
 #pragma unroll
@@ -298,85 +357,85 @@ __device__ __forceinline__ void put_stack(bf16* base, F f) {
   }
 }
 
-// Corner probabilities of one token from its projections (registers).
-// p[s] for s = l*R + r, tables l < L; h[j] = tanh(proj_j) kept for the backward.
-template <int K, int SP>
-__device__ __forceinline__ void token_probs(const float (&proj)[PJ], int L, float inv_scale,
-                                            float (&p)[SP], float (&h)[PJ]) {
-  constexpr int R = 1 << K;
-  constexpr int LMAX = (SP / R < PJ / K) ? SP / R : PJ / K;
+// Bucket groups of the hash: GB = max(8, R) buckets (GT = GB / R tables, GK =
+// GT K planes) -- whole 16-byte chunks of a probability row and whole tables.
+template <int K>
+struct Groups {
+  static constexpr int R = 1 << K;
+  static constexpr int GB = R > 8 ? R : 8;
+  static constexpr int GT = GB / R;
+  static constexpr int GK = GT * K;
+};
+
+// Corner probabilities of tables l0 .. l0 + GT - 1 of one token (tables >= L
+// give 0); h = tanh of their projections, kept for the backward.
+template <int K>
+__device__ __forceinline__ void group_probs(const float* proj, int l0, int L, float inv_scale,
+                                            float (&p)[Groups<K>::GB], float (&h)[Groups<K>::GK]) {
+  constexpr int R = 1 << K, GT = Groups<K>::GT;
 #pragma unroll
-  for (int s = 0; s < SP; ++s) p[s] = 0.f;
+  for (int u = 0; u < GT; ++u) {
+    const bool live = l0 + u < L;
+    float sp[K], sn[K];
 #pragma unroll
-  for (int j = 0; j < PJ; ++j) h[j] = 0.f;
+    for (int k = 0; k < K; ++k) {
+      const float hh = live ? tiles::tanh_exp(proj[u * K + k]) : 0.f;
+      h[u * K + k] = hh;
+      const float uu = hh * inv_scale;
+      const float ex = __expf(-2.f * fabsf(uu));
+      const float rc = __frcp_rn(1.f + ex);
+      sp[k] = uu >= 0.f ? rc : ex * rc;
+      sn[k] = uu >= 0.f ? ex * rc : rc;
+    }
 #pragma unroll
-  for (int l = 0; l < LMAX; ++l) {
-    if (l < L) {
-      float sp[K], sn[K];
+    for (int r = 0; r < R; ++r) {
+      float v = live ? 1.f : 0.f;
 #pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const float hh = tiles::tanh_exp(proj[l * K + k]);
-        h[l * K + k] = hh;
-        const float u = hh * inv_scale;
-        const float ex = __expf(-2.f * fabsf(u));
-        const float rc = __frcp_rn(1.f + ex);
-        sp[k] = u >= 0.f ? rc : ex * rc;
-        sn[k] = u >= 0.f ? ex * rc : rc;
-      }
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        float v = 1.f;
-#pragma unroll
-        for (int k = 0; k < K; ++k) v *= ((r >> (K - 1 - k)) & 1) ? sp[k] : sn[k];
-        p[l * R + r] = v;
-      }
+      for (int k = 0; k < K; ++k) v *= ((r >> (K - 1 - k)) & 1) ? sp[k] : sn[k];
+      p[u * R + r] = v;
     }
   }
 }
 
-// Backward of the corner probabilities of one token: given g[s] = dL/dp_s,
-// dj[j] = dL/dproj_j; ds += sum_j du_j h_j (the temperature's share).
-template <int K, int SP>
-__device__ __forceinline__ void token_probs_bwd(const float (&p)[SP], const float (&g)[SP],
-                                                const float (&h)[PJ], int L, float inv_scale,
-                                                float (&dj)[PJ], float& ds) {
-  constexpr int R = 1 << K;
-  constexpr int LMAX = (SP / R < PJ / K) ? SP / R : PJ / K;
+// Backward of group_probs: g = dL/dp of the group's buckets -> dj = dL/dproj
+// of its planes; ds += sum du h.
+template <int K>
+__device__ __forceinline__ void group_probs_bwd(const float (&p)[Groups<K>::GB],
+                                                const float (&g)[Groups<K>::GB],
+                                                const float (&h)[Groups<K>::GK], float inv_scale,
+                                                float (&dj)[Groups<K>::GK], float& ds) {
+  constexpr int R = 1 << K, GT = Groups<K>::GT;
 #pragma unroll
-  for (int j = 0; j < PJ; ++j) dj[j] = 0.f;
+  for (int u = 0; u < GT; ++u) {
+    float pbar = 0.f;
 #pragma unroll
-  for (int l = 0; l < LMAX; ++l) {
-    if (l < L) {
-      float pbar = 0.f;
+    for (int r = 0; r < R; ++r) pbar = fmaf(p[u * R + r], g[u * R + r], pbar);
+    float q[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) pbar = fmaf(p[l * R + r], g[l * R + r], pbar);
-      float q[R];
+    for (int r = 0; r < R; ++r) q[r] = p[u * R + r] * (g[u * R + r] - pbar);
 #pragma unroll
-      for (int r = 0; r < R; ++r) q[r] = p[l * R + r] * (g[l * R + r] - pbar);
+    for (int k = 0; k < K; ++k) {
+      float du = 0.f;
 #pragma unroll
-      for (int k = 0; k < K; ++k) {
-        float du = 0.f;
-#pragma unroll
-        for (int r = 0; r < R; ++r) du += ((r >> (K - 1 - k)) & 1) ? q[r] : -q[r];
-        const float hh = h[l * K + k];
-        ds = fmaf(du, hh, ds);
-        dj[l * K + k] = du * inv_scale * (1.f - hh * hh);
-      }
+      for (int r = 0; r < R; ++r) du += ((r >> (K - 1 - k)) & 1) ? q[r] : -q[r];
+      const float hh = h[u * K + k];
+      ds = fmaf(du, hh, ds);
+      dj[u * K + k] = du * inv_scale * (1.f - hh * hh);
     }
   }
 }
 
-template <typename T, int D>
-__device__ __forceinline__ void store_row(T* dst, const float* v) {
+template <typename T, int W>
+__device__ __forceinline__ void store_cols(T* dst, const float* v) {
   if constexpr (sizeof(T) == 4) {
     float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
-    for (int i = 0; i < D / 4; ++i)
+    for (int i = 0; i < W / 4; ++i)
       d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   } else {
     uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
+    for (int i = 0; i < W / 8; ++i) {
       uint4 u;
       __nv_bfloat162 b;
       b = __floats2bfloat162_rn(v[8 * i + 0], v[8 * i + 1]); u.x = *reinterpret_cast<uint32_t*>(&b);
@@ -406,31 +465,81 @@ __device__ __forceinline__ Item item_of(const Params& prm, int w) {
   return it;
 }
 
-// A tile slot holds TT x D fp32 as staged (4 B / element), converted in
-// place to NP bf16 parts (hi, lo or hi, mid, lo) of TT x D each; bf16 inputs
-// are staged straight into part 0.
+// A tile slot first holds the landed tile (TMA boxes, input type), then --
+// converted in place -- NP bf16 operand parts (hi, lo or hi, mid, lo) of TT x D
+// each.  Slots are 1 KB aligned (the 128-byte swizzle works in 1 KB atoms).
 template <int D, int NP = 2>
 struct Slot {
-  static constexpr int FLOATS = TT * D * NP / 2;
+  static constexpr int FLOATS = (TT * D * (NP < 2 ? 2 : NP) / 2 + 255) / 256 * 256;
   __device__ static bf16* part(float* s, int i) { return reinterpret_cast<bf16*>(s) + i * TT * D; }
 };
+
+// Coalesced row stores through a warp-private scratch (32 rows x 48 B): the
+// warp's lanes hold rows r0 + lane, columns [c0, c0 + W) each; every pass
+// moves 32 B of each row, written as 16 rows x 32 B per store instruction.
+template <typename T, int W>
+__device__ __forceinline__ void store_rows(T* base, int64_t st, int64_t r0, int64_t t1, int c0,
+                                           const float* v, float* scratch) {
+  constexpr int EP = 32 / (int)sizeof(T);   // elements per pass per row
+  const int lane = threadIdx.x & 31;
+  if constexpr (W < EP) {   // a 16-byte slice per row: store it directly
+    static_assert(W * sizeof(T) == 16, "slice of 16 bytes");
+    (void)scratch;
+    if (r0 + lane < t1) store_cols<T, W>(base + (r0 + lane) * st + c0, v);
+    return;
+  }
+#pragma unroll
+  for (int ps = 0; ps < W / EP; ++ps) {
+    uint4* sc = reinterpret_cast<uint4*>(scratch);
+    if constexpr (sizeof(T) == 4) {
+      float4* sf = reinterpret_cast<float4*>(scratch);
+      sf[lane * 3] = make_float4(v[ps * 8 + 0], v[ps * 8 + 1], v[ps * 8 + 2], v[ps * 8 + 3]);
+      sf[lane * 3 + 1] = make_float4(v[ps * 8 + 4], v[ps * 8 + 5], v[ps * 8 + 6], v[ps * 8 + 7]);
+    } else {
+      uint4 a, b;
+      uint32_t* pa = &a.x;
+      uint32_t* pb = &b.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 x = __floats2bfloat162_rn(v[ps * 16 + 2 * j], v[ps * 16 + 2 * j + 1]);
+        __nv_bfloat162 y = __floats2bfloat162_rn(v[ps * 16 + 8 + 2 * j], v[ps * 16 + 9 + 2 * j]);
+        pa[j] = *reinterpret_cast<uint32_t*>(&x);
+        pb[j] = *reinterpret_cast<uint32_t*>(&y);
+      }
+      sc[lane * 3] = a;
+      sc[lane * 3 + 1] = b;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int rr = h * 16 + (lane >> 1);
+      const uint4 u = sc[rr * 3 + (lane & 1)];
+      const int64_t t = r0 + rr;
+      if (t < t1)
+        *reinterpret_cast<uint4*>(base + t * st + c0 + ps * EP + (lane & 1) * (EP / 2)) = u;
+    }
+    __syncwarp();
+  }
+}
 
 // ------------------------------------------------------------------ layouts (in floats)
 template <int D, int SPAD>
 struct ReadoutLay {
+  static constexpr int NTH = RACE_T5_NTH_RO;          // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;   // bucket columns (MMA K)
   static constexpr int QX = 0;                        // [2] slots
   static constexpr int PQ = QX + 2 * Slot<D>::FLOATS; // bf16 [TT x SP] hi, then lo
   static constexpr int PS = PQ + TT * SP;             // bf16 [2*PJ x D] planes [hi; lo]
   static constexpr int ET = PS + PJ * D;              // bf16 [2*D x SP] E^T [hi; lo]
-  static constexpr int BAR = ET + D * SP;             // mbarrier (8 B) + TMEM base slot
-  static constexpr int FLOATS = BAR + 8;
+  static constexpr int BAR = ET + D * SP;             // four mbarriers + TMEM base slot
+  static constexpr int FLOATS = BAR + 12 + 256;       // + slack for 1 KB alignment
   static constexpr int TCOLS = 256;                   // PROJ [0, 32), OUT [128, 128 + 2D)
   static constexpr int C_PROJ = 0, C_OUT = 128;
 };
 
 template <int D, int SPAD>
 struct BwdKVLay {
+  static constexpr int NTH = RACE_T5_NTH_KV;           // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;    // bucket columns (MMA K and N)
   static constexpr int KX = 0;                         // [2] slots
   static constexpr int VX = KX + 2 * Slot<D>::FLOATS;  // [2] slots of three parts
@@ -441,9 +550,9 @@ struct BwdKVLay {
   static constexpr int DB = PT + D * PJ;               // bf16 [3*SP x D] dB [hi; mid; lo]
   static constexpr int DBT = DB + 3 * SP * D / 2;      // bf16 [2*D x SP] dB^T [hi; lo]
   static constexpr int DA = DBT + D * SP;              // [32] dA
-  static constexpr int RED = DA + 32;                  // [8] reductions
-  static constexpr int BAR = RED + 8;
-  static constexpr int FLOATS = BAR + 8;
+  static constexpr int RED = DA + 32;                  // [16] reductions
+  static constexpr int BAR = RED + 16;                 // four mbarriers + TMEM base slot
+  static constexpr int FLOATS = BAR + 12 + 256;        // + slack for 1 KB alignment
   static constexpr int TCOLS = 512;   // PROJ [0,32), DPK [32, 32+3SP), DV [128, 128+2D), DK [256, 256+2D)
   static constexpr int C_PROJ = 0, C_DPK = 32, C_DV = 128, C_DK = 256;
 };
@@ -459,54 +568,56 @@ struct BwdKVLay {
     }                                                            \
   } while (0)
 
-// Converts this thread's rows of staged fp32 slots in place to hi | lo (all
-// threads read before any writes).
-template <int D>
-__device__ __forceinline__ void convert_one(float* slot) {
-  float x[D];
-  read_row_f32<D>(slot, x);
-  __syncthreads();
-  put_row<D>(Slot<D>::part(slot, 0), Slot<D>::part(slot, 1), x);
-}
-// a -> hi, lo;  b -> hi, mid, lo
-template <int D>
-__device__ __forceinline__ void convert_two(float* a, float* b) {
-  float x[D], y[D];
-  read_row_f32<D>(a, x);
-  read_row_f32<D>(b, y);
-  __syncthreads();
-  put_row<D>(Slot<D>::part(a, 0), Slot<D>::part(a, 1), x);
-  put_row3<D>(Slot<D, 3>::part(b, 0), Slot<D, 3>::part(b, 1), Slot<D, 3>::part(b, 2), y);
-}
+#define T5_PROLOGUE                                                          \
+  extern __shared__ __align__(1024) float sm_raw[];                          \
+  float* sm = sm_raw + ((1024 - (saddr(sm_raw) & 1023)) & 1023) / 4;         \
+  uint64_t* barA = reinterpret_cast<uint64_t*>(sm + LY::BAR);                \
+  uint64_t* barB = barA + 1;                                                 \
+  uint64_t* full = barA + 2; /* [2]: the tile of a slot has landed */        \
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + LY::BAR + 8);           \
+  const int tid = threadIdx.x, warp = tid >> 5;                              \
+  const int row = tid & (TT - 1), sub = tid / TT;                            \
+  const float inv_scale = 1.f / __ldg(prm.scale);                            \
+  const int L = prm.L;                                                       \
+  const int items = prm.N * prm.P;                                           \
+  if ((int)blockIdx.x >= items) return;                                      \
+  if (tid == 0) {                                                            \
+    bar_init(barA);                                                          \
+    bar_init(barB);                                                          \
+    bar_init(full);                                                          \
+    bar_init(full + 1);                                                      \
+  }                                                                          \
+  if (warp == 0) tmem_alloc<LY::TCOLS>(tslot);                               \
+  fence_before();                                                            \
+  __syncthreads();                                                           \
+  fence_after();                                                             \
+  const uint32_t tbase = *tslot;                                             \
+  const uint32_t tlane = tbase + ((uint32_t)((warp & 3) * 32) << 16);        \
+  uint32_t phA = 0, phB = 0, phF = 0; /* phF bit s: parity of full[s] */   \
+  uint32_t inflight = 0;              /* bit s: a tile of slot s in flight */\
+  bool failed = false;                                                       \
+  int cur_n = -1, cur_m = -1;
+
+#define T5_EPILOGUE                                                          \
+  for (int s_ = 0; s_ < 2; ++s_)                                             \
+    if ((inflight >> s_) & 1) bar_wait(full + s_, (phF >> s_) & 1);          \
+  fence_before();                                                            \
+  __syncthreads();                                                           \
+  fence_after();                                                             \
+  if (warp == 0) tmem_free<LY::TCOLS>(tbase);
 
 // ------------------------------------------------------------------ F2 readout
 // out[t] = sum_s pQ[t][s] E[s]  with E = B / (A + eps) of the stream's state.
 template <typename T, int D, int SPAD, int K>
-__global__ void __launch_bounds__(NT, 1) k_t5_readout(const Params prm) {
+__global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout(const Params prm, const __grid_constant__ TmaMaps maps) {
   using LY = ReadoutLay<D, SPAD>;
-  constexpr int SP = LY::SP;
+  constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
+  using G = Groups<K>;
   constexpr bool F32 = sizeof(T) == 4;
-  extern __shared__ __align__(128) float sm[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + LY::BAR);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + LY::BAR + 2);
+  T5_PROLOGUE
   bf16* pq = reinterpret_cast<bf16*>(sm + LY::PQ);
   bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
   bf16* et = reinterpret_cast<bf16*>(sm + LY::ET);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const float inv_scale = 1.f / __ldg(prm.scale);
-  const int L = prm.L;
-  const int items = prm.N * prm.P;
-  if ((int)blockIdx.x >= items) return;
-  if (tid == 0) bar_init(bar);
-  if (warp == 0) tmem_alloc<LY::TCOLS>(tslot);
-  fence_before();
-  __syncthreads();
-  fence_after();
-  const uint32_t tbase = *tslot;
-  const uint32_t tlane = tbase + ((uint32_t)(warp * 32) << 16);
-  uint32_t phase = 0;
-  bool failed = false;
-  int cur_n = -1, cur_m = -1;
   for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
     const Item it = item_of(prm, w);
     if (it.ntiles <= 0) continue;
@@ -515,50 +626,85 @@ __global__ void __launch_bounds__(NT, 1) k_t5_readout(const Params prm) {
     __syncthreads();   // the previous item's MMAs are complete; tables may change
     if (m != cur_m) {
       const float* pl = prm.planes + (size_t)m * prm.LK * D;
-      put_stack<PJ, D>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+      put_stack<PJ, D, 2, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
       cur_m = m;
     }
     if (n != cur_n) {
       const float* st = prm.state + (size_t)n * prm.SS;
       const float* mass = st + prm.S * D;
-      put_stack<D, SP>(et, [&](int d, int s) {
+      put_stack<D, SP, 2, NTHR>(et, [&](int d, int s) {
         return s < prm.S ? st[s * D + d] / (mass[s] + prm.eps) : 0.f;
       });
       cur_n = n;
     }
-    const T* qb = static_cast<const T*>(prm.q) + stream_offset(prm.lq, n, prm.B, prm.H);
     T* ob = static_cast<T*>(prm.out) + stream_offset(prm.lo, n, prm.B, prm.H);
-    stage<T, D>(sm + LY::QX, qb, prm.lq.st, it.t0, it.t1);
-    tiles::cp_commit();
+    // Pipeline per tile i: load(i+1) | convert(i) -> MMA proj(i) || store(i-1)
+    // -> probabilities(i) -> MMA out(i) || next tile ...
+    float* scratch = sm + LY::PQ + warp * 384;   // store_rows scratch (PQ is free then)
+    auto store_prev = [&](int64_t tprev) {
+      T5_CHECK(bar_wait(barB, phB));
+      phB ^= 1;
+      if (failed) return;
+      fence_after();
+      float o[W];
+      tld_sum<W>(tlane + LY::C_OUT + sub * W, D, o);
+      store_rows<T, W>(ob, prm.lo.st, tprev + (warp & 3) * 32, it.t1, sub * W, o, scratch);
+      fence_before();
+    };
+    auto load = [&](int j) {
+      inflight |= 1u << (j & 1);
+      if (tid == 0) {
+        float* const dst[1] = {sm + LY::QX + (j & 1) * Slot<D>::FLOATS};
+        const Layout* const lay[1] = {&prm.lq};
+        tma_tile<T, D, 1>(maps, dst, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j & 1));
+      }
+    };
+    load(0);
     for (int i = 0; i < it.ntiles; ++i) {
       const int64_t tile0 = it.t0 + (int64_t)i * TT;
       float* X = sm + LY::QX + (i & 1) * Slot<D>::FLOATS;
-      if (i + 1 < it.ntiles)
-        stage<T, D>(sm + LY::QX + ((i + 1) & 1) * Slot<D>::FLOATS, qb, prm.lq.st, tile0 + TT,
-                    it.t1);
-      tiles::cp_commit();
-      tiles::cp_wait<1>();
-      if constexpr (F32) {
+      if (i + 1 < it.ntiles) load(i + 1);
+      T5_CHECK(bar_wait(full + (i & 1), (phF >> (i & 1)) & 1));
+      if (failed) break;
+      phF ^= 1u << (i & 1);
+      inflight &= ~(1u << (i & 1));
+      {
+        float x[W];
+        read_cols<T, D, W>(X, row, sub * W, x);
         __syncthreads();
-        convert_one<D>(X);
+        put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(X, 0), Slot<D>::part(X, 1), nullptr, row,
+                                    sub * W, x);
       }
       fence_async_smem();
+      fence_before();
       __syncthreads();
       if (tid == 0) {
         fence_after();
         gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(X, 0),
                                         Slot<D>::part(X, 1), nullptr, F32 ? 2 : 1, ps, false);
-        commit(bar);
+        commit(barA);
       }
-      T5_CHECK(bar_wait(bar, phase));
-      phase ^= 1;
+      if (i > 0) {
+        store_prev(tile0 - TT);
+        if (failed) break;
+      }
+      T5_CHECK(bar_wait(barA, phA));
+      phA ^= 1;
       if (failed) break;
       fence_after();
       {
-        float proj[PJ], h[PJ], p[SP];
+        float proj[PJ];
         tld_sum<PJ>(tlane + LY::C_PROJ, PJ, proj);
-        token_probs<K, SP>(proj, L, inv_scale, p, h);
-        put_row<SP>(pq, pq + TT * SP, p);
+#pragma unroll
+        for (int gi = 0; gi < SP / G::GB; ++gi) {
+          if (gi % NTH == sub) {
+            float p[G::GB], h[G::GK];
+            const bool has = gi * G::GK < PJ;
+            group_probs<K>(has ? proj + gi * G::GK : proj, gi * G::GT, has ? L : 0, inv_scale, p,
+                           h);
+            put_cols<SP, G::GB, 2>(pq, pq + TT * SP, nullptr, row, gi * G::GB, p);
+          }
+        }
       }
       fence_async_smem();
       fence_before();
@@ -567,61 +713,32 @@ __global__ void __launch_bounds__(NT, 1) k_t5_readout(const Params prm) {
         fence_after();
         gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_OUT, pq, pq + TT * SP, nullptr, 2, et,
                                           false);
-        commit(bar);
+        commit(barB);
       }
-      T5_CHECK(bar_wait(bar, phase));
-      phase ^= 1;
-      if (failed) break;
-      fence_after();
-      {
-        float o[D];
-        tld_sum<D>(tlane + LY::C_OUT, D, o);
-        const int64_t t = tile0 + tid;
-        if (t < it.t1) store_row<T, D>(ob + t * prm.lo.st, o);
-      }
-      fence_before();
     }
-    tiles::cp_wait<0>();
+    if (!failed) store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT);
   }
-  tiles::cp_wait<0>();
-  fence_before();
-  __syncthreads();
-  fence_after();
-  if (warp == 0) tmem_free<LY::TCOLS>(tbase);
+  T5_EPILOGUE
 }
 
 // ------------------------------------------------------------------ B2 key/value backward
 // dv = pK . dB,  dpK = v . dB^T + dA,  dk = dproj(pK, dpK) . P;  the k-side dscale.
 template <typename T, int D, int SPAD, int K>
-__global__ void __launch_bounds__(NT, 1) k_t5_bwd_kv(const Params prm) {
+__global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(const Params prm, const __grid_constant__ TmaMaps maps) {
   using LY = BwdKVLay<D, SPAD>;
-  constexpr int SP = LY::SP;
+  constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
+  using G = Groups<K>;
   constexpr bool F32 = sizeof(T) == 4;
-  extern __shared__ __align__(128) float sm[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + LY::BAR);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + LY::BAR + 2);
+  T5_PROLOGUE
   bf16* pk = reinterpret_cast<bf16*>(sm + LY::PK);
   bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
   bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
   bf16* pt = reinterpret_cast<bf16*>(sm + LY::PT);
   bf16* db = reinterpret_cast<bf16*>(sm + LY::DB);
   bf16* dbt = reinterpret_cast<bf16*>(sm + LY::DBT);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const float inv_scale = 1.f / __ldg(prm.scale);
-  const int L = prm.L;
-  const int items = prm.N * prm.P;
-  if ((int)blockIdx.x >= items) return;
-  if (tid == 0) bar_init(bar);
-  if (warp == 0) tmem_alloc<LY::TCOLS>(tslot);
-  fence_before();
-  __syncthreads();
-  fence_after();
-  const uint32_t tbase = *tslot;
-  const uint32_t tlane = tbase + ((uint32_t)(warp * 32) << 16);
-  uint32_t phase = 0;
-  bool failed = false;
-  int cur_n = -1, cur_m = -1;
   float* dA = sm + LY::DA;
+  // planes of DJ not covered by any bucket group stay zero
+  for (int i = tid; i < TT * PJ; i += NTHR) reinterpret_cast<float*>(dj)[i] = 0.f;
   for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
     const Item it = item_of(prm, w);
     const int n = it.n;
@@ -631,8 +748,8 @@ __global__ void __launch_bounds__(NT, 1) k_t5_bwd_kv(const Params prm) {
       __syncthreads();
       if (m != cur_m) {
         const float* pl = prm.planes + (size_t)m * prm.LK * D;
-        put_stack<PJ, D>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
-        put_stack<D, PJ>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+        put_stack<PJ, D, 2, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+        put_stack<D, PJ, 2, NTHR>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
         cur_m = m;
       }
       if (n != cur_n) {
@@ -640,10 +757,10 @@ __global__ void __launch_bounds__(NT, 1) k_t5_bwd_kv(const Params prm) {
         const float* gs = prm.gstate_in + (size_t)n * prm.SS;
         const float* mass = st + prm.S * D;
         // dB = dE / (A + eps);  dA_s = -sum_d dE_sd B_sd / (A_s + eps)^2
-        put_stack<SP, D, 3>(db, [&](int s, int d) {
+        put_stack<SP, D, 3, NTHR>(db, [&](int s, int d) {
           return s < prm.S ? gs[s * D + d] / (mass[s] + prm.eps) : 0.f;
         });
-        put_stack<D, SP>(dbt, [&](int d, int s) {
+        put_stack<D, SP, 2, NTHR>(dbt, [&](int d, int s) {
           return s < prm.S ? gs[s * D + d] / (mass[s] + prm.eps) : 0.f;
         });
         if (tid < 32) {
@@ -658,37 +775,60 @@ __global__ void __launch_bounds__(NT, 1) k_t5_bwd_kv(const Params prm) {
         cur_n = n;
       }
       __syncthreads();
-      float dAr[SP];
-#pragma unroll
-      for (int s = 0; s < SP; ++s) dAr[s] = s < 32 ? dA[s] : 0.f;
-      const T* kb = static_cast<const T*>(prm.k) + stream_offset(prm.lk, n, prm.B, prm.H);
-      const T* vb = static_cast<const T*>(prm.v) + stream_offset(prm.lv, n, prm.B, prm.H);
       T* dkb = static_cast<T*>(prm.dk) + stream_offset(prm.ldk, n, prm.B, prm.H);
       T* dvb = static_cast<T*>(prm.dv) + stream_offset(prm.ldv, n, prm.B, prm.H);
-      stage<T, D>(sm + LY::KX, kb, prm.lk.st, it.t0, it.t1);
-      stage<T, D>(sm + LY::VX, vb, prm.lv.st, it.t0, it.t1);
-      tiles::cp_commit();
+      // Pipeline per tile i: load(i+1) | convert(i) -> MMA proj, dpK (i) ||
+      // store(i-1) -> hash backward(i) -> MMA dv, dk (i) || next tile ...
+      float* scratch = sm + LY::PK + warp * 384;   // store_rows scratch (PK, DJ free then)
+      auto store_prev = [&](int64_t tprev) {
+        T5_CHECK(bar_wait(barB, phB));
+        phB ^= 1;
+        if (failed) return;
+        fence_after();
+        const int64_t r0 = tprev + (warp & 3) * 32;
+        float o[W];
+        tld_sum<W>(tlane + LY::C_DV + sub * W, D, o);
+        store_rows<T, W>(dvb, prm.ldv.st, r0, it.t1, sub * W, o, scratch);
+        tld_sum<W>(tlane + LY::C_DK + sub * W, D, o);
+        store_rows<T, W>(dkb, prm.ldk.st, r0, it.t1, sub * W, o, scratch);
+        fence_before();
+      };
+      auto load = [&](int j) {
+        inflight |= 1u << (j & 1);
+        if (tid == 0) {
+          float* const dst[2] = {sm + LY::KX + (j & 1) * Slot<D>::FLOATS,
+                                 sm + LY::VX + (j & 1) * Slot<D, 3>::FLOATS};
+          const Layout* const lay[2] = {&prm.lk, &prm.lv};
+          tma_tile<T, D, 2>(maps, dst, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j & 1));
+        }
+      };
+      load(0);
       for (int i = 0; i < it.ntiles; ++i) {
         const int64_t tile0 = it.t0 + (int64_t)i * TT;
         float* KXt = sm + LY::KX + (i & 1) * Slot<D>::FLOATS;
         float* VXt = sm + LY::VX + (i & 1) * Slot<D, 3>::FLOATS;
-        if (i + 1 < it.ntiles) {
-          stage<T, D>(sm + LY::KX + ((i + 1) & 1) * Slot<D>::FLOATS, kb, prm.lk.st, tile0 + TT,
-                      it.t1);
-          stage<T, D>(sm + LY::VX + ((i + 1) & 1) * Slot<D, 3>::FLOATS, vb, prm.lv.st, tile0 + TT,
-                      it.t1);
-        }
-        tiles::cp_commit();
-        tiles::cp_wait<1>();
-        if constexpr (F32) {
+        if (i + 1 < it.ntiles) load(i + 1);
+        T5_CHECK(bar_wait(full + (i & 1), (phF >> (i & 1)) & 1));
+        if (failed) break;
+        phF ^= 1u << (i & 1);
+        inflight &= ~(1u << (i & 1));
+        {
+          float x[W], y[W];
+          read_cols<T, D, W>(KXt, row, sub * W, x);
+          read_cols<T, D, W>(VXt, row, sub * W, y);
           __syncthreads();
-          convert_two<D>(KXt, VXt);
+          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), nullptr, row,
+                                      sub * W, x);
+          put_cols<D, W, F32 ? 3 : 1>(Slot<D, 3>::part(VXt, 0), Slot<D, 3>::part(VXt, 1),
+                                      Slot<D, 3>::part(VXt, 2), row, sub * W, y);
         }
         fence_async_smem();
+        fence_before();
         __syncthreads();
         // projections and dpK = v . dB^T
         if (tid == 0) {
           fence_after();
+          if (!(RACE_T5_ABL & 8)) {
           gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
                                           Slot<D>::part(KXt, 1), nullptr, F32 ? 2 : 1, ps, false);
           // dpK carries three parts on both sides: where v matches a bucket's
@@ -696,51 +836,64 @@ __global__ void __launch_bounds__(NT, 1) k_t5_bwd_kv(const Params prm) {
           gemm_parts<SP, 3, D / 16, D, D>(tbase + LY::C_DPK, Slot<D, 3>::part(VXt, 0),
                                           Slot<D, 3>::part(VXt, 1), Slot<D, 3>::part(VXt, 2),
                                           F32 ? 3 : 1, db, false);
-          commit(bar);
+          }
+          commit(barA);
         }
-        T5_CHECK(bar_wait(bar, phase));
-        phase ^= 1;
+        if (i > 0) {
+          store_prev(tile0 - TT);
+          if (failed) break;
+        }
+        T5_CHECK(bar_wait(barA, phA));
+        phA ^= 1;
         if (failed) break;
         fence_after();
         {
-          float proj[PJ], h[PJ], p[SP], g[SP], dj_[PJ];
+          float proj[PJ];
           tld_sum<PJ>(tlane + LY::C_PROJ, PJ, proj);
-          tld_sum<SP, 3>(tlane + LY::C_DPK, SP, g);
+          const bool valid = tile0 + row < it.t1;
 #pragma unroll
-          for (int s = 0; s < SP; ++s) g[s] += dAr[s];
-          token_probs<K, SP>(proj, L, inv_scale, p, h);
-          float dsl = 0.f;
-          token_probs_bwd<K, SP>(p, g, h, L, inv_scale, dj_, dsl);
-          if (tile0 + tid < it.t1) ds += dsl;
-          put_row<SP>(pk, pk + TT * SP, p);
-          put_row<PJ>(dj, dj + TT * PJ, dj_);
+          for (int gi = 0; gi < SP / G::GB; ++gi) {
+            if (gi % NTH == sub && !(RACE_T5_ABL & 2)) {
+              float p[G::GB], h[G::GK], g[G::GB], dj_[G::GK];
+              const bool has = gi * G::GK < PJ;
+              group_probs<K>(has ? proj + gi * G::GK : proj, gi * G::GT, has ? L : 0, inv_scale, p,
+                             h);
+              tld_sum<G::GB, 3>(tlane + LY::C_DPK + gi * G::GB, SP, g);
+#pragma unroll
+              for (int b = 0; b < G::GB; ++b) g[b] += dA[gi * G::GB + b];
+              float dsl = 0.f;
+              group_probs_bwd<K>(p, g, h, inv_scale, dj_, dsl);
+              if (valid) ds += dsl;
+              put_cols<SP, G::GB, 2>(pk, pk + TT * SP, nullptr, row, gi * G::GB, p);
+              if (has) {
+#pragma unroll
+                for (int j = 0; j < G::GK; ++j) {
+                  const int jj = gi * G::GK + j;
+                  if (jj < PJ) {
+                    const bf16 hb = __float2bfloat16_rn(dj_[j]);
+                    dj[elem<PJ>(row, jj)] = hb;
+                    dj[TT * PJ + elem<PJ>(row, jj)] = __float2bfloat16_rn(dj_[j] - __bfloat162float(hb));
+                  }
+                }
+              }
+            }
+          }
         }
         fence_async_smem();
         fence_before();
         __syncthreads();
         if (tid == 0) {
           fence_after();
+          if (!(RACE_T5_ABL & 8)) {
           gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_DV, pk, pk + TT * SP, nullptr, 2, dbt,
                                             false);
           gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DK, dj, dj + TT * PJ, nullptr, 2, pt,
                                             false);
-          commit(bar);
+          }
+          commit(barB);
         }
-        T5_CHECK(bar_wait(bar, phase));
-        phase ^= 1;
-        if (failed) break;
-        fence_after();
-        {
-          const int64_t t = tile0 + tid;
-          float o[D];
-          tld_sum<D>(tlane + LY::C_DV, D, o);
-          if (t < it.t1) store_row<T, D>(dvb + t * prm.ldv.st, o);
-          tld_sum<D>(tlane + LY::C_DK, D, o);
-          if (t < it.t1) store_row<T, D>(dkb + t * prm.ldk.st, o);
-        }
-        fence_before();
       }
-      tiles::cp_wait<0>();
+      if (!failed) store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT);
     }
     // per-item dscale partial (zero for an empty range), fixed-order CTA sum
     float x = ds;
@@ -749,18 +902,18 @@ __global__ void __launch_bounds__(NT, 1) k_t5_bwd_kv(const Params prm) {
     __syncthreads();
     if ((tid & 31) == 0) sm[LY::RED + warp] = x;
     __syncthreads();
-    if (tid == 0)
-      prm.dscale_part[(size_t)n * prm.P + it.part] =
-          (sm[LY::RED] + sm[LY::RED + 1]) + (sm[LY::RED + 2] + sm[LY::RED + 3]);
+    if (tid == 0) {
+      float tot = 0.f;
+      for (int i = 0; i < NTHR / 32; ++i) tot += sm[LY::RED + i];
+      prm.dscale_part[(size_t)n * prm.P + it.part] = tot;
+    }
   }
-  tiles::cp_wait<0>();
-  fence_before();
-  __syncthreads();
-  fence_after();
-  if (warp == 0) tmem_free<LY::TCOLS>(tbase);
+  T5_EPILOGUE
 }
 
 #undef T5_CHECK
+#undef T5_PROLOGUE
+#undef T5_EPILOGUE
 
 }  // namespace t5
 }  // namespace race
