@@ -97,6 +97,29 @@ __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t a, uint64_t b, uin
       "l"(a), "l"(b), "r"(id), "r"((uint32_t)acc));
 }
 
+// Contractions over the tokens of a tile read the token-major operands
+// directly as MN-major operands (rows of the result along the columns C of
+// the operand, K along its tokens): 8-column blocks 128 B apart (stride byte
+// offset), 8-token blocks 16C B apart (leading byte offset); a K = 16 step
+// advances the start by 32C B.
+template <int C>
+__device__ __forceinline__ uint64_t desc_mn(const void* base, int ks) {
+  const uint32_t a = saddr(base) + ks * 32 * C;
+  uint64_t d = (uint64_t)((a >> 4) & 0x3fff);
+  d |= (uint64_t)(((16 * C) >> 4) & 0x3fff) << 16;   // leading byte offset: next 8 tokens
+  d |= (uint64_t)(128 >> 4) << 32;                   // stride byte offset: next 8 columns
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+// instruction descriptor, M = 64, both operands MN-major (accumulator row m
+// in TMEM lane 32 (m/16) + m%16)
+template <int N>
+__host__ __device__ constexpr uint32_t idesc64_mn() {
+  static_assert(N % 8 == 0 && N >= 8 && N <= 256, "M = 64 needs N % 8 == 0, N <= 256");
+  return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(64 >> 4) << 24);
+}
+
 // Split product D = A . B^T with K = 16 KS.  A is given as NA bf16 parts
 // (a[0] + a[1] + ..., the later ones nullptr-free), B as BP parts stacked
 // along its rows ([B0; B1; ...], BP*N rows).  Column block j of D receives
@@ -137,17 +160,29 @@ __device__ __forceinline__ void bar_init(uint64_t* bar) {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 // Waits for phase `parity` of the barrier with a bounded number of polls.
+// With an abort word: gives up early once another thread has set it, and
+// sets it when its own polls run out.
+__device__ __forceinline__ bool bar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(saddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
+  for (int i = 0; i < kWaitPolls; ++i)
+    if (bar_try(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
   for (int i = 0; i < kWaitPolls; ++i) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(saddr(bar)), "r"(parity)
-        : "memory");
-    if (ok) return true;
+    if (bar_try(bar, parity)) return true;
+    if ((i & 63) == 63 && *abort != 0) return false;
   }
+  *abort = 1;
   return false;
 }
 
@@ -207,23 +242,24 @@ __device__ __forceinline__ void tmem_free(uint32_t base) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "n"(COLS));
 }
 
-// hi / lo bf16 parts of two floats, packed
+// hi / lo bf16 parts of two floats, packed (the residual with one packed
+// fp32x2 fused multiply-add)
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  const float2 hf = __bfloat1622float2(h);
-  const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  const float2 r = __ffma2_rn(__bfloat1622float2(h), make_float2(-1.f, -1.f), make_float2(a, b));
+  const __nv_bfloat162 l = __float22bfloat162_rn(r);
   hi = *reinterpret_cast<const uint32_t*>(&h);
   lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
 // hi / mid / lo bf16 parts of two floats (24 significant bits), packed
 __device__ __forceinline__ void split3(float a, float b, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+  const float2 m1 = make_float2(-1.f, -1.f);
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  const float2 hf = __bfloat1622float2(h);
-  const float ra = a - hf.x, rb = b - hf.y;
-  const __nv_bfloat162 m = __floats2bfloat162_rn(ra, rb);
-  const float2 mf = __bfloat1622float2(m);
-  const __nv_bfloat162 l = __floats2bfloat162_rn(ra - mf.x, rb - mf.y);
+  const float2 r1 = __ffma2_rn(__bfloat1622float2(h), m1, make_float2(a, b));
+  const __nv_bfloat162 m = __float22bfloat162_rn(r1);
+  const float2 r2 = __ffma2_rn(__bfloat1622float2(m), m1, r1);
+  const __nv_bfloat162 l = __float22bfloat162_rn(r2);
   hi = *reinterpret_cast<const uint32_t*>(&h);
   mid = *reinterpret_cast<const uint32_t*>(&m);
   lo = *reinterpret_cast<const uint32_t*>(&l);
@@ -531,8 +567,9 @@ struct ReadoutLay {
   static constexpr int PQ = QX + 2 * Slot<D>::FLOATS; // bf16 [TT x SP] hi, then lo
   static constexpr int PS = PQ + TT * SP;             // bf16 [2*PJ x D] planes [hi; lo]
   static constexpr int ET = PS + PJ * D;              // bf16 [2*D x SP] E^T [hi; lo]
-  static constexpr int BAR = ET + D * SP;             // four mbarriers + TMEM base slot
-  static constexpr int FLOATS = BAR + 12 + 256;       // + slack for 1 KB alignment
+  static constexpr int NFULL = 2;                      // tile-landed barriers
+  static constexpr int BAR = ET + D * SP;             // mbarriers + TMEM base slot
+  static constexpr int FLOATS = BAR + 16 + 256;       // + slack for 1 KB alignment
   static constexpr int TCOLS = 256;                   // PROJ [0, 32), OUT [128, 128 + 2D)
   static constexpr int C_PROJ = 0, C_OUT = 128;
 };
@@ -551,30 +588,33 @@ struct BwdKVLay {
   static constexpr int DBT = DB + 3 * SP * D / 2;      // bf16 [2*D x SP] dB^T [hi; lo]
   static constexpr int DA = DBT + D * SP;              // [32] dA
   static constexpr int RED = DA + 32;                  // [16] reductions
-  static constexpr int BAR = RED + 16;                 // four mbarriers + TMEM base slot
-  static constexpr int FLOATS = BAR + 12 + 256;        // + slack for 1 KB alignment
+  static constexpr int NFULL = 2;                       // tile-landed barriers
+  static constexpr int BAR = RED + 16;                 // mbarriers + TMEM base slot
+  static constexpr int FLOATS = BAR + 16 + 256;        // + slack for 1 KB alignment
   static constexpr int TCOLS = 512;   // PROJ [0,32), DPK [32, 32+3SP), DV [128, 128+2D), DK [256, 256+2D)
   static constexpr int C_PROJ = 0, C_DPK = 32, C_DV = 128, C_DK = 256;
 };
 
-// After a timed-out wait every thread of the CTA leaves its loops; the kernel
-// then waits for its own copies and frees its tensor memory.
-#define T5_CHECK(ok_expr)                                        \
+// A wait that times out sets the CTA's abort word (so the other threads'
+// waits return at once) and the thread's `failed`; side effects (stores,
+// MMA and copy issue) are skipped from then on, and every tile ends with one
+// CTA-wide vote so all threads leave the loops together.  The kernel then
+// waits for its own copies in flight and frees its tensor memory.
+#define T5_WAIT(bar_, ph_)                                       \
   do {                                                           \
-    const bool ok_ = (ok_expr);                                  \
-    if (__syncthreads_or(!ok_)) {                                \
-      if (threadIdx.x == 0) atomicOr(prm.err, kErrTimeout);      \
-      failed = true;                                             \
-    }                                                            \
+    if (!bar_wait(bar_, ph_, abort_flag)) failed = true;         \
   } while (0)
+#define T5_VOTE()                                                \
+  (__syncthreads_or(failed) ? (failed = true) : false)
 
 #define T5_PROLOGUE                                                          \
   extern __shared__ __align__(1024) float sm_raw[];                          \
   float* sm = sm_raw + ((1024 - (saddr(sm_raw) & 1023)) & 1023) / 4;         \
   uint64_t* barA = reinterpret_cast<uint64_t*>(sm + LY::BAR);                \
   uint64_t* barB = barA + 1;                                                 \
-  uint64_t* full = barA + 2; /* [2]: the tile of a slot has landed */        \
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + LY::BAR + 8);           \
+  uint64_t* full = barA + 2; /* [LY::NFULL]: the tile of a slot landed */   \
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + LY::BAR + 2 * (2 + LY::NFULL)); \
+  volatile uint32_t* abort_flag = tslot + 1;                                 \
   const int tid = threadIdx.x, warp = tid >> 5;                              \
   const int row = tid & (TT - 1), sub = tid / TT;                            \
   const float inv_scale = 1.f / __ldg(prm.scale);                            \
@@ -582,10 +622,10 @@ struct BwdKVLay {
   const int items = prm.N * prm.P;                                           \
   if ((int)blockIdx.x >= items) return;                                      \
   if (tid == 0) {                                                            \
+    *abort_flag = 0;                                                         \
     bar_init(barA);                                                          \
     bar_init(barB);                                                          \
-    bar_init(full);                                                          \
-    bar_init(full + 1);                                                      \
+    for (int f_ = 0; f_ < LY::NFULL; ++f_) bar_init(full + f_);              \
   }                                                                          \
   if (warp == 0) tmem_alloc<LY::TCOLS>(tslot);                               \
   fence_before();                                                            \
@@ -599,8 +639,9 @@ struct BwdKVLay {
   int cur_n = -1, cur_m = -1;
 
 #define T5_EPILOGUE                                                          \
-  for (int s_ = 0; s_ < 2; ++s_)                                             \
+  for (int s_ = 0; s_ < LY::NFULL; ++s_)                                     \
     if ((inflight >> s_) & 1) bar_wait(full + s_, (phF >> s_) & 1);          \
+  if (tid == 0 && *abort_flag != 0) atomicOr(prm.err, kErrTimeout);          \
   fence_before();                                                            \
   __syncthreads();                                                           \
   fence_after();                                                             \
@@ -642,16 +683,17 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
     // -> probabilities(i) -> MMA out(i) || next tile ...
     float* scratch = sm + LY::PQ + warp * 384;   // store_rows scratch (PQ is free then)
     auto store_prev = [&](int64_t tprev) {
-      T5_CHECK(bar_wait(barB, phB));
+      T5_WAIT(barB, phB);
       phB ^= 1;
-      if (failed) return;
       fence_after();
       float o[W];
       tld_sum<W>(tlane + LY::C_OUT + sub * W, D, o);
-      store_rows<T, W>(ob, prm.lo.st, tprev + (warp & 3) * 32, it.t1, sub * W, o, scratch);
+      if (!failed)
+        store_rows<T, W>(ob, prm.lo.st, tprev + (warp & 3) * 32, it.t1, sub * W, o, scratch);
       fence_before();
     };
     auto load = [&](int j) {
+      if (failed) return;
       inflight |= 1u << (j & 1);
       if (tid == 0) {
         float* const dst[1] = {sm + LY::QX + (j & 1) * Slot<D>::FLOATS};
@@ -664,10 +706,11 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       const int64_t tile0 = it.t0 + (int64_t)i * TT;
       float* X = sm + LY::QX + (i & 1) * Slot<D>::FLOATS;
       if (i + 1 < it.ntiles) load(i + 1);
-      T5_CHECK(bar_wait(full + (i & 1), (phF >> (i & 1)) & 1));
-      if (failed) break;
-      phF ^= 1u << (i & 1);
-      inflight &= ~(1u << (i & 1));
+      T5_WAIT(full + (i & 1), (phF >> (i & 1)) & 1);
+      if (!failed) {
+        phF ^= 1u << (i & 1);
+        inflight &= ~(1u << (i & 1));
+      }
       {
         float x[W];
         read_cols<T, D, W>(X, row, sub * W, x);
@@ -678,19 +721,16 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       fence_async_smem();
       fence_before();
       __syncthreads();
-      if (tid == 0) {
+      if (tid == 0 && !failed) {
         fence_after();
         gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(X, 0),
                                         Slot<D>::part(X, 1), nullptr, F32 ? 2 : 1, ps, false);
         commit(barA);
       }
-      if (i > 0) {
-        store_prev(tile0 - TT);
-        if (failed) break;
-      }
-      T5_CHECK(bar_wait(barA, phA));
+      if (i > 0) store_prev(tile0 - TT);
+      T5_WAIT(barA, phA);
       phA ^= 1;
-      if (failed) break;
+      __syncthreads();   // every warp is done with its store scratch (the PQ area)
       fence_after();
       {
         float proj[PJ];
@@ -709,14 +749,215 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       fence_async_smem();
       fence_before();
       __syncthreads();
-      if (tid == 0) {
+      if (tid == 0 && !failed) {
         fence_after();
         gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_OUT, pq, pq + TT * SP, nullptr, 2, et,
                                           false);
         commit(barB);
       }
+      if (T5_VOTE()) break;
     }
     if (!failed) store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT);
+    T5_VOTE();
+  }
+  T5_EPILOGUE
+}
+
+// ------------------------------------------------------------------ F1 reduce
+template <int D, int SPAD>
+struct ReduceLay {
+  static constexpr int NTH = RACE_T5_NTH_KV;           // threads per token
+  static constexpr int SP = (SPAD + 15) / 16 * 16;     // bucket columns
+  static constexpr int NFULL = 2;
+  static constexpr int KX = 0;                          // [2] k slots (landed, then 2 parts)
+  static constexpr int VX = KX + 2 * Slot<D>::FLOATS;   // [2] landed v tiles
+  static constexpr int VP = VX + 2 * Slot<D>::FLOATS;   // v parts hi, mid, lo: [TT x D] each
+  static constexpr int PK3 = VP + 3 * TT * D / 2;       // pK parts: [TT x 3 SP] = [hi | mid | lo]
+  static constexpr int PS = PK3 + 3 * TT * SP / 2;      // bf16 [2*PJ x D] planes [hi; lo]
+  static constexpr int BAR = PS + PJ * D;
+  static constexpr int FLOATS = BAR + 16 + 256;
+  static constexpr int TCOLS = 256;   // PROJ [0, 32), STATE [128, 128 + 3 SP) (M = 64)
+  static constexpr int C_PROJ = 0, C_ST = 128;
+  static_assert(3 * TT * SP / 2 >= TT * SP, "pK area doubles as the mass scratch");
+};
+
+// Per range: B[s][d] = sum_t pK[t][s] v[t][d] and A[s] = sum_t pK[t][s] into
+// the range's partial slot ([S][D] then [S]).  The tensor core accumulates
+// v^T . pK over every tile of the range in tensor memory (M = 64 rows of d,
+// both operands read MN-major from the token-major parts) with three bf16
+// parts on both sides (24 significant bits: a bucket that holds one token
+// must reproduce that token's v to fp32 accuracy, or the backward's
+// v . dB - dB . E loses it); the bucket mass is summed by the threads that
+// own each bucket group.
+template <typename T, int D, int SPAD, int K>
+__global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
+    k_t5_reduce(const Params prm, const __grid_constant__ TmaMaps maps) {
+  using LY = ReduceLay<D, SPAD>;
+  constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
+  using G = Groups<K>;
+  constexpr int NG = SP / G::GB;                       // bucket groups
+  constexpr int MYG = (NG + NTH - 1) / NTH;            // groups per thread (at most)
+  constexpr bool F32 = sizeof(T) == 4;
+  T5_PROLOGUE
+  bf16* vp = reinterpret_cast<bf16*>(sm + LY::VP);
+  bf16* pk3 = reinterpret_cast<bf16*>(sm + LY::PK3);
+  bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
+  for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
+    const Item it = item_of(prm, w);
+    const int n = it.n;
+    float* dst = prm.part + ((size_t)n * prm.P + it.part) * prm.SS;
+    const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
+    __syncthreads();
+    if (m != cur_m) {
+      const float* pl = prm.planes + (size_t)m * prm.LK * D;
+      put_stack<PJ, D, 2, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+      cur_m = m;
+    }
+    float mass[MYG][G::GB];
+#pragma unroll
+    for (int a = 0; a < MYG; ++a)
+#pragma unroll
+      for (int b = 0; b < G::GB; ++b) mass[a][b] = 0.f;
+    auto load = [&](int j) {
+      if (failed) return;
+      inflight |= 1u << (j & 1);
+      if (tid == 0) {
+        float* const dsts[2] = {sm + LY::KX + (j & 1) * Slot<D>::FLOATS,
+                                sm + LY::VX + (j & 1) * Slot<D>::FLOATS};
+        const Layout* const lay[2] = {&prm.lk, &prm.lv};
+        tma_tile<T, D, 2>(maps, dsts, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j & 1));
+      }
+    };
+    // Per tile i: k parts -> MMA proj(i) || [wait state(i-1)] v parts ->
+    // probabilities -> pK parts -> MMA state(i) || next tile
+    if (it.ntiles > 0) load(0);
+    for (int i = 0; i < it.ntiles; ++i) {
+      const int64_t tile0 = it.t0 + (int64_t)i * TT;
+      float* KXt = sm + LY::KX + (i & 1) * Slot<D>::FLOATS;
+      float* VXt = sm + LY::VX + (i & 1) * Slot<D>::FLOATS;
+      if (i + 1 < it.ntiles) load(i + 1);
+      T5_WAIT(full + (i & 1), (phF >> (i & 1)) & 1);
+      if (!failed) {
+        phF ^= 1u << (i & 1);
+        inflight &= ~(1u << (i & 1));
+      }
+      const bool valid = tile0 + row < it.t1;
+      float y[W];
+      {
+        float x[W];
+        read_cols<T, D, W>(KXt, row, sub * W, x);
+        read_cols<T, D, W>(VXt, row, sub * W, y);
+        __syncthreads();
+        put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), nullptr, row,
+                                    sub * W, x);
+      }
+      fence_async_smem();
+      fence_before();
+      __syncthreads();
+      if (tid == 0 && !failed) {
+        fence_after();
+        gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
+                                        Slot<D>::part(KXt, 1), nullptr, F32 ? 2 : 1, ps, false);
+        commit(barA);
+      }
+      if (i > 0) {   // the previous tile's state MMAs read the v and pK parts
+        T5_WAIT(barB, phB);
+        phB ^= 1;
+      }
+      // v parts (rows past the range are zero)
+      if (!valid) {
+#pragma unroll
+        for (int c = 0; c < W; ++c) y[c] = 0.f;
+      }
+      put_cols<D, W, 3>(vp, vp + TT * D, vp + 2 * TT * D, row, sub * W, y);
+      T5_WAIT(barA, phA);
+      phA ^= 1;
+      fence_after();
+      {
+        float proj[PJ];
+        tld_sum<PJ>(tlane + LY::C_PROJ, PJ, proj);
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          const int a = gi / NTH;
+          if (gi % NTH == sub) {
+            float p[G::GB], h[G::GK];
+            const bool has = gi * G::GK < PJ;
+            group_probs<K>(has ? proj + gi * G::GK : proj, gi * G::GT, has ? L : 0, inv_scale, p,
+                           h);
+#pragma unroll
+            for (int b = 0; b < G::GB; ++b) {
+              if (!valid) p[b] = 0.f;
+              mass[a][b] += p[b];
+            }
+            // one row of [hi | mid | lo] bucket blocks
+#pragma unroll
+            for (int c8 = 0; c8 < G::GB / 8; ++c8) {
+              uint4 h, mq, l;
+              split3(p[8 * c8 + 0], p[8 * c8 + 1], h.x, mq.x, l.x);
+              split3(p[8 * c8 + 2], p[8 * c8 + 3], h.y, mq.y, l.y);
+              split3(p[8 * c8 + 4], p[8 * c8 + 5], h.z, mq.z, l.z);
+              split3(p[8 * c8 + 6], p[8 * c8 + 7], h.w, mq.w, l.w);
+              uint4* q4 = reinterpret_cast<uint4*>(pk3);
+              const int c0 = gi * G::GB / 8 + c8;
+              q4[chunk<3 * SP>(row, c0)] = h;
+              q4[chunk<3 * SP>(row, SP / 8 + c0)] = mq;
+              q4[chunk<3 * SP>(row, 2 * SP / 8 + c0)] = l;
+            }
+          }
+        }
+      }
+      fence_async_smem();
+      fence_before();
+      __syncthreads();
+      if (tid == 0 && !failed) {
+        fence_after();
+        // state^T[d][s-block j] += sum_a v_a^T . pK_j  (v_a, pK MN-major over the tile's tokens)
+#pragma unroll
+        for (int a = 0; a < 3; ++a)
+#pragma unroll
+          for (int ks = 0; ks < TT / 16; ++ks)
+            mma(tbase + LY::C_ST, desc_mn<D>(vp + a * TT * D, ks), desc_mn<3 * SP>(pk3, ks),
+                idesc64_mn<3 * SP>(), i > 0 || a > 0 || ks > 0);
+        commit(barB);
+      }
+      if (T5_VOTE()) break;
+    }
+    if (failed) break;
+    if (it.ntiles > 0) {
+      T5_WAIT(barB, phB);
+      phB ^= 1;
+      if (T5_VOTE()) break;
+      fence_after();
+      // state: lane 32 q + l (l < 16) of warps 0..3 holds row d = 16 q + l
+      if (sub == 0) {
+        float st[3 * SP];
+#pragma unroll
+        for (int c = 0; c < 3 * SP; c += 8) tld8(tlane + LY::C_ST + c, st + c);
+        tld_wait();
+        const int l = tid & 31, d = 16 * (warp & 3) + l;
+        if (l < 16 && d < D) {
+#pragma unroll
+          for (int sidx = 0; sidx < SP; ++sidx)
+            if (sidx < prm.S) dst[sidx * D + d] = st[sidx] + st[SP + sidx] + st[2 * SP + sidx];
+        }
+      }
+      fence_before();
+      // bucket mass: per-thread sums -> scratch (pK area is free) -> fixed-order sum
+      float* ms = sm + LY::PK3;
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi)
+        if (gi % NTH == sub)
+#pragma unroll
+          for (int b = 0; b < G::GB; ++b) ms[row * SP + gi * G::GB + b] = mass[gi / NTH][b];
+      __syncthreads();
+      if (tid < prm.S) {
+        float tot = 0.f;
+        for (int r = 0; r < TT; ++r) tot += ms[r * SP + tid];
+        dst[prm.S * D + tid] = tot;
+      }
+    } else {
+      for (int e = tid; e < prm.S * D + prm.S; e += NTHR) dst[e] = 0.f;
+    }
   }
   T5_EPILOGUE
 }
@@ -781,19 +1022,19 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
       // store(i-1) -> hash backward(i) -> MMA dv, dk (i) || next tile ...
       float* scratch = sm + LY::PK + warp * 384;   // store_rows scratch (PK, DJ free then)
       auto store_prev = [&](int64_t tprev) {
-        T5_CHECK(bar_wait(barB, phB));
+        T5_WAIT(barB, phB);
         phB ^= 1;
-        if (failed) return;
         fence_after();
         const int64_t r0 = tprev + (warp & 3) * 32;
         float o[W];
         tld_sum<W>(tlane + LY::C_DV + sub * W, D, o);
-        store_rows<T, W>(dvb, prm.ldv.st, r0, it.t1, sub * W, o, scratch);
+        if (!failed) store_rows<T, W>(dvb, prm.ldv.st, r0, it.t1, sub * W, o, scratch);
         tld_sum<W>(tlane + LY::C_DK + sub * W, D, o);
-        store_rows<T, W>(dkb, prm.ldk.st, r0, it.t1, sub * W, o, scratch);
+        if (!failed) store_rows<T, W>(dkb, prm.ldk.st, r0, it.t1, sub * W, o, scratch);
         fence_before();
       };
       auto load = [&](int j) {
+        if (failed) return;
         inflight |= 1u << (j & 1);
         if (tid == 0) {
           float* const dst[2] = {sm + LY::KX + (j & 1) * Slot<D>::FLOATS,
@@ -808,10 +1049,11 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         float* KXt = sm + LY::KX + (i & 1) * Slot<D>::FLOATS;
         float* VXt = sm + LY::VX + (i & 1) * Slot<D, 3>::FLOATS;
         if (i + 1 < it.ntiles) load(i + 1);
-        T5_CHECK(bar_wait(full + (i & 1), (phF >> (i & 1)) & 1));
-        if (failed) break;
-        phF ^= 1u << (i & 1);
-        inflight &= ~(1u << (i & 1));
+        T5_WAIT(full + (i & 1), (phF >> (i & 1)) & 1);
+        if (!failed) {
+          phF ^= 1u << (i & 1);
+          inflight &= ~(1u << (i & 1));
+        }
         {
           float x[W], y[W];
           read_cols<T, D, W>(KXt, row, sub * W, x);
@@ -826,7 +1068,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         fence_before();
         __syncthreads();
         // projections and dpK = v . dB^T
-        if (tid == 0) {
+        if (tid == 0 && !failed) {
           fence_after();
           if (!(RACE_T5_ABL & 8)) {
           gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
@@ -839,13 +1081,10 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
           }
           commit(barA);
         }
-        if (i > 0) {
-          store_prev(tile0 - TT);
-          if (failed) break;
-        }
-        T5_CHECK(bar_wait(barA, phA));
+        if (i > 0) store_prev(tile0 - TT);
+        T5_WAIT(barA, phA);
         phA ^= 1;
-        if (failed) break;
+        __syncthreads();   // every warp is done with its store scratch (the PK area)
         fence_after();
         {
           float proj[PJ];
@@ -882,7 +1121,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         fence_async_smem();
         fence_before();
         __syncthreads();
-        if (tid == 0) {
+        if (tid == 0 && !failed) {
           fence_after();
           if (!(RACE_T5_ABL & 8)) {
           gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_DV, pk, pk + TT * SP, nullptr, 2, dbt,
@@ -892,8 +1131,10 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
           }
           commit(barB);
         }
+        if (T5_VOTE()) break;
       }
       if (!failed) store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT);
+      T5_VOTE();
     }
     // per-item dscale partial (zero for an empty range), fixed-order CTA sum
     float x = ds;
@@ -911,7 +1152,8 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
   T5_EPILOGUE
 }
 
-#undef T5_CHECK
+#undef T5_WAIT
+#undef T5_VOTE
 #undef T5_PROLOGUE
 #undef T5_EPILOGUE
 
