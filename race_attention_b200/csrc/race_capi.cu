@@ -340,6 +340,7 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
   if (mma_sync && id == K_NC_READOUT) id = K_NC_READOUT_SYNC;
   if (mma_sync && id == K_NC_BWD_KV) id = K_NC_BWD_KV_SYNC;
   if (mma_sync && id == K_NC_REDUCE) id = K_C_TOTALS;
+  if (mma_sync && id == K_NC_BWD_Q) id = K_NC_BWD_Q_SYNC;
   KernelInfo ki;
   const int K = d->num_bits, sp = c.plan.spad;
   bool ok;
@@ -361,12 +362,16 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
     bool ok_map = false;
     if (id == K_NC_READOUT)
       ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, d->head_dim);
+    else if (id == K_NC_BWD_Q)
+      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, d->head_dim) &&
+               encode_map(&maps.map[1], prm.dout, prm.ldo, d->dtype, prm, d->head_dim);
     else if (id == K_NC_BWD_KV || id == K_NC_REDUCE)
       ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, d->head_dim) &&
                encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, d->head_dim);
     if (!ok_map) {   // layouts the copy engine cannot walk: warp-level kernels
       const KernelId alt = id == K_NC_READOUT  ? K_NC_READOUT_SYNC
                            : id == K_NC_BWD_KV ? K_NC_BWD_KV_SYNC
+                           : id == K_NC_BWD_Q  ? K_NC_BWD_Q_SYNC
                                                : K_C_TOTALS;
       return launch(d, c, alt, stream);
     }

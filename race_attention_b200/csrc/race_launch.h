@@ -14,6 +14,7 @@ enum KernelId {
   K_C_BWD_KV,
   K_NC_READOUT_SYNC,   // warp-level mma.sync generation (comparison)
   K_C_TOTALS,          // causal range totals: mma.sync reduce over 32-token tiles
+  K_NC_BWD_Q_SYNC,
   K_NC_BWD_KV_SYNC,
   K_COUNT
 };

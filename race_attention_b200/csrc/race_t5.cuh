@@ -578,12 +578,14 @@ template <int D, int SPAD>
 struct BwdKVLay {
   static constexpr int NTH = RACE_T5_NTH_KV;           // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;    // bucket columns (MMA K and N)
-  static constexpr int KX = 0;                         // [2] slots
-  static constexpr int VX = KX + 2 * Slot<D>::FLOATS;  // [2] slots of three parts
-  static constexpr int PK = VX + 2 * Slot<D, 3>::FLOATS;  // bf16 [TT x SP] hi, then lo
+  static constexpr int KX = 0;                         // [2] k slots (landed, then hi | mid)
+  static constexpr int VX = KX + 2 * Slot<D>::FLOATS;  // [2] v slots (landed, then hi | mid)
+  static constexpr int KL = VX + 2 * Slot<D>::FLOATS;  // bf16 [TT x D] third part of k
+  static constexpr int VL = KL + TT * D / 2;           // bf16 [TT x D] third part of v
+  static constexpr int PK = VL + TT * D / 2;           // bf16 [TT x SP] hi, then lo
   static constexpr int DJ = PK + TT * SP;              // bf16 [TT x PJ] hi, then lo
-  static constexpr int PS = DJ + TT * PJ;              // bf16 [2*PJ x D] planes [hi; lo]
-  static constexpr int PT = PS + PJ * D;               // bf16 [2*D x PJ] planes^T [hi; lo]
+  static constexpr int PS = DJ + TT * PJ;              // bf16 [3*PJ x D] planes [hi; mid; lo]
+  static constexpr int PT = PS + 3 * PJ * D / 2;       // bf16 [2*D x PJ] planes^T [hi; lo]
   static constexpr int DB = PT + D * PJ;               // bf16 [3*SP x D] dB [hi; mid; lo]
   static constexpr int DBT = DB + 3 * SP * D / 2;      // bf16 [2*D x SP] dB^T [hi; lo]
   static constexpr int DA = DBT + D * SP;              // [32] dA
@@ -591,8 +593,9 @@ struct BwdKVLay {
   static constexpr int NFULL = 2;                       // tile-landed barriers
   static constexpr int BAR = RED + 16;                 // mbarriers + TMEM base slot
   static constexpr int FLOATS = BAR + 16 + 256;        // + slack for 1 KB alignment
-  static constexpr int TCOLS = 512;   // PROJ [0,32), DPK [32, 32+3SP), DV [128, 128+2D), DK [256, 256+2D)
-  static constexpr int C_PROJ = 0, C_DPK = 32, C_DV = 128, C_DK = 256;
+  // PROJ [0, 48), DPK [64, 64 + 3SP), DV [160, 160 + 2D), DK [288, 288 + 2D)
+  static constexpr int TCOLS = 512;
+  static constexpr int C_PROJ = 0, C_DPK = 64, C_DV = 160, C_DK = 288;
 };
 
 // A wait that times out sets the CTA's abort word (so the other threads'
@@ -962,6 +965,242 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
   T5_EPILOGUE
 }
 
+// ------------------------------------------------------------------ B1 query backward
+template <int D, int SPAD>
+struct BwdQLay {
+  static constexpr int NTH = RACE_T5_NTH_KV;           // threads per token
+  static constexpr int SP = (SPAD + 15) / 16 * 16;     // bucket columns
+  static constexpr int NFULL = 3;                      // dO slots in rotation
+  static constexpr int QX = 0;                          // [2] q slots (landed, then hi | mid)
+  static constexpr int GX = QX + 2 * Slot<D>::FLOATS;   // [3] dO slots (landed, then hi | lo)
+  static constexpr int QL = GX + 3 * Slot<D>::FLOATS;   // bf16 [TT x D] third part of q
+  static constexpr int PQ = QL + TT * D / 2;            // pQ parts [TT x 2 SP] = [hi | lo]
+  static constexpr int DJ = PQ + TT * SP;               // bf16 [TT x PJ] hi, then lo
+  static constexpr int PS = DJ + TT * PJ;               // bf16 [3*PJ x D] planes [hi; mid; lo]
+  static constexpr int PT = PS + 3 * PJ * D / 2;        // bf16 [2*D x PJ] planes^T [hi; lo]
+  static constexpr int ET = PT + D * PJ;                // bf16 [3*SP x D] E [hi; mid; lo]
+  static constexpr int RED = ET + 3 * SP * D / 2;       // [16] reductions
+  static constexpr int BAR = RED + 16;
+  static constexpr int FLOATS = BAR + 16 + 256;
+  // PROJ [0, 48), DPQ [64, 64 + 3SP), DQ [160, 160 + 2D), DE [384, 384 + 2SP) (M = 64)
+  static constexpr int TCOLS = 512;
+  static constexpr int C_PROJ = 0, C_DPQ = 64, C_DQ = 160, C_DE = 384;
+};
+
+// dq = dproj(pQ, dO . E^T) . P per token; per range the partial dE[s][d] =
+// sum_t pQ[t][s] dO[t][d] (accumulated over the range's tiles in tensor memory,
+// M = 64 rows of d, dO and pQ read MN-major) and the q-side dscale.
+template <typename T, int D, int SPAD, int K>
+__global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
+    k_t5_bwd_q(const Params prm, const __grid_constant__ TmaMaps maps) {
+  using LY = BwdQLay<D, SPAD>;
+  constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
+  using G = Groups<K>;
+  constexpr bool F32 = sizeof(T) == 4;
+  T5_PROLOGUE
+  bf16* pq = reinterpret_cast<bf16*>(sm + LY::PQ);
+  bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
+  bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
+  bf16* pt = reinterpret_cast<bf16*>(sm + LY::PT);
+  bf16* et = reinterpret_cast<bf16*>(sm + LY::ET);
+  // planes of DJ not covered by any bucket group stay zero
+  for (int i = tid; i < TT * PJ; i += NTHR) reinterpret_cast<float*>(dj)[i] = 0.f;
+  for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
+    const Item it = item_of(prm, w);
+    const int n = it.n;
+    float* dst = prm.part + ((size_t)n * prm.P + it.part) * prm.SS;
+    float ds = 0.f;
+    if (it.ntiles > 0) {
+      const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
+      __syncthreads();
+      if (m != cur_m) {
+        const float* pl = prm.planes + (size_t)m * prm.LK * D;
+        put_stack<PJ, D, 3, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+        put_stack<D, PJ, 2, NTHR>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+        cur_m = m;
+      }
+      if (n != cur_n) {
+        const float* st = prm.state + (size_t)n * prm.SS;
+        const float* mass = st + prm.S * D;
+        // E in three parts: dpQ cancels against its bucket average where a
+        // bucket's means are nearly equal
+        put_stack<SP, D, 3, NTHR>(et, [&](int sidx, int d) {
+          return sidx < prm.S ? st[sidx * D + d] / (mass[sidx] + prm.eps) : 0.f;
+        });
+        cur_n = n;
+      }
+      __syncthreads();
+      T* dqb = static_cast<T*>(prm.dq) + stream_offset(prm.ldq, n, prm.B, prm.H);
+      float* scratch = sm + LY::PQ + warp * 384;   // store_rows scratch (PQ is free then)
+      auto store_prev = [&](int64_t tprev) {
+        T5_WAIT(barB, phB);
+        phB ^= 1;
+        fence_after();
+        float o[W];
+        tld_sum<W>(tlane + LY::C_DQ + sub * W, D, o);
+        if (!failed)
+          store_rows<T, W>(dqb, prm.ldq.st, tprev + (warp & 3) * 32, it.t1, sub * W, o, scratch);
+        fence_before();
+      };
+      auto load = [&](int j) {
+        if (failed) return;
+        inflight |= 1u << (j % 3);
+        if (tid == 0) {
+          float* const dsts[2] = {sm + LY::QX + (j & 1) * Slot<D>::FLOATS,
+                                  sm + LY::GX + (j % 3) * Slot<D>::FLOATS};
+          const Layout* const lay[2] = {&prm.lq, &prm.ldo};
+          tma_tile<T, D, 2>(maps, dsts, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j % 3));
+        }
+      };
+      // Per tile i: q, dO parts -> MMA proj, dpQ (i) || store dq(i-1) -> hash
+      // backward(i) -> MMA dE += dO^T pQ, dq (i) || next tile
+      load(0);
+      for (int i = 0; i < it.ntiles; ++i) {
+        const int64_t tile0 = it.t0 + (int64_t)i * TT;
+        float* QXt = sm + LY::QX + (i & 1) * Slot<D>::FLOATS;
+        float* GXt = sm + LY::GX + (i % 3) * Slot<D>::FLOATS;
+        bf16* ql = reinterpret_cast<bf16*>(sm + LY::QL);
+        if (i + 1 < it.ntiles) load(i + 1);
+        T5_WAIT(full + (i % 3), (phF >> (i % 3)) & 1);
+        if (!failed) {
+          phF ^= 1u << (i % 3);
+          inflight &= ~(1u << (i % 3));
+        }
+        const bool valid = tile0 + row < it.t1;
+        {
+          float x[W], y[W];
+          read_cols<T, D, W>(QXt, row, sub * W, x);
+          read_cols<T, D, W>(GXt, row, sub * W, y);
+          if (!valid) {   // rows past the range add nothing to dE
+#pragma unroll
+            for (int c = 0; c < W; ++c) y[c] = 0.f;
+          }
+          __syncthreads();
+          // hi | mid in place, the third part beside (read only by this tile's
+          // projection MMAs, which finish before the next conversion)
+          put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(QXt, 0), Slot<D>::part(QXt, 1), ql, row,
+                                      sub * W, x);
+          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1), nullptr, row,
+                                      sub * W, y);
+        }
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          fence_after();
+          // projections in three parts on both sides: they feed the
+          // temperature gradient, a sum with heavy cancellation
+          gemm_parts<PJ, 3, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(QXt, 0),
+                                          Slot<D>::part(QXt, 1), ql, F32 ? 3 : 1, ps, false);
+          gemm_parts<SP, 3, D / 16, D, D>(tbase + LY::C_DPQ, Slot<D>::part(GXt, 0),
+                                          Slot<D>::part(GXt, 1), nullptr, F32 ? 2 : 1, et, false);
+          commit(barA);
+        }
+        if (i > 0) store_prev(tile0 - TT);
+        T5_WAIT(barA, phA);
+        phA ^= 1;
+        __syncthreads();   // every warp is done with its store scratch (the PQ area)
+        fence_after();
+        {
+          float proj[PJ];
+          tld_sum<PJ, 3>(tlane + LY::C_PROJ, PJ, proj);
+#pragma unroll
+          for (int gi = 0; gi < SP / G::GB; ++gi) {
+            if (gi % NTH == sub) {
+              float p[G::GB], h[G::GK], g[G::GB], dj_[G::GK];
+              const bool has = gi * G::GK < PJ;
+              group_probs<K>(has ? proj + gi * G::GK : proj, gi * G::GT, has ? L : 0, inv_scale, p,
+                             h);
+              tld_sum<G::GB, 3>(tlane + LY::C_DPQ + gi * G::GB, SP, g);
+              float dsl = 0.f;
+              group_probs_bwd<K>(p, g, h, inv_scale, dj_, dsl);
+              if (valid) ds += dsl;
+              if (!valid) {
+#pragma unroll
+                for (int b = 0; b < G::GB; ++b) p[b] = 0.f;
+              }
+              // one row of [hi | lo] bucket blocks
+#pragma unroll
+              for (int c8 = 0; c8 < G::GB / 8; ++c8) {
+                uint4 hq, lq;
+                split2(p[8 * c8 + 0], p[8 * c8 + 1], hq.x, lq.x);
+                split2(p[8 * c8 + 2], p[8 * c8 + 3], hq.y, lq.y);
+                split2(p[8 * c8 + 4], p[8 * c8 + 5], hq.z, lq.z);
+                split2(p[8 * c8 + 6], p[8 * c8 + 7], hq.w, lq.w);
+                uint4* q4 = reinterpret_cast<uint4*>(pq);
+                const int c0 = gi * G::GB / 8 + c8;
+                q4[chunk<2 * SP>(row, c0)] = hq;
+                q4[chunk<2 * SP>(row, SP / 8 + c0)] = lq;
+              }
+              if (has) {
+#pragma unroll
+                for (int j = 0; j < G::GK; ++j) {
+                  const int jj = gi * G::GK + j;
+                  if (jj < PJ) {
+                    const bf16 hb = __float2bfloat16_rn(dj_[j]);
+                    dj[elem<PJ>(row, jj)] = hb;
+                    dj[TT * PJ + elem<PJ>(row, jj)] = __float2bfloat16_rn(dj_[j] - __bfloat162float(hb));
+                  }
+                }
+              }
+            }
+          }
+        }
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          fence_after();
+          // dE^T[d][s-block j] += sum_a dO_a^T . pQ_j (MN-major over the tile's tokens)
+#pragma unroll
+          for (int a = 0; a < (F32 ? 2 : 1); ++a)
+#pragma unroll
+            for (int ks = 0; ks < TT / 16; ++ks)
+              mma(tbase + LY::C_DE, desc_mn<D>(Slot<D>::part(GXt, a), ks), desc_mn<2 * SP>(pq, ks),
+                  idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
+          gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DQ, dj, dj + TT * PJ, nullptr, 2, pt,
+                                            false);
+          commit(barB);
+        }
+        if (T5_VOTE()) break;
+      }
+      if (!failed) store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT);
+      if (T5_VOTE()) break;
+      fence_after();
+      // dE: lane 32 q + l (l < 16) of warps 0..3 holds row d = 16 q + l
+      if (sub == 0) {
+        float e[2 * SP];
+#pragma unroll
+        for (int c = 0; c < 2 * SP; c += 8) tld8(tlane + LY::C_DE + c, e + c);
+        tld_wait();
+        const int l = tid & 31, d = 16 * (warp & 3) + l;
+        if (l < 16 && d < D) {
+#pragma unroll
+          for (int sidx = 0; sidx < SP; ++sidx)
+            if (sidx < prm.S) dst[sidx * D + d] = e[sidx] + e[SP + sidx];
+        }
+      }
+      fence_before();
+      for (int e2 = tid; e2 < prm.S; e2 += NTHR) dst[prm.S * D + e2] = 0.f;
+    } else {
+      for (int e2 = tid; e2 < prm.S * D + prm.S; e2 += NTHR) dst[e2] = 0.f;
+    }
+    // per-item dscale partial (zero for an empty range), fixed-order CTA sum
+    float x = ds;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    __syncthreads();
+    if ((tid & 31) == 0) sm[LY::RED + warp] = x;
+    __syncthreads();
+    if (tid == 0) {
+      float tot = 0.f;
+      for (int i = 0; i < NTHR / 32; ++i) tot += sm[LY::RED + i];
+      prm.dscale_part[(size_t)n * prm.P + it.part] = tot;
+    }
+  }
+  T5_EPILOGUE
+}
+
 // ------------------------------------------------------------------ B2 key/value backward
 // dv = pK . dB,  dpK = v . dB^T + dA,  dk = dproj(pK, dpK) . P;  the k-side dscale.
 template <typename T, int D, int SPAD, int K>
@@ -989,7 +1228,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
       __syncthreads();
       if (m != cur_m) {
         const float* pl = prm.planes + (size_t)m * prm.LK * D;
-        put_stack<PJ, D, 2, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+        put_stack<PJ, D, 3, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
         put_stack<D, PJ, 2, NTHR>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
         cur_m = m;
       }
@@ -1038,7 +1277,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         inflight |= 1u << (j & 1);
         if (tid == 0) {
           float* const dst[2] = {sm + LY::KX + (j & 1) * Slot<D>::FLOATS,
-                                 sm + LY::VX + (j & 1) * Slot<D, 3>::FLOATS};
+                                 sm + LY::VX + (j & 1) * Slot<D>::FLOATS};
           const Layout* const lay[2] = {&prm.lk, &prm.lv};
           tma_tile<T, D, 2>(maps, dst, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j & 1));
         }
@@ -1047,7 +1286,9 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
       for (int i = 0; i < it.ntiles; ++i) {
         const int64_t tile0 = it.t0 + (int64_t)i * TT;
         float* KXt = sm + LY::KX + (i & 1) * Slot<D>::FLOATS;
-        float* VXt = sm + LY::VX + (i & 1) * Slot<D, 3>::FLOATS;
+        float* VXt = sm + LY::VX + (i & 1) * Slot<D>::FLOATS;
+        bf16* kl = reinterpret_cast<bf16*>(sm + LY::KL);
+        bf16* vl = reinterpret_cast<bf16*>(sm + LY::VL);
         if (i + 1 < it.ntiles) load(i + 1);
         T5_WAIT(full + (i & 1), (phF >> (i & 1)) & 1);
         if (!failed) {
@@ -1059,10 +1300,12 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
           read_cols<T, D, W>(KXt, row, sub * W, x);
           read_cols<T, D, W>(VXt, row, sub * W, y);
           __syncthreads();
-          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), nullptr, row,
+          // hi | mid in place, the third part beside (read only by this tile's
+          // projection / dpK MMAs, which finish before the next conversion)
+          put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), kl, row,
                                       sub * W, x);
-          put_cols<D, W, F32 ? 3 : 1>(Slot<D, 3>::part(VXt, 0), Slot<D, 3>::part(VXt, 1),
-                                      Slot<D, 3>::part(VXt, 2), row, sub * W, y);
+          put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), vl, row,
+                                      sub * W, y);
         }
         fence_async_smem();
         fence_before();
@@ -1071,13 +1314,13 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         if (tid == 0 && !failed) {
           fence_after();
           if (!(RACE_T5_ABL & 8)) {
-          gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
-                                          Slot<D>::part(KXt, 1), nullptr, F32 ? 2 : 1, ps, false);
-          // dpK carries three parts on both sides: where v matches a bucket's
-          // mean (tiny buckets), v . dB and dA cancel to far below |v| |dB|
-          gemm_parts<SP, 3, D / 16, D, D>(tbase + LY::C_DPK, Slot<D, 3>::part(VXt, 0),
-                                          Slot<D, 3>::part(VXt, 1), Slot<D, 3>::part(VXt, 2),
-                                          F32 ? 3 : 1, db, false);
+          // three parts on both sides: the projections feed the temperature
+          // gradient (a sum with heavy cancellation), and where v matches a
+          // bucket's mean (tiny buckets) v . dB and dA cancel to far below |v| |dB|
+          gemm_parts<PJ, 3, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
+                                          Slot<D>::part(KXt, 1), kl, F32 ? 3 : 1, ps, false);
+          gemm_parts<SP, 3, D / 16, D, D>(tbase + LY::C_DPK, Slot<D>::part(VXt, 0),
+                                          Slot<D>::part(VXt, 1), vl, F32 ? 3 : 1, db, false);
           }
           commit(barA);
         }
@@ -1088,7 +1331,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         fence_after();
         {
           float proj[PJ];
-          tld_sum<PJ>(tlane + LY::C_PROJ, PJ, proj);
+          tld_sum<PJ, 3>(tlane + LY::C_PROJ, PJ, proj);
           const bool valid = tile0 + row < it.t1;
 #pragma unroll
           for (int gi = 0; gi < SP / G::GB; ++gi) {
