@@ -199,6 +199,21 @@ class Layer:
                 "backward_kv": 4 * e}
 
 
+# Measured DRAM bytes (read + write) of the dominant phase's main kernel per
+# launch at 2^18 tokens, from
+#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#       --clock-control none python bench.py --steps 2 --warmup 3 --no-e2e --no-cpu
+#       --tokens 262144
+TRAFFIC_2P18 = {
+    (False, "f32", "backward_kv"): 225.8e6,
+    (False, "f32", "backward_q"): 171.6e6,
+    (False, "bf16", "backward_kv"): 89.4e6,
+    (False, "bf16", "backward_q"): 73.3e6,
+    (True, "f32", "backward_kv"): 396.3e6,
+    (True, "bf16", "backward_kv"): 197.7e6,
+}
+
+
 def timed(fn, steps, warmup, group, device):
     for _ in range(warmup):
         fn()
@@ -335,9 +350,16 @@ def run_ours(args):
             rec["phases_ms"] = ph
             dom = max(ph, key=ph.get)
             ach = pb[dom] * args.tokens / (ph[dom] / 1e3) / 1e9
+            tr = TRAFFIC_2P18.get((causal, rec["dtype"], dom))
             rec["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak,
-                               "unit": "GB/s", "frac": ach / peak, "traffic": None,
+                               "unit": "GB/s", "frac": ach / peak,
+                               "traffic": None if tr is None else tr * args.tokens / 2 ** 18,
                                "peak_kind": peak_kind}
+            if tr is not None:
+                rec["roofline"]["traffic_note"] = (
+                    "DRAM read+write bytes per launch from one ncu capture at 2^18 tokens, "
+                    "scaled by tokens; reads equal the algorithmic bytes, writes of the last "
+                    "tiles are still in L2 when a launch ends")
         rec["gpu_launches_per_step"] = layer.kernels_per_step()
         results.append(rec)
         if i == 0:
