@@ -360,14 +360,22 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
   std::memset(&maps, 0, sizeof(maps));
   if (ki.tma > 0) {
     bool ok_map = false;
+    const int hd = d->head_dim;
     if (id == K_NC_READOUT)
-      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, d->head_dim);
+      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, hd) &&
+               encode_map(&maps.map[1], prm.out, prm.lo, d->dtype, prm, hd);
     else if (id == K_NC_BWD_Q)
-      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, d->head_dim) &&
-               encode_map(&maps.map[1], prm.dout, prm.ldo, d->dtype, prm, d->head_dim);
-    else if (id == K_NC_BWD_KV || id == K_NC_REDUCE)
-      ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, d->head_dim) &&
-               encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, d->head_dim);
+      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, hd) &&
+               encode_map(&maps.map[1], prm.dout, prm.ldo, d->dtype, prm, hd) &&
+               encode_map(&maps.map[2], prm.dq, prm.ldq, d->dtype, prm, hd);
+    else if (id == K_NC_BWD_KV)
+      ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, hd) &&
+               encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, hd) &&
+               encode_map(&maps.map[2], prm.dk, prm.ldk, d->dtype, prm, hd) &&
+               encode_map(&maps.map[3], prm.dv, prm.ldv, d->dtype, prm, hd);
+    else if (id == K_NC_REDUCE)
+      ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, hd) &&
+               encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, hd);
     if (!ok_map) {   // layouts the copy engine cannot walk: warp-level kernels
       const KernelId alt = id == K_NC_READOUT  ? K_NC_READOUT_SYNC
                            : id == K_NC_BWD_KV ? K_NC_BWD_KV_SYNC

@@ -63,11 +63,12 @@ struct Params {
 
 __host__ __device__ constexpr int round_up(int a, int b) { return (a + b - 1) / b * b; }
 
-// TMA descriptors of a kernel's streamed inputs (encoded per call on the host;
-// a __grid_constant__ kernel parameter).  Each maps a [M, B, T, H, D] tensor
-// as 5-D (D, T, H, B, M) with 128-row boxes.
+// TMA descriptors of a kernel's streamed inputs and outputs (encoded per call
+// on the host; a __grid_constant__ kernel parameter).  Each maps a
+// [M, B, T, H, D] tensor as 5-D (D, T, H, B, M) with 128-row boxes; maps 0-1
+// are inputs, 2-3 outputs.
 struct TmaMaps {
-  CUtensorMap map[2];
+  CUtensorMap map[4];
 };
 
 // ---------------------------------------------------------------- row I/O

@@ -346,6 +346,65 @@ __device__ __forceinline__ void read_cols(const void* tile, int r, int c0, float
   }
 }
 
+// Writes columns [c0, c0 + W) of row r into a tile in the box layout (the
+// inverse of read_cols), for a TMA store.
+template <typename T, int D, int W>
+__device__ __forceinline__ void put_tile_cols(void* tile, int r, int c0, const float* v) {
+  using BX = Box<T, D>;
+  constexpr int EPC = 16 / (int)sizeof(T);
+  char* base = static_cast<char*>(tile);
+#pragma unroll
+  for (int i = 0; i < W / EPC; ++i) {
+    const int gc = c0 / EPC + i;
+    const int bx = gc / (BX::IB / 16), c = gc % (BX::IB / 16);
+    const int pc = BX::SWZ ? (c ^ (r & 7)) : c;
+    uint4 u;
+    if constexpr (sizeof(T) == 4) {
+      u = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]),
+                     __float_as_uint(v[4 * i + 2]), __float_as_uint(v[4 * i + 3]));
+    } else {
+      uint32_t* up = &u.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+        up[j] = *reinterpret_cast<const uint32_t*>(&b2);
+      }
+    }
+    *reinterpret_cast<uint4*>(base + bx * TT * BX::IB + r * BX::IB + pc * 16) = u;
+  }
+}
+
+__device__ __forceinline__ void tma_store5(const CUtensorMap* map, const void* src, int c0, int c1,
+                                           int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5, %6}], "
+      "[%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(saddr(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory sources of this thread's bulk stores may be reused
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// this thread's bulk stores are complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// One thread: stores a staged tile (box layout) to rows [t0, t0 + TT) of
+// stream n of a mapped output.  Ranges are whole tiles, so only the tensor's
+// last tile is ragged, and the copy engine clips rows past its end.
+template <typename T, int D>
+__device__ __forceinline__ void tma_store_tile(const CUtensorMap* map, const void* tile,
+                                               const Layout& lay, const Params& prm, int n,
+                                               int64_t t0) {
+  using BX = Box<T, D>;
+  const int h = n % prm.H, b = (n / prm.H) % prm.B, m = n / (prm.H * prm.B);
+#pragma unroll
+  for (int x = 0; x < BX::NB; ++x)
+    tma_store5(map, static_cast<const char*>(tile) + x * TT * BX::IB, x * BX::IB / (int)sizeof(T),
+               (int)t0, h, b, lay.sm == 0 ? 0 : m);
+}
+
 // Writes W values (columns [c0, c0 + W), W and c0 multiples of 8) of row r
 // as NP bf16 parts into operands p0 (, p1, p2) with C columns (NP = 1: the
 // values are exact in bf16).
@@ -510,54 +569,6 @@ struct Slot {
   __device__ static bf16* part(float* s, int i) { return reinterpret_cast<bf16*>(s) + i * TT * D; }
 };
 
-// Coalesced row stores through a warp-private scratch (32 rows x 48 B): the
-// warp's lanes hold rows r0 + lane, columns [c0, c0 + W) each; every pass
-// moves 32 B of each row, written as 16 rows x 32 B per store instruction.
-template <typename T, int W>
-__device__ __forceinline__ void store_rows(T* base, int64_t st, int64_t r0, int64_t t1, int c0,
-                                           const float* v, float* scratch) {
-  constexpr int EP = 32 / (int)sizeof(T);   // elements per pass per row
-  const int lane = threadIdx.x & 31;
-  if constexpr (W < EP) {   // a 16-byte slice per row: store it directly
-    static_assert(W * sizeof(T) == 16, "slice of 16 bytes");
-    (void)scratch;
-    if (r0 + lane < t1) store_cols<T, W>(base + (r0 + lane) * st + c0, v);
-    return;
-  }
-#pragma unroll
-  for (int ps = 0; ps < W / EP; ++ps) {
-    uint4* sc = reinterpret_cast<uint4*>(scratch);
-    if constexpr (sizeof(T) == 4) {
-      float4* sf = reinterpret_cast<float4*>(scratch);
-      sf[lane * 3] = make_float4(v[ps * 8 + 0], v[ps * 8 + 1], v[ps * 8 + 2], v[ps * 8 + 3]);
-      sf[lane * 3 + 1] = make_float4(v[ps * 8 + 4], v[ps * 8 + 5], v[ps * 8 + 6], v[ps * 8 + 7]);
-    } else {
-      uint4 a, b;
-      uint32_t* pa = &a.x;
-      uint32_t* pb = &b.x;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        __nv_bfloat162 x = __floats2bfloat162_rn(v[ps * 16 + 2 * j], v[ps * 16 + 2 * j + 1]);
-        __nv_bfloat162 y = __floats2bfloat162_rn(v[ps * 16 + 8 + 2 * j], v[ps * 16 + 9 + 2 * j]);
-        pa[j] = *reinterpret_cast<uint32_t*>(&x);
-        pb[j] = *reinterpret_cast<uint32_t*>(&y);
-      }
-      sc[lane * 3] = a;
-      sc[lane * 3 + 1] = b;
-    }
-    __syncwarp();
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int rr = h * 16 + (lane >> 1);
-      const uint4 u = sc[rr * 3 + (lane & 1)];
-      const int64_t t = r0 + rr;
-      if (t < t1)
-        *reinterpret_cast<uint4*>(base + t * st + c0 + ps * EP + (lane & 1) * (EP / 2)) = u;
-    }
-    __syncwarp();
-  }
-}
-
 // ------------------------------------------------------------------ layouts (in floats)
 template <int D, int SPAD>
 struct ReadoutLay {
@@ -642,6 +653,7 @@ struct BwdKVLay {
   int cur_n = -1, cur_m = -1;
 
 #define T5_EPILOGUE                                                          \
+  if (tid == 0) bulk_wait_all();                                             \
   for (int s_ = 0; s_ < LY::NFULL; ++s_)                                     \
     if ((inflight >> s_) & 1) bar_wait(full + s_, (phF >> s_) & 1);          \
   if (tid == 0 && *abort_flag != 0) atomicOr(prm.err, kErrTimeout);          \
@@ -681,24 +693,28 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       });
       cur_n = n;
     }
-    T* ob = static_cast<T*>(prm.out) + stream_offset(prm.lo, n, prm.B, prm.H);
-    // Pipeline per tile i: load(i+1) | convert(i) -> MMA proj(i) || store(i-1)
-    // -> probabilities(i) -> MMA out(i) || next tile ...
-    float* scratch = sm + LY::PQ + warp * 384;   // store_rows scratch (PQ is free then)
-    auto store_prev = [&](int64_t tprev) {
+    // Pipeline per tile i: load(i+1) | convert(i) -> MMA proj(i) -> store(i-1)
+    // through slot i (its parts are consumed) -> probabilities(i) -> MMA out(i)
+    auto store_prev = [&](int64_t tprev, float* stage_slot) {
       T5_WAIT(barB, phB);
       phB ^= 1;
       fence_after();
       float o[W];
       tld_sum<W>(tlane + LY::C_OUT + sub * W, D, o);
-      if (!failed)
-        store_rows<T, W>(ob, prm.lo.st, tprev + (warp & 3) * 32, it.t1, sub * W, o, scratch);
+      put_tile_cols<T, D, W>(stage_slot, row, sub * W, o);
+      fence_async_smem();
       fence_before();
+      __syncthreads();
+      if (tid == 0 && !failed) {
+        tma_store_tile<T, D>(&maps.map[1], stage_slot, prm.lo, prm, n, tprev);
+        bulk_commit();
+      }
     };
     auto load = [&](int j) {
       if (failed) return;
       inflight |= 1u << (j & 1);
       if (tid == 0) {
+        bulk_wait_read();   // a store may still be reading this slot
         float* const dst[1] = {sm + LY::QX + (j & 1) * Slot<D>::FLOATS};
         const Layout* const lay[1] = {&prm.lq};
         tma_tile<T, D, 1>(maps, dst, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j & 1));
@@ -730,10 +746,9 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
                                         Slot<D>::part(X, 1), nullptr, F32 ? 2 : 1, ps, false);
         commit(barA);
       }
-      if (i > 0) store_prev(tile0 - TT);
-      T5_WAIT(barA, phA);
+      T5_WAIT(barA, phA);   // also covers the previous tile's output MMAs
       phA ^= 1;
-      __syncthreads();   // every warp is done with its store scratch (the PQ area)
+      if (i > 0) store_prev(tile0 - TT, X);
       fence_after();
       {
         float proj[PJ];
@@ -760,7 +775,9 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       }
       if (T5_VOTE()) break;
     }
-    if (!failed) store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT);
+    if (!failed)
+      store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT,
+                 sm + LY::QX + ((it.ntiles - 1) & 1) * Slot<D>::FLOATS);
     T5_VOTE();
   }
   T5_EPILOGUE
@@ -802,6 +819,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
   constexpr int MYG = (NG + NTH - 1) / NTH;            // groups per thread (at most)
   constexpr bool F32 = sizeof(T) == 4;
   T5_PROLOGUE
+  (void)cur_n;
   bf16* vp = reinterpret_cast<bf16*>(sm + LY::VP);
   bf16* pk3 = reinterpret_cast<bf16*>(sm + LY::PK3);
   bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
@@ -1030,22 +1048,27 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
         cur_n = n;
       }
       __syncthreads();
-      T* dqb = static_cast<T*>(prm.dq) + stream_offset(prm.ldq, n, prm.B, prm.H);
-      float* scratch = sm + LY::PQ + warp * 384;   // store_rows scratch (PQ is free then)
-      auto store_prev = [&](int64_t tprev) {
+      // dq of tile i-1 leaves through q slot i (its parts are consumed by then)
+      auto store_prev = [&](int64_t tprev, float* stage_slot) {
         T5_WAIT(barB, phB);
         phB ^= 1;
         fence_after();
         float o[W];
         tld_sum<W>(tlane + LY::C_DQ + sub * W, D, o);
-        if (!failed)
-          store_rows<T, W>(dqb, prm.ldq.st, tprev + (warp & 3) * 32, it.t1, sub * W, o, scratch);
+        put_tile_cols<T, D, W>(stage_slot, row, sub * W, o);
+        fence_async_smem();
         fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          tma_store_tile<T, D>(&maps.map[2], stage_slot, prm.ldq, prm, n, tprev);
+          bulk_commit();
+        }
       };
       auto load = [&](int j) {
         if (failed) return;
         inflight |= 1u << (j % 3);
         if (tid == 0) {
+          bulk_wait_read();   // a store may still be reading the q slot
           float* const dsts[2] = {sm + LY::QX + (j & 1) * Slot<D>::FLOATS,
                                   sm + LY::GX + (j % 3) * Slot<D>::FLOATS};
           const Layout* const lay[2] = {&prm.lq, &prm.ldo};
@@ -1096,10 +1119,9 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
                                           Slot<D>::part(GXt, 1), nullptr, F32 ? 2 : 1, et, false);
           commit(barA);
         }
-        if (i > 0) store_prev(tile0 - TT);
-        T5_WAIT(barA, phA);
+        T5_WAIT(barA, phA);   // also covers the previous tile's dE / dq MMAs
         phA ^= 1;
-        __syncthreads();   // every warp is done with its store scratch (the PQ area)
+        if (i > 0) store_prev(tile0 - TT, QXt);
         fence_after();
         {
           float proj[PJ];
@@ -1164,7 +1186,9 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
         }
         if (T5_VOTE()) break;
       }
-      if (!failed) store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT);
+      if (!failed)
+        store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT,
+                   sm + LY::QX + ((it.ntiles - 1) & 1) * Slot<D>::FLOATS);
       if (T5_VOTE()) break;
       fence_after();
       // dE: lane 32 q + l (l < 16) of warps 0..3 holds row d = 16 q + l
@@ -1255,27 +1279,34 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         cur_n = n;
       }
       __syncthreads();
-      T* dkb = static_cast<T*>(prm.dk) + stream_offset(prm.ldk, n, prm.B, prm.H);
-      T* dvb = static_cast<T*>(prm.dv) + stream_offset(prm.ldv, n, prm.B, prm.H);
       // Pipeline per tile i: load(i+1) | convert(i) -> MMA proj, dpK (i) ||
       // store(i-1) -> hash backward(i) -> MMA dv, dk (i) || next tile ...
-      float* scratch = sm + LY::PK + warp * 384;   // store_rows scratch (PK, DJ free then)
-      auto store_prev = [&](int64_t tprev) {
+      // dv, dk of tile i-1 leave through k, v slots i (their parts are consumed)
+      auto store_prev = [&](int64_t tprev, float* stage_k, float* stage_v) {
         T5_WAIT(barB, phB);
         phB ^= 1;
         fence_after();
-        const int64_t r0 = tprev + (warp & 3) * 32;
-        float o[W];
-        tld_sum<W>(tlane + LY::C_DV + sub * W, D, o);
-        if (!failed) store_rows<T, W>(dvb, prm.ldv.st, r0, it.t1, sub * W, o, scratch);
-        tld_sum<W>(tlane + LY::C_DK + sub * W, D, o);
-        if (!failed) store_rows<T, W>(dkb, prm.ldk.st, r0, it.t1, sub * W, o, scratch);
+        if (!(RACE_T5_ABL & 4)) {
+          float o[W];
+          tld_sum<W>(tlane + LY::C_DV + sub * W, D, o);
+          put_tile_cols<T, D, W>(stage_k, row, sub * W, o);
+          tld_sum<W>(tlane + LY::C_DK + sub * W, D, o);
+          put_tile_cols<T, D, W>(stage_v, row, sub * W, o);
+        }
+        fence_async_smem();
         fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed && !(RACE_T5_ABL & 4)) {
+          tma_store_tile<T, D>(&maps.map[3], stage_k, prm.ldv, prm, n, tprev);
+          tma_store_tile<T, D>(&maps.map[2], stage_v, prm.ldk, prm, n, tprev);
+          bulk_commit();
+        }
       };
       auto load = [&](int j) {
         if (failed) return;
         inflight |= 1u << (j & 1);
         if (tid == 0) {
+          bulk_wait_read();   // stores may still be reading these slots
           float* const dst[2] = {sm + LY::KX + (j & 1) * Slot<D>::FLOATS,
                                  sm + LY::VX + (j & 1) * Slot<D>::FLOATS};
           const Layout* const lay[2] = {&prm.lk, &prm.lv};
@@ -1302,10 +1333,12 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
           __syncthreads();
           // hi | mid in place, the third part beside (read only by this tile's
           // projection / dpK MMAs, which finish before the next conversion)
+          if (!(RACE_T5_ABL & 1)) {
           put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), kl, row,
                                       sub * W, x);
           put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), vl, row,
                                       sub * W, y);
+          }
         }
         fence_async_smem();
         fence_before();
@@ -1324,10 +1357,9 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
           }
           commit(barA);
         }
-        if (i > 0) store_prev(tile0 - TT);
-        T5_WAIT(barA, phA);
+        T5_WAIT(barA, phA);   // also covers the previous tile's dv / dk MMAs
         phA ^= 1;
-        __syncthreads();   // every warp is done with its store scratch (the PK area)
+        if (i > 0) store_prev(tile0 - TT, KXt, VXt);
         fence_after();
         {
           float proj[PJ];
@@ -1376,7 +1408,11 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         }
         if (T5_VOTE()) break;
       }
-      if (!failed) store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT);
+      if (!failed) {
+        const int lt = (it.ntiles - 1) & 1;
+        store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT, sm + LY::KX + lt * Slot<D>::FLOATS,
+                   sm + LY::VX + lt * Slot<D>::FLOATS);
+      }
       T5_VOTE();
     }
     // per-item dscale partial (zero for an empty range), fixed-order CTA sum
