@@ -256,11 +256,16 @@ def phase_times(layer, steps, device):
     return {n: acc[n] / steps for n in names}
 
 
-def e2e_rate(causal, dtype, tokens, steps, device):
+def e2e_rate(causal, dtype, tokens, steps, device, group=None):
     """Same metric through the public autograd API with pinned HOST buffers:
-    H2D of q, k, v, dO and D2H of out, dq, dk, dv inside the timed region."""
+    H2D of q, k, v, dO and D2H of out, dq, dk, dv inside the timed region.
+    Every rank runs its own shard of the sequence (race_attention(...,
+    group=...)); the time is taken with CUDA events on the launching stream
+    (the copies are on it) and the maximum over ranks is used."""
     from race_attention_b200 import race_attention
-    g = torch.Generator().manual_seed(1)
+    world = 1 if group is None else torch.distributed.get_world_size(group)
+    rank = 0 if group is None else torch.distributed.get_rank(group)
+    g = torch.Generator().manual_seed(1 + rank)
     shape = (1, tokens, 1, D)
     host = [torch.randn(shape, generator=g).to(dtype).pin_memory() for _ in range(4)]
     outs = [torch.empty(shape, dtype=dtype).pin_memory() for _ in range(4)]
@@ -271,22 +276,18 @@ def e2e_rate(causal, dtype, tokens, steps, device):
         q, k, v, do = (h.to(device, non_blocking=True) for h in host)
         for t in (q, k, v):
             t.requires_grad_(True)
-        out = race_attention(q, k, v, planes, K, L, lt.exp().clamp(1e-2, 20.0), causal=causal)
+        out = race_attention(q, k, v, planes, K, L, lt.exp().clamp(1e-2, 20.0), causal=causal,
+                             group=group)
         out.backward(do)
         for dst, src in zip(outs, (out, q.grad, k.grad, v.grad)):
             dst.copy_(src.detach(), non_blocking=True)
         lt.grad = None
 
     step()
-    torch.cuda.synchronize(device)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        step()
-    torch.cuda.synchronize(device)
-    dt = (time.perf_counter() - t0) / steps
+    dt = timed(step, steps, 0, group, device) / 1e3
     nbytes = tokens * D * torch.tensor([], dtype=dtype).element_size() * 4
-    return {"value": tokens / dt, "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
-            "d2h_bytes_per_step": nbytes, "steps": steps}
+    return {"value": world * tokens / dt, "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
+            "d2h_bytes_per_step": nbytes, "steps": steps, "per_rank_shard_tokens": tokens}
 
 
 def cpu_rate(causal, tokens, budget_s=10.0, iters_max=50):
@@ -389,8 +390,8 @@ def run_ours(args):
         line["phases_ms"] = rec["phases_ms"]
     del layer
     torch.cuda.empty_cache()
-    if rank == 0 and not args.no_e2e:
-        line["e2e"] = e2e_rate(False, torch.float32, args.tokens, args.e2e_steps, device)
+    if not args.no_e2e:
+        line["e2e"] = e2e_rate(False, torch.float32, args.tokens, args.e2e_steps, device, group)
     if world > 1:
         torch.distributed.barrier()
     if rank == 0 and not args.no_cpu and world == 1:

@@ -130,3 +130,27 @@ def test_chunk_length_independent():
     b = run_streams(q, k, v, planes, K, L, 1.0, True, dout, chunk=1024)
     for x, y in zip(a[:4], b[:4]):
         assert O.rel_l2(x, y) < 1e-5
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
+def test_broadcast_batch_layout(causal):
+    """A batch axis broadcast with stride 0 (one sequence shared by two batch
+    rows) cannot be walked by the copy engine's tensor maps; the library then
+    runs the warp-level kernels.  Results must equal two explicit copies."""
+    from race_attention_b200 import race_attention
+    dev = "cuda"
+    g = torch.Generator().manual_seed(5)
+    T, d, K, L = 700, 64, 2, 5
+    base = [torch.randn(1, T, 1, d, generator=g) for _ in range(3)]
+    planes = torch.randn(1, K * L, d, generator=g).to(dev)
+    dout = torch.randn(2, T, 1, d, generator=g).to(dev)
+    scale = torch.tensor(1.1, device=dev)
+    outs = []
+    for expand in (True, False):
+        leaves = [b.to(dev).requires_grad_(True) for b in base]
+        ins = [x.expand(2, -1, -1, -1) if expand else x.repeat(2, 1, 1, 1) for x in leaves]
+        out = race_attention(*ins, planes, K, L, scale, causal=causal)
+        out.backward(dout)
+        outs.append([out.detach()] + [x.grad.detach() for x in leaves])
+    for a, b in zip(*outs):
+        assert O.rel_l2(a.double().cpu().numpy(), b.double().cpu().numpy()) < 1e-5
