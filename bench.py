@@ -205,10 +205,10 @@ class Layer:
 #       --clock-control none python bench.py --steps 2 --warmup 3 --no-e2e --no-cpu
 #       --tokens 262144
 TRAFFIC_2P18 = {
-    (False, "f32", "backward_kv"): 225.8e6,
-    (False, "f32", "backward_q"): 171.6e6,
-    (False, "bf16", "backward_kv"): 89.4e6,
-    (False, "bf16", "backward_q"): 73.3e6,
+    (False, "f32", "backward_kv"): 216.0e6,
+    (False, "f32", "backward_q"): 169.4e6,
+    (False, "bf16", "backward_kv"): 86.0e6,
+    (False, "bf16", "backward_q"): 72.1e6,
     (True, "f32", "backward_kv"): 396.3e6,
     (True, "bf16", "backward_kv"): 197.7e6,
 }

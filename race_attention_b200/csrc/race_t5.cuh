@@ -41,16 +41,6 @@ namespace t5 {
 
 using bf16 = __nv_bfloat16;
 
-#ifndef RACE_T5_NTH_KV
-#define RACE_T5_NTH_KV 4
-#endif
-#ifndef RACE_T5_NTH_RO
-#define RACE_T5_NTH_RO 2
-#endif
-#ifndef RACE_T5_ABL
-#define RACE_T5_ABL 0
-#endif
-
 constexpr int TT = 128;   // tokens per tile = MMA M = TMEM lanes
 constexpr int PJ = 16;    // projection columns (L*K <= 16)
 constexpr int kWaitPolls = 1 << 22;   // bounded mbarrier polls before giving up
@@ -572,7 +562,7 @@ struct Slot {
 // ------------------------------------------------------------------ layouts (in floats)
 template <int D, int SPAD>
 struct ReadoutLay {
-  static constexpr int NTH = RACE_T5_NTH_RO;          // threads per token
+  static constexpr int NTH = 2;          // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;   // bucket columns (MMA K)
   static constexpr int QX = 0;                        // [2] slots
   static constexpr int PQ = QX + 2 * Slot<D>::FLOATS; // bf16 [TT x SP] hi, then lo
@@ -587,7 +577,7 @@ struct ReadoutLay {
 
 template <int D, int SPAD>
 struct BwdKVLay {
-  static constexpr int NTH = RACE_T5_NTH_KV;           // threads per token
+  static constexpr int NTH = 4;           // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;    // bucket columns (MMA K and N)
   static constexpr int KX = 0;                         // [2] k slots (landed, then hi | mid)
   static constexpr int VX = KX + 2 * Slot<D>::FLOATS;  // [2] v slots (landed, then hi | mid)
@@ -786,7 +776,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
 // ------------------------------------------------------------------ F1 reduce
 template <int D, int SPAD>
 struct ReduceLay {
-  static constexpr int NTH = RACE_T5_NTH_KV;           // threads per token
+  static constexpr int NTH = 4;           // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;     // bucket columns
   static constexpr int NFULL = 2;
   static constexpr int KX = 0;                          // [2] k slots (landed, then 2 parts)
@@ -986,7 +976,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
 // ------------------------------------------------------------------ B1 query backward
 template <int D, int SPAD>
 struct BwdQLay {
-  static constexpr int NTH = RACE_T5_NTH_KV;           // threads per token
+  static constexpr int NTH = 4;           // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;     // bucket columns
   static constexpr int NFULL = 3;                      // dO slots in rotation
   static constexpr int QX = 0;                          // [2] q slots (landed, then hi | mid)
@@ -1286,7 +1276,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         T5_WAIT(barB, phB);
         phB ^= 1;
         fence_after();
-        if (!(RACE_T5_ABL & 4)) {
+        {
           float o[W];
           tld_sum<W>(tlane + LY::C_DV + sub * W, D, o);
           put_tile_cols<T, D, W>(stage_k, row, sub * W, o);
@@ -1296,7 +1286,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         fence_async_smem();
         fence_before();
         __syncthreads();
-        if (tid == 0 && !failed && !(RACE_T5_ABL & 4)) {
+        if (tid == 0 && !failed) {
           tma_store_tile<T, D>(&maps.map[3], stage_k, prm.ldv, prm, n, tprev);
           tma_store_tile<T, D>(&maps.map[2], stage_v, prm.ldk, prm, n, tprev);
           bulk_commit();
@@ -1333,12 +1323,10 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
           __syncthreads();
           // hi | mid in place, the third part beside (read only by this tile's
           // projection / dpK MMAs, which finish before the next conversion)
-          if (!(RACE_T5_ABL & 1)) {
           put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), kl, row,
                                       sub * W, x);
           put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), vl, row,
                                       sub * W, y);
-          }
         }
         fence_async_smem();
         fence_before();
@@ -1346,7 +1334,6 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         // projections and dpK = v . dB^T
         if (tid == 0 && !failed) {
           fence_after();
-          if (!(RACE_T5_ABL & 8)) {
           // three parts on both sides: the projections feed the temperature
           // gradient (a sum with heavy cancellation), and where v matches a
           // bucket's mean (tiny buckets) v . dB and dA cancel to far below |v| |dB|
@@ -1354,7 +1341,6 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
                                           Slot<D>::part(KXt, 1), kl, F32 ? 3 : 1, ps, false);
           gemm_parts<SP, 3, D / 16, D, D>(tbase + LY::C_DPK, Slot<D>::part(VXt, 0),
                                           Slot<D>::part(VXt, 1), vl, F32 ? 3 : 1, db, false);
-          }
           commit(barA);
         }
         T5_WAIT(barA, phA);   // also covers the previous tile's dv / dk MMAs
@@ -1367,7 +1353,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
           const bool valid = tile0 + row < it.t1;
 #pragma unroll
           for (int gi = 0; gi < SP / G::GB; ++gi) {
-            if (gi % NTH == sub && !(RACE_T5_ABL & 2)) {
+            if (gi % NTH == sub) {
               float p[G::GB], h[G::GK], g[G::GB], dj_[G::GK];
               const bool has = gi * G::GK < PJ;
               group_probs<K>(has ? proj + gi * G::GK : proj, gi * G::GT, has ? L : 0, inv_scale, p,
@@ -1398,12 +1384,10 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         __syncthreads();
         if (tid == 0 && !failed) {
           fence_after();
-          if (!(RACE_T5_ABL & 8)) {
           gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_DV, pk, pk + TT * SP, nullptr, 2, dbt,
                                             false);
           gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DK, dj, dj + TT * PJ, nullptr, 2, pt,
                                             false);
-          }
           commit(barB);
         }
         if (T5_VOTE()) break;

@@ -136,7 +136,8 @@ def test_chunk_length_independent():
 def test_broadcast_batch_layout(causal):
     """A batch axis broadcast with stride 0 (one sequence shared by two batch
     rows) cannot be walked by the copy engine's tensor maps; the library then
-    runs the warp-level kernels.  Results must equal two explicit copies."""
+    runs the warp-level kernels.  Results must match two explicit copies (run
+    by the tcgen05 kernels) within the path's fp32 bar of 1e-4."""
     from race_attention_b200 import race_attention
     dev = "cuda"
     g = torch.Generator().manual_seed(5)
@@ -153,4 +154,4 @@ def test_broadcast_batch_layout(causal):
         out.backward(dout)
         outs.append([out.detach()] + [x.grad.detach() for x in leaves])
     for a, b in zip(*outs):
-        assert O.rel_l2(a.double().cpu().numpy(), b.double().cpu().numpy()) < 1e-5
+        assert O.rel_l2(a.double().cpu().numpy(), b.double().cpu().numpy()) < 1e-4
