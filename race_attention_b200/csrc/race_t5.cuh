@@ -198,6 +198,11 @@ __device__ __forceinline__ void tld8(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tld1(uint32_t taddr, float& v) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  v = __uint_as_float(r);
+}
 __device__ __forceinline__ void tld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -217,6 +222,25 @@ __device__ __forceinline__ void tld_sum(uint32_t taddr, int off, float* out) {
 #pragma unroll
     for (int j = 1; j < BP; ++j) x += v[j][c];
     out[c] = x;
+  }
+}
+
+// The GK projection columns [c0, c0 + GK) of this lane, summed over NB
+// column blocks PJ apart (c0 may vary at run time; warp-uniform).
+template <int GK, int NB>
+__device__ __forceinline__ void tld_group(uint32_t taddr, int c0, float (&out)[GK]) {
+  float v[NB][GK];
+#pragma unroll
+  for (int b = 0; b < NB; ++b)
+#pragma unroll
+    for (int k = 0; k < GK; ++k) tld1(taddr + b * PJ + c0 + k, v[b][k]);
+  tld_wait();
+#pragma unroll
+  for (int k = 0; k < GK; ++k) {
+    float x = v[0][k];
+#pragma unroll
+    for (int b = 1; b < NB; ++b) x += v[b][k];
+    out[k] = x;
   }
 }
 
@@ -741,6 +765,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       if (i > 0) store_prev(tile0 - TT, X);
       fence_after();
       {
+        // two threads per token take two groups each: unrolled (constant offsets)
         float proj[PJ];
         tld_sum<PJ>(tlane + LY::C_PROJ, PJ, proj);
 #pragma unroll
@@ -885,16 +910,15 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
       phA ^= 1;
       fence_after();
       {
-        float proj[PJ];
-        tld_sum<PJ>(tlane + LY::C_PROJ, PJ, proj);
-#pragma unroll
-        for (int gi = 0; gi < NG; ++gi) {
-          const int a = gi / NTH;
-          if (gi % NTH == sub) {
-            float p[G::GB], h[G::GK];
+        static_assert(MYG == 1, "one bucket group per thread");
+#pragma unroll 1
+        for (int gi = sub; gi < NG; gi += NTH) {
+          const int a = 0;
+          {
+            float pj[G::GK], p[G::GB], h[G::GK];
             const bool has = gi * G::GK < PJ;
-            group_probs<K>(has ? proj + gi * G::GK : proj, gi * G::GT, has ? L : 0, inv_scale, p,
-                           h);
+            tld_group<G::GK, 2>(tlane + LY::C_PROJ, has ? gi * G::GK : 0, pj);
+            group_probs<K>(pj, gi * G::GT, has ? L : 0, inv_scale, p, h);
 #pragma unroll
             for (int b = 0; b < G::GB; ++b) {
               if (!valid) p[b] = 0.f;
@@ -955,11 +979,9 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
       fence_before();
       // bucket mass: per-thread sums -> scratch (pK area is free) -> fixed-order sum
       float* ms = sm + LY::PK3;
+      if (sub < NG)
 #pragma unroll
-      for (int gi = 0; gi < NG; ++gi)
-        if (gi % NTH == sub)
-#pragma unroll
-          for (int b = 0; b < G::GB; ++b) ms[row * SP + gi * G::GB + b] = mass[gi / NTH][b];
+        for (int b = 0; b < G::GB; ++b) ms[row * SP + sub * G::GB + b] = mass[0][b];
       __syncthreads();
       if (tid < prm.S) {
         float tot = 0.f;
@@ -1114,15 +1136,15 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
         if (i > 0) store_prev(tile0 - TT, QXt);
         fence_after();
         {
-          float proj[PJ];
-          tld_sum<PJ, 3>(tlane + LY::C_PROJ, PJ, proj);
-#pragma unroll
-          for (int gi = 0; gi < SP / G::GB; ++gi) {
-            if (gi % NTH == sub) {
-              float p[G::GB], h[G::GK], g[G::GB], dj_[G::GK];
+
+          // one copy of the group code: groups gi = sub, sub + NTH, ... (warp-uniform)
+#pragma unroll 1
+          for (int gi = sub; gi < SP / G::GB; gi += NTH) {
+            {
+              float pj[G::GK], p[G::GB], h[G::GK], g[G::GB], dj_[G::GK];
               const bool has = gi * G::GK < PJ;
-              group_probs<K>(has ? proj + gi * G::GK : proj, gi * G::GT, has ? L : 0, inv_scale, p,
-                             h);
+              tld_group<G::GK, 3>(tlane + LY::C_PROJ, has ? gi * G::GK : 0, pj);
+              group_probs<K>(pj, gi * G::GT, has ? L : 0, inv_scale, p, h);
               tld_sum<G::GB, 3>(tlane + LY::C_DPQ + gi * G::GB, SP, g);
               float dsl = 0.f;
               group_probs_bwd<K>(p, g, h, inv_scale, dj_, dsl);
@@ -1348,16 +1370,16 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         if (i > 0) store_prev(tile0 - TT, KXt, VXt);
         fence_after();
         {
-          float proj[PJ];
-          tld_sum<PJ, 3>(tlane + LY::C_PROJ, PJ, proj);
+
           const bool valid = tile0 + row < it.t1;
-#pragma unroll
-          for (int gi = 0; gi < SP / G::GB; ++gi) {
-            if (gi % NTH == sub) {
-              float p[G::GB], h[G::GK], g[G::GB], dj_[G::GK];
+          // one copy of the group code: groups gi = sub, sub + NTH, ... (warp-uniform)
+#pragma unroll 1
+          for (int gi = sub; gi < SP / G::GB; gi += NTH) {
+            {
+              float pj[G::GK], p[G::GB], h[G::GK], g[G::GB], dj_[G::GK];
               const bool has = gi * G::GK < PJ;
-              group_probs<K>(has ? proj + gi * G::GK : proj, gi * G::GT, has ? L : 0, inv_scale, p,
-                             h);
+              tld_group<G::GK, 3>(tlane + LY::C_PROJ, has ? gi * G::GK : 0, pj);
+              group_probs<K>(pj, gi * G::GT, has ? L : 0, inv_scale, p, h);
               tld_sum<G::GB, 3>(tlane + LY::C_DPK + gi * G::GB, SP, g);
 #pragma unroll
               for (int b = 0; b < G::GB; ++b) g[b] += dA[gi * G::GB + b];
