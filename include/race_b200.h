@@ -169,6 +169,25 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q,
 int race_add_offset(const race_desc_t* desc, float* slots, const float* offset,
                     int is_gradient, cudaStream_t stream);
 
+/* Bucket probabilities of one tensor, for hybrid models that gate on them.
+ * Replaces the torch sequence of race_bucket_probs_from_qk
+ * (misc/arxiv_64K.py:1580-1642: x @ planes_T, tanh, / scale, @ protos_T,
+ * softmax per table), which the reference runs for q and k separately.
+ * x: [M, B, T, H, d] through its strides (desc->causal is ignored).
+ * probs: float32 [N][T][S], N = M*B*H streams in (m, b, h) order and bucket
+ * s = l*2^K + r with r in itertools.product([-1, 1]) order -- the
+ * reference's [M, B, H, T, L, R] tensor. */
+int race_probs(const race_desc_t* desc, race_tensor_t x, const float* planes,
+               const float* scale, float* probs, cudaStream_t stream);
+/* Workspace bytes race_probs_backward needs (temperature partial sums). */
+size_t race_probs_workspace(const race_desc_t* desc);
+/* Gradient of race_probs: dx from dprobs (float32 [N][T][S]); *dscale is
+ * set (accumulate = 0) or incremented (accumulate = 1) by dL/dscale. */
+int race_probs_backward(const race_desc_t* desc, race_tensor_t x, const float* planes,
+                        const float* scale, const float* dprobs, race_tensor_t dx,
+                        float* dscale, int accumulate, void* workspace,
+                        size_t workspace_bytes, cudaStream_t stream);
+
 /* Forward without any device allocation: for callers that cannot call
  * cudaMalloc or own a caching allocator -- e.g. code running inside another
  * runtime's memory pool, a plugin host that forbids allocation after start-up,

@@ -21,6 +21,7 @@ SYMBOLS = (
     "race_version", "race_strerror", "race_last_cuda_error", "race_query",
     "race_forward", "race_backward", "race_forward_reduce", "race_forward_readout",
     "race_backward_q", "race_backward_kv", "race_add_offset", "race_forward_static",
+    "race_probs", "race_probs_workspace", "race_probs_backward",
 )
 
 
@@ -74,6 +75,10 @@ _SIGS = {
                           ctypes.c_size_t, _P], ctypes.c_int),
     "race_add_offset": ([ctypes.POINTER(RaceDesc), _P, _P, ctypes.c_int, _P], ctypes.c_int),
     "race_forward_static": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _T, _P], ctypes.c_int),
+    "race_probs": ([ctypes.POINTER(RaceDesc), _T, _P, _P, _P, _P], ctypes.c_int),
+    "race_probs_workspace": ([ctypes.POINTER(RaceDesc)], ctypes.c_size_t),
+    "race_probs_backward": ([ctypes.POINTER(RaceDesc), _T, _P, _P, _P, _T, _P, ctypes.c_int, _P,
+                             ctypes.c_size_t, _P], ctypes.c_int),
 }
 
 

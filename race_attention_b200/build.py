@@ -18,7 +18,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "librace_b200.so")
 SOURCES = ["race_capi.cu", "race_f32_d32.cu", "race_f32_d64.cu", "race_bf16_d32.cu",
-           "race_bf16_d64.cu"]
+           "race_bf16_d64.cu", "race_probs.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]

@@ -443,6 +443,86 @@ int zero_fill(void* p, size_t bytes, cudaStream_t stream) {
 
 using namespace race;
 
+namespace {
+// Parameters of the probability export: the plan's shape checks and a Params
+// carrying x in the q slot and dx in the dq slot.
+int probs_params(const race_desc_t* d, race_tensor_t x, const float* planes, const float* scale,
+                 Plan* plan, Params* p) {
+  const int rc = make_plan(d, plan);
+  if (rc != RACE_OK) return rc;
+  if (planes == nullptr || scale == nullptr) return RACE_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(planes) % 16 != 0) return RACE_ERR_ALIGN;
+  const int rt = check_tensor(d, x);
+  if (rt != RACE_OK) return rt;
+  std::memset(p, 0, sizeof(*p));
+  p->N = plan->N;
+  p->M = d->ensembles;
+  p->B = d->batch;
+  p->H = d->heads;
+  p->T = d->tokens;
+  p->K = d->num_bits;
+  p->L = d->num_tables;
+  p->R = 1 << d->num_bits;
+  p->S = plan->S;
+  p->LK = plan->LK;
+  p->Mp = d->shared_planes ? 1 : d->ensembles;
+  p->planes = planes;
+  p->scale = scale;
+  fill_layout(p->lq, x);
+  p->q = x.data;
+  return RACE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int race_probs(const race_desc_t* desc, race_tensor_t x, const float* planes, const float* scale,
+               float* probs, cudaStream_t stream) {
+  Plan plan;
+  Params p;
+  RACE_TRY(probs_params(desc, x, planes, scale, &plan, &p));
+  if (probs == nullptr) return RACE_ERR_INVALID;
+  if (desc->tokens == 0) return RACE_OK;
+  const cudaError_t e =
+      launch_probs(false, desc->dtype == RACE_BF16, desc->head_dim, p, probs, nullptr, stream);
+  return e == cudaSuccess ? RACE_OK : cuda_fail(e);
+}
+
+size_t race_probs_workspace(const race_desc_t* desc) {
+  Plan plan;
+  if (make_plan(desc, &plan) != RACE_OK) return 0;
+  return (size_t)plan.N * (size_t)probs_blocks(desc->tokens) * sizeof(float) + 16;
+}
+
+int race_probs_backward(const race_desc_t* desc, race_tensor_t x, const float* planes,
+                        const float* scale, const float* dprobs, race_tensor_t dx, float* dscale,
+                        int accumulate, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream) {
+  Plan plan;
+  Params p;
+  RACE_TRY(probs_params(desc, x, planes, scale, &plan, &p));
+  if (dprobs == nullptr || dscale == nullptr) return RACE_ERR_INVALID;
+  RACE_TRY(check_tensor(desc, dx));
+  if (workspace == nullptr || workspace_bytes < race_probs_workspace(desc))
+    return RACE_ERR_WORKSPACE;
+  if (desc->tokens == 0) {
+    if (!accumulate) RACE_TRY(zero_fill(dscale, sizeof(float), stream));
+    return RACE_OK;
+  }
+  fill_layout(p.ldq, dx);
+  p.dq = dx.data;
+  float* part = static_cast<float*>(workspace);
+  cudaError_t e = launch_probs(true, desc->dtype == RACE_BF16, desc->head_dim, p,
+                               const_cast<float*>(dprobs), part, stream);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const int count = (int)((int64_t)plan.N * probs_blocks(desc->tokens));
+  k_dscale_final<<<1, 1024, 0, stream>>>(part, count, scale, dscale, accumulate);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? RACE_OK : cuda_fail(e);
+}
+
+}  // extern "C"
+
 extern "C" {
 
 const char* race_version(void) { return "race_b200 1.0 (sm_100a)"; }

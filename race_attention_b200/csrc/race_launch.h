@@ -44,4 +44,11 @@ bool kernels_f32_d64(int spad, int K, KernelId id, KernelInfo* info);
 bool kernels_bf16_d32(int spad, int K, KernelId id, KernelInfo* info);
 bool kernels_bf16_d64(int spad, int K, KernelId id, KernelInfo* info);
 
+// Bucket-probability export (race_probs.cu): forward writes [N][T][S] fp32
+// probabilities of the tensor in prm.q; backward reads dprobs and writes
+// prm.dq plus one temperature partial per block.
+cudaError_t launch_probs(bool bwd, bool bf16, int D, const Params& prm, float* out_or_dp,
+                         float* part, cudaStream_t s);
+int64_t probs_blocks(int64_t T);
+
 }  // namespace race

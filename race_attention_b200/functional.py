@@ -203,3 +203,56 @@ def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: to
 def default_causal_scale(head_dim: int) -> float:
     """Fixed divisor of the causal module (misc/race.py:67)."""
     return math.sqrt(head_dim)
+
+
+class _ProbsFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, planes, scale, K, L, shared_planes):
+        if not x.is_cuda:
+            raise RuntimeError("bucket_probs runs on CUDA devices only (no CPU fallback)")
+        ctx.in_dtype = x.dtype
+        dtype = x.dtype if x.dtype in _SUPPORTED else torch.float32
+        x = _prep(x, dtype)
+        planes = planes.detach().to(torch.float32).contiguous()
+        scale_d = scale.detach().to(torch.float32).reshape(()).contiguous()
+        M, B, T, H, d = x.shape
+        desc = make_desc(tuple(x.shape), dtype, K, L, False, 0.0, 0, shared_planes)
+        S = L << K
+        probs = torch.empty((M, B, H, T, L, 1 << K), dtype=torch.float32, device=x.device)
+        check(_lib.load().race_probs(desc, _rt(x), _ptr(planes), _ptr(scale_d), _ptr(probs),
+                                     _stream()))
+        ctx.save_for_backward(x, planes, scale_d)
+        ctx.desc = desc
+        ctx.scale_shape = scale.shape
+        assert probs.numel() == M * B * H * T * S
+        return probs
+
+    @staticmethod
+    def backward(ctx, dprobs):
+        x, planes, scale_d = ctx.saved_tensors
+        lib = _lib.load()
+        dprobs = dprobs.to(torch.float32).contiguous()
+        dx = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+        dscale = torch.empty((), dtype=torch.float32, device=x.device)
+        ws = torch.empty(max(16, lib.race_probs_workspace(ctx.desc)), dtype=torch.uint8,
+                         device=x.device)
+        check(lib.race_probs_backward(ctx.desc, _rt(x), _ptr(planes), _ptr(scale_d),
+                                      _ptr(dprobs), _rt(dx), _ptr(dscale), 0, _ptr(ws),
+                                      ws.numel(), _stream()))
+        return dx.to(ctx.in_dtype), None, dscale.reshape(ctx.scale_shape), None, None, None
+
+
+def bucket_probs(x: torch.Tensor, planes: torch.Tensor, num_bits: int, num_tables: int,
+                 scale=1.0, shared_planes: Optional[bool] = None) -> torch.Tensor:
+    """Soft-hash bucket probabilities of x [M, B, T, H, d] (4-D [B, T, H, d]
+    is taken as M = 1): [M, B, H, T, L, 2^K] float32, the tensor the
+    reference's race_bucket_probs_from_qk returns (misc/arxiv_64K.py:1580-1642).
+    Differentiable in x and in ``scale`` (a tensor or a float)."""
+    if x.dim() == 4:
+        x = x.unsqueeze(0)
+    if planes.dim() == 2:
+        planes = planes.unsqueeze(0)
+    if shared_planes is None:
+        shared_planes = planes.shape[0] == 1
+    scale_t = _scale_tensor(scale, x.device)
+    return _ProbsFunction.apply(x, planes, scale_t, num_bits, num_tables, bool(shared_planes))

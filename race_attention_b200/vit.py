@@ -104,3 +104,22 @@ class RACEBlock(nn.Module):
         x = self.drop(self.att(self.norm1(x))) + h
         h = x
         return self.drop(self.ff(self.norm2(x))) + h
+
+
+def race_bucket_probs_from_qk(attn: RACEAttention, Q: torch.Tensor, K: torch.Tensor):
+    """Bucket probabilities of q and k with ``attn``'s planes and temperature,
+    for hybrid models (the reference's ``race_bucket_probs_from_qk``,
+    misc/arxiv_64K.py:1580-1642): Q, K [B, T, H, d_k] ->
+    (probsQ, probsK), each [M, B, H, T, L, R]."""
+    from .functional import bucket_probs
+    ace = attn.ace
+    M = attn.M
+
+    def pack(z):
+        return z.unsqueeze(0).expand(M, -1, -1, -1, -1)   # [M, B, T, H, d_k]
+
+    planes = ace.planes()
+    scale = ace.scale()
+    probsQ = bucket_probs(pack(Q), planes, ace.K, ace.L, scale, shared_planes=ace.share_planes)
+    probsK = bucket_probs(pack(K), planes, ace.K, ace.L, scale, shared_planes=ace.share_planes)
+    return probsQ, probsK

@@ -20,6 +20,7 @@ import itertools
 import math
 import os
 import sys
+import types
 
 import numpy as np
 import torch
@@ -39,6 +40,57 @@ def load_class(path: str, name: str):
             exec(compile(seg, f"{path}:{name}", "exec"), ns)
             return ns[name]
     raise KeyError(name)
+
+
+def load_function(path: str, name: str, extra=None):
+    src = open(path).read()
+    tree = ast.parse(src)
+    for node in tree.body:
+        if isinstance(node, ast.FunctionDef) and node.name == name:
+            seg = ast.get_source_segment(src, node)
+            ns = {"torch": torch, "nn": nn, "F": F, "itertools": itertools, "math": math}
+            ns.update(extra or {})
+            exec(compile(seg, f"{path}:{name}", "exec"), ns)
+            return ns[name]
+    raise KeyError(name)
+
+
+def run_probs_case(fn, cls, *, M, B, T, H, d, K, L, share_planes, logit_temp, seed):
+    """The reference's race_bucket_probs_from_qk (misc/arxiv_64K.py:1580-1642)
+    on a stand-in attention module holding the reference's BatchedACE."""
+    torch.manual_seed(seed)
+    ace = cls(d, K, L, M, device="cpu", share_planes=share_planes).double()
+    with torch.no_grad():
+        ace.logit_temp.fill_(logit_temp)
+    attn = types.SimpleNamespace(ace=ace, M=M)
+    x = lambda: torch.randn(B, T, H, d, dtype=torch.float32).double()
+    q, k = x(), x()
+    q.requires_grad_(True)
+    k.requires_grad_(True)
+    pq, pk = fn(attn, q, k)                                     # [M,B,H,T,L,R] each
+    gq = torch.randn(pq.shape, dtype=torch.float32).double()
+    gk = torch.randn(pk.shape, dtype=torch.float32).double()
+    ((pq * gq).sum() + (pk * gk).sum()).backward()
+    planes_T = ace.planes_T.detach()
+    if planes_T.dim() == 2:
+        planes_T = planes_T.unsqueeze(0)
+    planes = planes_T.transpose(1, 2).contiguous()
+    scale = float(ace.logit_temp.detach().exp().clamp(1e-2, 20.0))   # as the function computes it
+    return dict(
+        q=q.detach().float().numpy(), k=k.detach().float().numpy(),
+        planes=planes.float().numpy(), probs_q=pq.detach().numpy(),
+        probs_k=pk.detach().numpy(), gq=gq.float().numpy(), gk=gk.float().numpy(),
+        dq=q.grad.numpy(), dk=k.grad.numpy(), scale=np.float64(scale),
+        dlogit_temp=np.float64(ace.logit_temp.grad),
+        meta=np.array([M, B, T, H, d, K, L, int(share_planes)], np.int64),
+    )
+
+
+PROBS_CASES = [
+    # name, M, B, T, H, d, K, L, share_planes, logit_temp
+    ("probs_k2l5_t40", 1, 2, 40, 2, 64, 2, 5, False, 0.0),
+    ("probs_k3l3_t29_m2_shared", 2, 1, 29, 3, 32, 3, 3, True, math.log(0.7)),
+]
 
 
 def run_case(cls, *, causal, M, B, T, H, d, K, L, share_planes, logit_temp, seed):
@@ -95,6 +147,14 @@ def main(ref_root: str):
         cls = race_cls if causal else vit_cls
         res = run_case(cls, causal=causal, M=M, B=B, T=T, H=H, d=d, K=K, L=L,
                        share_planes=sp, logit_temp=lt, seed=i)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **res)
+        print("wrote", path, os.path.getsize(path))
+    fn = load_function(os.path.join(ref_root, "misc/arxiv_64K.py"), "race_bucket_probs_from_qk",
+                       {"RACEAttention": object})
+    for i, (name, M, B, T, H, d, K, L, sp, lt) in enumerate(PROBS_CASES):
+        res = run_probs_case(fn, vit_cls, M=M, B=B, T=T, H=H, d=d, K=K, L=L, share_planes=sp,
+                             logit_temp=lt, seed=100 + i)
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **res)
         print("wrote", path, os.path.getsize(path))

@@ -8,7 +8,14 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
 def golden_files():
-    return sorted(glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+    """Attention fixtures (the reference's BatchedACE modules)."""
+    return sorted(p for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
+                  if not os.path.basename(p).startswith("probs_"))
+
+
+def probs_files():
+    """Probability-export fixtures (the reference's race_bucket_probs_from_qk)."""
+    return sorted(glob.glob(os.path.join(GOLDEN_DIR, "probs_*.npz")))
 
 
 def load(path):

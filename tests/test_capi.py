@@ -14,7 +14,7 @@ HEADER = os.path.join(ROOT, "include", "race_b200.h")
 
 def declared_symbols():
     txt = open(HEADER).read()
-    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(race_[a-z_]+)\(", txt, re.M)))
+    return sorted(set(re.findall(r"^(?:int|size_t|const char\*)\s+(race_[a-z_]+)\(", txt, re.M)))
 
 
 @pytest.fixture(scope="module")

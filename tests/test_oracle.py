@@ -102,3 +102,33 @@ def test_streamed_causal_matches_dense():
             np.testing.assert_allclose(a, b, rtol=1e-9, atol=1e-12)
         assert math.isclose(got[4], ref[4], rel_tol=1e-9)
     np.testing.assert_allclose(O.causal_streamed(q, k, v, P, K, L, 0.9, chunk=50), ref[0], rtol=1e-9, atol=1e-12)
+
+
+def _probs_streams(g, name):
+    """[B,T,H,d] input of a probs golden -> [N,T,d] streams in (m, b, h) order."""
+    M, B, T, H, d = (int(v) for v in g["meta"][:5])
+    x = np.asarray(g[name], np.float64)
+    xs = np.broadcast_to(x.transpose(0, 2, 1, 3)[None], (M, B, H, T, d)).reshape(M * B * H, T, d)
+    return xs, (M, B, T, H, d)
+
+
+@pytest.mark.parametrize("path", G.probs_files(), ids=lambda p: p.split("/")[-1][:-4])
+def test_oracle_matches_reference_probs_export(path):
+    """soft_hash / soft_hash_backward reproduce race_bucket_probs_from_qk
+    (misc/arxiv_64K.py:1580-1642) run under autograd in float64."""
+    g = np.load(path)
+    K, L = int(g["meta"][5]), int(g["meta"][6])
+    scale = float(g["scale"])
+    planes = np.asarray(g["planes"], np.float64)
+    dl = 0.0
+    for name, pname, gname, dname in (("q", "probs_q", "gq", "dq"), ("k", "probs_k", "gk", "dk")):
+        xs, (M, B, T, H, d) = _probs_streams(g, name)
+        P = planes[np.repeat(np.arange(M) if planes.shape[0] == M else np.zeros(M, int), B * H)]
+        p, h = O.soft_hash(xs, P, K, L, scale)
+        np.testing.assert_allclose(p, g[pname].reshape(M * B * H, T, -1), rtol=1e-10, atol=1e-12)
+        dp = np.asarray(g[gname], np.float64).reshape(M * B * H, T, -1)
+        dx, ds = O.soft_hash_backward(dp, p, h, P, K, L, scale)
+        dx = dx.reshape(M, B, H, T, d).sum(0).transpose(0, 2, 1, 3)   # -> [B,T,H,d]
+        np.testing.assert_allclose(dx, g[dname], rtol=1e-9, atol=1e-11)
+        dl += ds * scale
+    assert math.isclose(dl, float(g["dlogit_temp"]), rel_tol=1e-9, abs_tol=1e-12)
