@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define RACE_ABI_VERSION 1
+#define RACE_ABI_VERSION 2
 
 typedef enum {
   RACE_OK = 0,
@@ -63,6 +63,16 @@ typedef enum {
 } race_status_t;
 
 typedef enum { RACE_F32 = 0, RACE_BF16 = 1 } race_dtype_t;
+
+/* Causal normalisation.  BUCKET: every bucket's prefix mean is normalised by
+ * its own mass, out(t) = sum_s pQ_s(t) B_s(t) / (A_s(t) + eps) (misc/race.py).
+ * GLOBAL: one denominator per token summed over all buckets and tables,
+ * out(t) = sum_s pQ_s(t) B_s(t) / max(sum_s pQ_s(t) A_s(t), eps), the chunked
+ * ELSAA form (misc/race_kernel.py:9-124 + misc/elsaa_causal_complete.py:551-560;
+ * eps is its clamp_min floor: 1e-6 for the Triton path, which sums over tables,
+ * L * 1e-6 for the torch fallback, which averages num and den over tables).
+ * GLOBAL is causal only. */
+typedef enum { RACE_NORM_BUCKET = 0, RACE_NORM_GLOBAL = 1 } race_norm_t;
 
 /* One activation tensor: element strides of the (m, b, h, t) axes; the head
  * dimension is contiguous. */
@@ -83,7 +93,9 @@ typedef struct {
   int64_t tokens;         /* T held by this rank                                 */
   int32_t chunk;          /* causal chunk length, 0 = chosen by the library      */
   int32_t shared_planes;  /* 1: planes [1][L*K][d]; 0: planes [M][L*K][d]        */
-  float eps;              /* added to the bucket mass (reference: 1e-6)          */
+  float eps;              /* added to the bucket mass (reference: 1e-6); GLOBAL:
+                             the floor of the per-token denominator             */
+  int32_t normalize;      /* race_norm_t (0 = BUCKET)                            */
 } race_desc_t;
 
 typedef struct {
@@ -163,6 +175,36 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q,
                      const float* gstate, race_tensor_t dout, race_tensor_t dk,
                      race_tensor_t dv, float* dscale, void* workspace,
                      size_t workspace_bytes, cudaStream_t stream);
+/* The same calls with the global-normalisation denominator exposed
+ * (desc->normalize == RACE_NORM_GLOBAL only; otherwise a non-NULL den / dden
+ * is RACE_ERR_INVALID).  den: optional float32 [N][T] output, the unclamped
+ * per-token denominator sum_s pQ_s(t) A_s(t) (the reference's den_sumL,
+ * misc/elsaa_causal_complete.py:553-561, from which it derives d_token).
+ * dden: optional float32 [N][T] incoming gradient of that den, added to the
+ * gradient the output contributes.  Both follow the (m, b, h) stream order. */
+int race_forward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
+                    race_tensor_t v, const float* planes, const float* scale,
+                    race_tensor_t out, float* den, float* state, void* workspace,
+                    size_t workspace_bytes, cudaStream_t stream);
+int race_forward_readout_ex(const race_desc_t* desc, race_tensor_t q,
+                            race_tensor_t k, race_tensor_t v,
+                            const float* planes, const float* scale,
+                            const float* state, race_tensor_t out, float* den,
+                            void* workspace, size_t workspace_bytes,
+                            cudaStream_t stream);
+int race_backward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
+                     race_tensor_t v, const float* planes, const float* scale,
+                     const float* state, race_tensor_t dout, const float* dden,
+                     race_tensor_t dq, race_tensor_t dk, race_tensor_t dv,
+                     float* dscale, float* gstate, void* workspace,
+                     size_t workspace_bytes, cudaStream_t stream);
+int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
+                       race_tensor_t v, const float* planes, const float* scale,
+                       const float* state, race_tensor_t dout, const float* dden,
+                       race_tensor_t dq, float* dscale, float* gstate, float* total,
+                       void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream);
+
 /* Causal only: adds offset (N slots) to every chunk slot of `slots`
  * (state or gstate).  Gradient slots also carry the per-chunk key mass,
  * which the offset does not touch. */

@@ -21,6 +21,9 @@ Reference semantics restated here (paths inside the reference project):
   * causal per-bucket prefix mean (``misc/race.py:108-138``,
     ``kernels/cpu/race_pref.cpp:36-101``) and its backward
     (``kernels/cpu/race_pref.cpp:104-220``).
+  * causal global normalisation, one denominator per token over all buckets
+    (``misc/elsaa_causal_complete.py:520-571``, ``misc/race_kernel.py:9-124``),
+    pinned by golden vectors of the reference's ``CausalRACEAttention``.
 """
 from __future__ import annotations
 
@@ -242,6 +245,52 @@ def causal_streamed(q, k, v, planes, K, L, scale, dout=None, eps=1e-6, chunk=204
     dq, dsq = soft_hash_backward(dpQ, pQ, hQ, planes, K, L, scale)
     dk, dsk = soft_hash_backward(dpK, pK, hK, planes, K, L, scale)
     return out, dq, dk, dv, dsq + dsk
+
+
+# ------------------------------------------------------- causal, global normalisation
+def causal_global(q, k, v, planes, K, L, scale, dout=None, dden=None, eps=1e-6):
+    """Global-normalised causal RACE (the chunked ELSAA form).
+
+    misc/elsaa_causal_complete.py:520-571 (CausalRACEAttention.forward, the
+    torch path) and misc/race_kernel.py:9-124 (the Triton chunk kernel): with
+    inclusive prefixes A_s(t) = sum_{u<=t} pK_s(u), B_s(t) = sum_{u<=t} pK_s(u) v(u),
+    num(t) = sum_s pQ_s(t) B_s(t), den(t) = sum_s pQ_s(t) A_s(t) (summed over
+    tables, like den_sumL) and out = num / max(den, eps).  The chunking of the
+    reference only reorganises these sums.  Here ``scale`` is 1 / beta
+    (beta = exp(log_beta).clamp(1e-2, 20), misc/elsaa_causal_complete.py:502-506).
+
+    Returns (out, den) when ``dout`` is None, else
+    (out, den, dq, dk, dv, dscale); ``dden`` is an optional incoming gradient
+    of den.  Backward (derived from the forward above):
+      gnum = dout / dd, gden = -(dout . out) / dd (0 where the clamp holds) + dden
+      dpQ_s(t) = B_s(t) . gnum(t) + A_s(t) gden(t)
+      dA_s(t) = pQ_s gden, dB_s(t) = pQ_s gnum, pushed to every key u <= t.
+    """
+    pK, hK = soft_hash(k, planes, K, L, scale)
+    pQ, hQ = soft_hash(q, planes, K, L, scale)
+    v = np.asarray(v, np.float64)
+    A, B = _causal_states(pK, v, eps)
+    num = np.einsum("nts,ntsd->ntd", pQ, B, optimize=True)
+    den = np.einsum("nts,nts->nt", pQ, A)
+    dd = np.maximum(den, eps)
+    out = num / dd[..., None]
+    if dout is None:
+        return out, den
+    dout = np.asarray(dout, np.float64)
+    gnum = dout / dd[..., None]
+    gden = np.where(den >= eps, -(dout * out).sum(-1) / dd, 0.0)
+    if dden is not None:
+        gden = gden + np.asarray(dden, np.float64)
+    dpQ = np.einsum("ntsd,ntd->nts", B, gnum, optimize=True) + A * gden[..., None]
+    alpha = pQ * gden[..., None]                                  # d A_s(t)
+    beta = pQ[..., None] * gnum[:, :, None, :]                    # d B_s(t)
+    a_suf = np.cumsum(alpha[:, ::-1], axis=1)[:, ::-1]
+    b_suf = np.cumsum(beta[:, ::-1], axis=1)[:, ::-1]
+    dpK = a_suf + np.einsum("ntsd,ntd->nts", b_suf, v, optimize=True)
+    dv = np.einsum("nts,ntsd->ntd", pK, b_suf, optimize=True)
+    dq, dsq = soft_hash_backward(dpQ, pQ, hQ, planes, K, L, scale)
+    dk, dsk = soft_hash_backward(dpK, pK, hK, planes, K, L, scale)
+    return out, den, dq, dk, dv, dsq + dsk
 
 
 def forward(q, k, v, planes, K, L, scale, causal, eps=1e-6):

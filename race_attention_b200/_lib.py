@@ -16,12 +16,15 @@ RACE_OK = 0
 RACE_ERR_TOO_LARGE = 6
 RACE_F32 = 0
 RACE_BF16 = 1
+RACE_NORM_BUCKET = 0
+RACE_NORM_GLOBAL = 1
 
 SYMBOLS = (
     "race_version", "race_strerror", "race_last_cuda_error", "race_query",
     "race_forward", "race_backward", "race_forward_reduce", "race_forward_readout",
     "race_backward_q", "race_backward_kv", "race_add_offset", "race_forward_static",
     "race_probs", "race_probs_workspace", "race_probs_backward",
+    "race_forward_ex", "race_forward_readout_ex", "race_backward_ex", "race_backward_q_ex",
 )
 
 
@@ -37,7 +40,8 @@ class RaceDesc(ctypes.Structure):
                 ("num_tables", ctypes.c_int32), ("ensembles", ctypes.c_int32),
                 ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("tokens", ctypes.c_int64), ("chunk", ctypes.c_int32),
-                ("shared_planes", ctypes.c_int32), ("eps", ctypes.c_float)]
+                ("shared_planes", ctypes.c_int32), ("eps", ctypes.c_float),
+                ("normalize", ctypes.c_int32)]
 
 
 class RaceSizes(ctypes.Structure):
@@ -75,6 +79,14 @@ _SIGS = {
                           ctypes.c_size_t, _P], ctypes.c_int),
     "race_add_offset": ([ctypes.POINTER(RaceDesc), _P, _P, ctypes.c_int, _P], ctypes.c_int),
     "race_forward_static": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _T, _P], ctypes.c_int),
+    "race_forward_ex": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _T, _P, _P, _P,
+                         ctypes.c_size_t, _P], ctypes.c_int),
+    "race_forward_readout_ex": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _P, _T, _P, _P,
+                                 ctypes.c_size_t, _P], ctypes.c_int),
+    "race_backward_ex": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _P, _T, _P, _T, _T, _T,
+                          _P, _P, _P, ctypes.c_size_t, _P], ctypes.c_int),
+    "race_backward_q_ex": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _P, _T, _P, _T, _P, _P,
+                            _P, _P, ctypes.c_size_t, _P], ctypes.c_int),
     "race_probs": ([ctypes.POINTER(RaceDesc), _T, _P, _P, _P, _P], ctypes.c_int),
     "race_probs_workspace": ([ctypes.POINTER(RaceDesc)], ctypes.c_size_t),
     "race_probs_backward": ([ctypes.POINTER(RaceDesc), _T, _P, _P, _P, _T, _P, ctypes.c_int, _P,

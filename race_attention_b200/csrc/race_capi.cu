@@ -172,8 +172,11 @@ int make_plan(const race_desc_t* d, Plan* p) {
   if (d == nullptr || p == nullptr) return RACE_ERR_INVALID;
   if (d->dtype != RACE_F32 && d->dtype != RACE_BF16) return RACE_ERR_INVALID;
   if (d->num_bits < 1 || d->num_tables < 1 || d->ensembles < 1 || d->batch < 1 || d->heads < 1 ||
-      d->tokens < 0 || d->head_dim < 1 || d->chunk < 0 || !(d->eps >= 0.f))
+      d->tokens < 0 || d->head_dim < 1 || d->chunk < 0 || !(d->eps >= 0.f) ||
+      (d->normalize != RACE_NORM_BUCKET && d->normalize != RACE_NORM_GLOBAL))
     return RACE_ERR_INVALID;
+  // the global denominator exists only for the causal form (misc/race_kernel.py)
+  if (d->normalize == RACE_NORM_GLOBAL && !d->causal) return RACE_ERR_UNSUPPORTED;
   if (d->head_dim != 32 && d->head_dim != 64) return RACE_ERR_UNSUPPORTED;
   if (d->num_bits > 5) return RACE_ERR_UNSUPPORTED;
   const int S = d->num_tables << d->num_bits;
@@ -266,6 +269,7 @@ int prepare(const race_desc_t* d, const float* planes, const float* scale, void*
   p.LK = c->plan.LK;
   p.Mp = d->shared_planes ? 1 : d->ensembles;
   p.eps = d->eps;
+  p.global_norm = d->normalize == RACE_NORM_GLOBAL ? 1 : 0;
   p.planes = planes;
   p.scale = scale;
   p.part = c->part;
@@ -591,13 +595,15 @@ int race_forward_reduce(const race_desc_t* desc, race_tensor_t k, race_tensor_t 
   return RACE_OK;
 }
 
-int race_forward_readout(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
-                         const float* planes, const float* scale, const float* state,
-                         race_tensor_t out, void* workspace, size_t workspace_bytes,
-                         cudaStream_t stream) {
+int race_forward_readout_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
+                            race_tensor_t v, const float* planes, const float* scale,
+                            const float* state, race_tensor_t out, float* den, void* workspace,
+                            size_t workspace_bytes, cudaStream_t stream) {
   Call c;
   RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
   if (state == nullptr) return RACE_ERR_INVALID;
+  if (den != nullptr && !c.prm.global_norm) return RACE_ERR_INVALID;
+  c.prm.den_out = den;
   if (desc->tokens == 0) return RACE_OK;
   RACE_TRY(check_tensor(desc, q));
   RACE_TRY(check_tensor(desc, out));
@@ -620,22 +626,40 @@ int race_forward_readout(const race_desc_t* desc, race_tensor_t q, race_tensor_t
   return RACE_OK;
 }
 
+int race_forward_readout(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                         const float* planes, const float* scale, const float* state,
+                         race_tensor_t out, void* workspace, size_t workspace_bytes,
+                         cudaStream_t stream) {
+  return race_forward_readout_ex(desc, q, k, v, planes, scale, state, out, nullptr, workspace,
+                                 workspace_bytes, stream);
+}
+
+int race_forward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                    const float* planes, const float* scale, race_tensor_t out, float* den,
+                    float* state, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  RACE_TRY(race_forward_reduce(desc, k, v, planes, scale, state, nullptr, workspace,
+                               workspace_bytes, stream));
+  return race_forward_readout_ex(desc, q, k, v, planes, scale, state, out, den, workspace,
+                                 workspace_bytes, stream);
+}
+
 int race_forward(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
                  const float* planes, const float* scale, race_tensor_t out, float* state,
                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  RACE_TRY(race_forward_reduce(desc, k, v, planes, scale, state, nullptr, workspace,
-                               workspace_bytes, stream));
-  return race_forward_readout(desc, q, k, v, planes, scale, state, out, workspace, workspace_bytes,
-                              stream);
+  return race_forward_ex(desc, q, k, v, planes, scale, out, nullptr, state, workspace,
+                         workspace_bytes, stream);
 }
 
-int race_backward_q(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
-                    const float* planes, const float* scale, const float* state,
-                    race_tensor_t dout, race_tensor_t dq, float* dscale, float* gstate,
-                    float* total, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                       const float* planes, const float* scale, const float* state,
+                       race_tensor_t dout, const float* dden, race_tensor_t dq, float* dscale,
+                       float* gstate, float* total, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream) {
   Call c;
   RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
   if (state == nullptr || gstate == nullptr || dscale == nullptr) return RACE_ERR_INVALID;
+  if (dden != nullptr && !c.prm.global_norm) return RACE_ERR_INVALID;
+  c.prm.dden_in = dden;
   if (desc->tokens == 0) {
     RACE_TRY(zero_fill(gstate, c.plan.gstate_floats * sizeof(float), stream));
     if (total) RACE_TRY(zero_fill(total, (size_t)c.plan.N * c.plan.SS * sizeof(float), stream));
@@ -674,6 +698,14 @@ int race_backward_q(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, r
     RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 0, stream));
   }
   return RACE_OK;
+}
+
+int race_backward_q(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                    const float* planes, const float* scale, const float* state,
+                    race_tensor_t dout, race_tensor_t dq, float* dscale, float* gstate,
+                    float* total, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return race_backward_q_ex(desc, q, k, v, planes, scale, state, dout, nullptr, dq, dscale, gstate,
+                            total, workspace, workspace_bytes, stream);
 }
 
 int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
@@ -719,8 +751,17 @@ int race_backward(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, rac
                   const float* planes, const float* scale, const float* state, race_tensor_t dout,
                   race_tensor_t dq, race_tensor_t dk, race_tensor_t dv, float* dscale,
                   float* gstate, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  RACE_TRY(race_backward_q(desc, q, k, v, planes, scale, state, dout, dq, dscale, gstate, nullptr,
-                           workspace, workspace_bytes, stream));
+  return race_backward_ex(desc, q, k, v, planes, scale, state, dout, nullptr, dq, dk, dv, dscale,
+                          gstate, workspace, workspace_bytes, stream);
+}
+
+int race_backward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
+                     const float* planes, const float* scale, const float* state,
+                     race_tensor_t dout, const float* dden, race_tensor_t dq, race_tensor_t dk,
+                     race_tensor_t dv, float* dscale, float* gstate, void* workspace,
+                     size_t workspace_bytes, cudaStream_t stream) {
+  RACE_TRY(race_backward_q_ex(desc, q, k, v, planes, scale, state, dout, dden, dq, dscale, gstate,
+                              nullptr, workspace, workspace_bytes, stream));
   return race_backward_kv(desc, q, k, v, planes, scale, state, gstate, dout, dk, dv, dscale,
                           workspace, workspace_bytes, stream);
 }

@@ -213,6 +213,39 @@ __device__ __forceinline__ void column_sums(const float* X, float* out, int S) {
   }
 }
 
+// W of the tile (split, [t][s] into W2 and, when given, [s][t] into WT2) from
+// the query probabilities PQ and the inclusive key mass ACUM.  Per-bucket
+// normalisation: W_s(t) = pQ_s(t) / (A_s(t) + eps).  Global normalisation
+// (misc/elsaa_causal_complete.py:551-560, misc/race_kernel.py:9-124): one
+// denominator per token, den(t) = sum_s pQ_s(t) A_s(t), and
+// W_s(t) = pQ_s(t) / max(den(t), eps).  Thread (t = tid / 8, e = tid % 8)
+// handles buckets e, e + 8, ...; returns den(t) (0 in per-bucket mode).
+template <class LY>
+__device__ __forceinline__ float weights(float* sm, const Params& prm, int S, const float2* PQ,
+                                         float2* W2, float2* WT2) {
+  const int t = threadIdx.x >> 3, e = threadIdx.x & 7;
+  const float* acum = sm + LY::ACUM + t * LY::ACS;
+  float den = 0.f;
+  if (prm.global_norm) {
+    for (int s = e; s < S; s += 8) {
+      const float2 p = PQ[t * LY::P2S + s];
+      den = fmaf(p.x + p.y, acum[s], den);
+    }
+    den += __shfl_xor_sync(0xffffffffu, den, 1);
+    den += __shfl_xor_sync(0xffffffffu, den, 2);
+    den += __shfl_xor_sync(0xffffffffu, den, 4);
+  }
+  const float dd = fmaxf(den, prm.eps);
+  for (int s = e; s < S; s += 8) {
+    const float2 p = PQ[t * LY::P2S + s];
+    const float w = prm.global_norm ? (p.x + p.y) / dd : (p.x + p.y) / (acum[s] + prm.eps);
+    const float2 w2 = split2(w);
+    W2[t * LY::P2S + s] = w2;
+    if (WT2) WT2[s * LY::PT2S + t] = w2;
+  }
+  return den;
+}
+
 // 32 x 32 products C = A . B (M = N = 32) written back split, keeping
 // (col <= row) for LOWER or (col >= row) for UPPER.  Warp w: C tile
 // (rows 16(w&1), cols 8(w>>1)).
@@ -347,13 +380,12 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_fwd(const Params prm) {
     probs_to<LY, K>(sm, sh, inv_scale, valid, reinterpret_cast<float2*>(sm + LY::P2), nullptr,
                     nullptr);
     __syncthreads();
-    {   // W = pQ / (A + eps)
-      const int t = threadIdx.x >> 3, e = threadIdx.x & 7;
-      const float2* P2 = reinterpret_cast<const float2*>(sm + LY::P2);
-      for (int s = e; s < sh.S; s += 8) {
-        const float2 p = P2[t * LY::P2S + s];
-        W2[t * LY::P2S + s] = split2((p.x + p.y) / (sm[LY::ACUM + t * LY::ACS + s] + prm.eps));
-      }
+    {
+      const float den =
+          weights<LY>(sm, prm, sh.S, reinterpret_cast<const float2*>(sm + LY::P2), W2, nullptr);
+      const int64_t tok = tile0 + (threadIdx.x >> 3);
+      if (prm.den_out && (threadIdx.x & 7) == 0 && tok < tr.t1)
+        prm.den_out[(size_t)n * prm.T + tok] = den;
     }
     __syncthreads();
     // G = W pK^T, lower-triangular
@@ -439,16 +471,9 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_q(const Params prm) {
     // product only touches MM2)
     masked_32x32<LY, true, D / 8>(sm, AView<LY::RS, 1, sizeof(T) == 2>{G}, BView<1, LY::RS, sizeof(T) == 2>{V});
     __syncthreads();
-    {   // W and its transpose
-      const int t = threadIdx.x >> 3, e = threadIdx.x & 7;
-      const float2* P2 = reinterpret_cast<const float2*>(sm + LY::P2);
-      for (int s = e; s < sh.S; s += 8) {
-        const float2 p = P2[t * LY::P2S + s];
-        const float2 w = split2((p.x + p.y) / (sm[LY::ACUM + t * LY::ACS + s] + prm.eps));
-        W2[t * LY::P2S + s] = w;
-        WT2[s * LY::PT2S + t] = w;
-      }
-    }
+    // W and its transpose; den(t) stays in this thread's register
+    const float den =
+        weights<LY>(sm, prm, sh.S, reinterpret_cast<const float2*>(sm + LY::P2), W2, WT2);
     {   // R = dO . B0^T + M . pK  -> DP (warp w: rows 16(w&1), bucket n-tile w>>1)
       const int w = threadIdx.x >> 5;
       const int nt = w >> 1;
@@ -463,7 +488,34 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_q(const Params prm) {
       }
     }
     __syncthreads();
-    {   // dpQ = invA R, alpha = -W dpQ
+    if (prm.global_norm) {
+      // out = num / dd, dd = max(den, eps), num = sum_s pQ_s B_s, den = sum_s pQ_s A_s:
+      //   gden  = -(dO . out) / dd (0 where the clamp holds) + incoming d(den)
+      //   dpQ_s = R_s / dd + A_s gden,  alpha_s = pQ_s gden  (d of A_s(t))
+      // with dO . out = sum_s W_s R_s.
+      const int t = threadIdx.x >> 3, e = threadIdx.x & 7;
+      const int64_t tok = tile0 + t;
+      const float2* P2 = reinterpret_cast<const float2*>(sm + LY::P2);
+      float wr = 0.f;
+      for (int s = e; s < sh.S; s += 8) {
+        const float2 w = W2[t * LY::P2S + s];
+        wr = fmaf(w.x + w.y, sm[LY::DP + t * LY::PS + s], wr);
+      }
+      wr += __shfl_xor_sync(0xffffffffu, wr, 1);
+      wr += __shfl_xor_sync(0xffffffffu, wr, 2);
+      wr += __shfl_xor_sync(0xffffffffu, wr, 4);
+      const float dd = fmaxf(den, prm.eps);
+      float gden = den >= prm.eps ? -wr / dd : 0.f;
+      if (prm.dden_in && tok < tr.t1) gden += prm.dden_in[(size_t)n * prm.T + tok];
+      for (int s = e; s < sh.S; s += 8) {
+        const float dpq = sm[LY::DP + t * LY::PS + s] / dd + sm[LY::ACUM + t * LY::ACS + s] * gden;
+        sm[LY::DP + t * LY::PS + s] = dpq;
+        const float2 p = P2[t * LY::P2S + s];
+        const float al = (p.x + p.y) * gden;
+        sm[LY::AUX + t * LY::ACS + s] = al;
+        if (tok < tr.t1) alpha[tok * prm.S + s] = al;
+      }
+    } else {   // dpQ = invA R, alpha = -W dpQ
       const int t = threadIdx.x >> 3, e = threadIdx.x & 7;
       const int64_t tok = tile0 + t;
       for (int s = e; s < sh.S; s += 8) {
@@ -568,14 +620,7 @@ __global__ void __launch_bounds__(NT, 1) k_ctc_bwd_kv(const Params prm) {
                     nullptr);
     __syncthreads();
     {   // W, W^T; asuf(t) = asuf_end + sum_{tau >= t in tile} alpha(tau) (AUX)
-      const int t = threadIdx.x >> 3, e = threadIdx.x & 7;
-      const float2* PQ = reinterpret_cast<const float2*>(sm + LY::Q2);
-      for (int s = e; s < sh.S; s += 8) {
-        const float2 p = PQ[t * LY::P2S + s];
-        const float2 w = split2((p.x + p.y) / (sm[LY::ACUM + t * LY::ACS + s] + prm.eps));
-        W2[t * LY::P2S + s] = w;
-        WT2[s * LY::PT2S + t] = w;
-      }
+      weights<LY>(sm, prm, sh.S, reinterpret_cast<const float2*>(sm + LY::Q2), W2, WT2);
       // alpha of the tile (contiguous [t][s]) into AUX
       for (int i = threadIdx.x; i < TT * prm.S; i += NT) {
         const int t = i / prm.S, ss = i - t * prm.S;

@@ -59,6 +59,9 @@ struct Params {
   int SS;                // floats per slot
   unsigned* err;         // sticky device error word (workspace tail), 0 = ok
   double* tilemass;      // causal: key mass at every 32-token tile start [N][tiles][S8]
+  int global_norm;       // causal: 1 = one denominator per token summed over all buckets
+  float* den_out;        // causal global: [N][T] denominators (optional)
+  const float* dden_in;  // causal global: [N][T] incoming gradient of den (optional)
 };
 
 __host__ __device__ constexpr int round_up(int a, int b) { return (a + b - 1) / b * b; }

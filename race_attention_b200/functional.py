@@ -60,13 +60,16 @@ def _stream():
     return torch.cuda.current_stream().cuda_stream
 
 
-def make_desc(shape, dtype, K, L, causal, eps, chunk, shared_planes) -> RaceDesc:
+_NORMS = {"bucket": _lib.RACE_NORM_BUCKET, "global": _lib.RACE_NORM_GLOBAL}
+
+
+def make_desc(shape, dtype, K, L, causal, eps, chunk, shared_planes, normalize=0) -> RaceDesc:
     M, B, T, H, d = shape
     return RaceDesc(
         dtype=_lib.RACE_F32 if dtype == torch.float32 else _lib.RACE_BF16,
         causal=int(bool(causal)), head_dim=d, num_bits=K, num_tables=L, ensembles=M,
         batch=B, heads=H, tokens=T, chunk=int(chunk), shared_planes=int(bool(shared_planes)),
-        eps=float(eps))
+        eps=float(eps), normalize=int(normalize))
 
 
 def query(desc: RaceDesc) -> RaceSizes:
@@ -99,7 +102,9 @@ def _scale_tensor(scale, device) -> torch.Tensor:
 
 class _RaceFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, planes, scale, K, L, causal, eps, chunk, shared_planes, group):
+    def forward(ctx, q, k, v, planes, scale, K, L, causal, eps, chunk, shared_planes, group,
+                normalize):
+        ctx.set_materialize_grads(False)
         if not q.is_cuda:
             raise RuntimeError("race_attention runs on CUDA devices only (no CPU fallback)")
         ctx.in_dtypes = (q.dtype, k.dtype, v.dtype)
@@ -107,31 +112,45 @@ class _RaceFunction(torch.autograd.Function):
         q, k, v = (_prep(t, dtype) for t in (q, k, v))
         planes = planes.detach().to(torch.float32).contiguous()
         scale_d = scale.detach().to(torch.float32).reshape(()).contiguous()
-        desc = make_desc(tuple(q.shape), dtype, K, L, causal, eps, chunk, shared_planes)
+        desc = make_desc(tuple(q.shape), dtype, K, L, causal, eps, chunk, shared_planes, normalize)
         sizes = query(desc)
         buf = Buffers(sizes, q.device)
         lib = _lib.load()
         out = torch.empty(q.shape, dtype=dtype, device=q.device)
+        M, B, T, H, _ = q.shape
+        # the per-token denominator of the global mode, [M, B, H, T] float32
+        den = (torch.empty((M, B, H, T), dtype=torch.float32, device=q.device) if normalize
+               else torch.empty(0, dtype=torch.float32, device=q.device))
         state = buf.floats(sizes.state_bytes)
         ws = buf.workspace()
         if group is None:
-            check(lib.race_forward(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale_d),
-                                   _rt(out), _ptr(state), _ptr(ws), ws.numel(), _stream()))
+            check(lib.race_forward_ex(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale_d),
+                                      _rt(out), _ptr(den) if normalize else None, _ptr(state),
+                                      _ptr(ws), ws.numel(), _stream()))
         else:
             from .sequence_parallel import sharded_forward
-            sharded_forward(lib, desc, sizes, buf, q, k, v, planes, scale_d, out, state, ws, group)
+            sharded_forward(lib, desc, sizes, buf, q, k, v, planes, scale_d, out, state, ws, group,
+                            den if normalize else None)
         ctx.save_for_backward(q, k, v, planes, scale_d, state)
         ctx.desc = desc
         ctx.group = group
         ctx.scale_shape = scale.shape
-        return out
+        if not normalize:
+            ctx.mark_non_differentiable(den)
+        return out, den
 
     @staticmethod
-    def backward(ctx, dout):
+    def backward(ctx, dout, dden):
         q, k, v, planes, scale_d, state = ctx.saved_tensors
         desc = ctx.desc
         dtype = q.dtype
+        if dout is None:
+            dout = torch.zeros(q.shape, dtype=dtype, device=q.device)
         dout = _prep(dout, dtype)
+        if dden is not None and desc.normalize:
+            dden = dden.to(torch.float32).contiguous()
+        else:
+            dden = None
         sizes = query(desc)
         buf = Buffers(sizes, q.device)
         lib = _lib.load()
@@ -143,22 +162,23 @@ class _RaceFunction(torch.autograd.Function):
         gstate = buf.floats(sizes.gstate_bytes)
         ws = buf.workspace()
         if ctx.group is None:
-            check(lib.race_backward(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale_d),
-                                    _ptr(state), _rt(dout), _rt(dq), _rt(dk), _rt(dv),
-                                    _ptr(dscale), _ptr(gstate), _ptr(ws), ws.numel(), _stream()))
+            check(lib.race_backward_ex(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale_d),
+                                       _ptr(state), _rt(dout), _ptr(dden), _rt(dq), _rt(dk),
+                                       _rt(dv), _ptr(dscale), _ptr(gstate), _ptr(ws), ws.numel(),
+                                       _stream()))
         else:
             from .sequence_parallel import sharded_backward
             sharded_backward(lib, desc, sizes, buf, q, k, v, planes, scale_d, state, dout,
-                             dq, dk, dv, dscale, gstate, ws, ctx.group)
+                             dq, dk, dv, dscale, gstate, ws, ctx.group, dden)
         dq, dk, dv = (g.to(t) for g, t in zip((dq, dk, dv), ctx.in_dtypes))
         return (dq, dk, dv, None, dscale.reshape(ctx.scale_shape), None, None, None, None, None,
-                None, None)
+                None, None, None)
 
 
 def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: torch.Tensor,
                    num_bits: int, num_tables: int, scale=1.0, causal: bool = False,
                    eps: float = 1e-6, chunk: int = 0, shared_planes: Optional[bool] = None,
-                   group=None) -> torch.Tensor:
+                   group=None, normalize: str = "bucket", return_den: bool = False):
     """RACE attention forward (autograd-aware) on [M, B, T, H, d] inputs.
 
     Args:
@@ -177,6 +197,14 @@ def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: to
         not depend on it beyond float rounding.
       group: torch.distributed process group across which the token axis is
         sharded (contiguous ranges in rank order), or None.
+      normalize: causal only.  "bucket" (default): every bucket normalised by
+        its own prefix mass (misc/race.py).  "global": one denominator per
+        token summed over all L*2^K buckets, out = num / max(den, eps) (the
+        ELSAA chunked form, misc/elsaa_causal_complete.py:520-571 and
+        misc/race_kernel.py); ``eps`` is then the clamp floor of den.
+      return_den: global mode only: also return den, the unclamped per-token
+        denominator [M, B, H, T] float32 (differentiable; 4-D inputs give
+        [B, H, T]).
     """
     squeeze = False
     if q.dim() == 4:
@@ -194,10 +222,20 @@ def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: to
         raise ValueError(f"planes must be [Mp, {LK}, {q.shape[-1]}], got {tuple(planes.shape)}")
     if not shared_planes and planes.shape[0] != M:
         raise ValueError("per-ensemble planes need one set per ensemble")
+    if normalize not in _NORMS:
+        raise ValueError(f"normalize must be 'bucket' or 'global', got {normalize!r}")
+    norm = _NORMS[normalize]
+    if norm and not causal:
+        raise ValueError("normalize='global' is defined for the causal form only")
+    if return_den and not norm:
+        raise ValueError("return_den needs normalize='global'")
     scale_t = _scale_tensor(scale, q.device)
-    out = _RaceFunction.apply(q, k, v, planes, scale_t, int(num_bits), int(num_tables),
-                              bool(causal), float(eps), int(chunk), bool(shared_planes), group)
-    return out.squeeze(0) if squeeze else out
+    out, den = _RaceFunction.apply(q, k, v, planes, scale_t, int(num_bits), int(num_tables),
+                                   bool(causal), float(eps), int(chunk), bool(shared_planes),
+                                   group, norm)
+    if squeeze:
+        out, den = out.squeeze(0), (den.squeeze(0) if norm else den)
+    return (out, den) if return_den else out
 
 
 def default_causal_scale(head_dim: int) -> float:

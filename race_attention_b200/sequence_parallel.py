@@ -60,24 +60,26 @@ def exchange_backward_state(gstate: torch.Tensor, total: Optional[torch.Tensor],
         add_offset(_ordered_sum(gathered[rank + 1:], total))
 
 
-def sharded_forward(lib, desc, sizes, buf, q, k, v, planes, scale, out, state, ws, group):
+def sharded_forward(lib, desc, sizes, buf, q, k, v, planes, scale, out, state, ws, group,
+                    den=None):
     from .functional import _ptr, _rt, _stream
     total = buf.floats(sizes.total_bytes) if desc.causal else None
     check(lib.race_forward_reduce(desc, _rt(k), _rt(v), _ptr(planes), _ptr(scale), _ptr(state),
                                   _ptr(total), _ptr(ws), ws.numel(), _stream()))
     add = lambda off: check(lib.race_add_offset(desc, _ptr(state), _ptr(off), 0, _stream()))
     exchange_forward_state(state, total, bool(desc.causal), group, add)
-    check(lib.race_forward_readout(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale),
-                                   _ptr(state), _rt(out), _ptr(ws), ws.numel(), _stream()))
+    check(lib.race_forward_readout_ex(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale),
+                                      _ptr(state), _rt(out), _ptr(den), _ptr(ws), ws.numel(),
+                                      _stream()))
 
 
 def sharded_backward(lib, desc, sizes, buf, q, k, v, planes, scale, state, dout, dq, dk, dv,
-                     dscale, gstate, ws, group):
+                     dscale, gstate, ws, group, dden=None):
     from .functional import _ptr, _rt, _stream
     total = buf.floats(sizes.total_bytes) if desc.causal else None
-    check(lib.race_backward_q(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale),
-                              _ptr(state), _rt(dout), _rt(dq), _ptr(dscale), _ptr(gstate),
-                              _ptr(total), _ptr(ws), ws.numel(), _stream()))
+    check(lib.race_backward_q_ex(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale),
+                                 _ptr(state), _rt(dout), _ptr(dden), _rt(dq), _ptr(dscale),
+                                 _ptr(gstate), _ptr(total), _ptr(ws), ws.numel(), _stream()))
     slots = gstate if not desc.causal else gstate[: (sizes.num_chunks * sizes.slot_floats
                                                      * desc.ensembles * desc.batch * desc.heads)]
     add = lambda off: check(lib.race_add_offset(desc, _ptr(gstate), _ptr(off), 1, _stream()))

@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference project is mounted read-only:
 
-    python tests/golden/make_golden.py /path/to/reference
+    python tests/golden/make_golden.py /path/to/reference [all|global]
 
 It extracts the class definitions ``BatchedACE`` from ``misc/vit.py``
 (non-causal, lines 888-978) and from ``misc/race.py`` (causal, lines 26-142)
@@ -30,13 +30,14 @@ from torch import nn
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def load_class(path: str, name: str):
+def load_class(path: str, name: str, extra=None):
     src = open(path).read()
     tree = ast.parse(src)
     for node in tree.body:
         if isinstance(node, ast.ClassDef) and node.name == name:
             seg = ast.get_source_segment(src, node)
             ns = {"torch": torch, "nn": nn, "F": F, "itertools": itertools, "math": math}
+            ns.update(extra or {})
             exec(compile(seg, f"{path}:{name}", "exec"), ns)
             return ns[name]
     raise KeyError(name)
@@ -140,6 +141,57 @@ CASES = [
 ]
 
 
+class _Const(nn.Module):
+    """Stands in for a projection: returns a fixed leaf tensor whatever its input."""
+
+    def __init__(self, t):
+        super().__init__()
+        self.t = t
+
+    def forward(self, x):
+        return self.t
+
+
+def run_global_case(cls, *, B, T, H, dk, K, L, chunk, group, beta, masked, seed):
+    """The reference's CausalRACEAttention (misc/elsaa_causal_complete.py:438-571)
+    on its torch path, with the q/k/v projections replaced by the inputs
+    themselves and the output projection by the identity, so the fixture holds
+    the attention alone: out, d_token and the gradients of Q, K, V, log_beta."""
+    torch.manual_seed(seed)
+    att = cls(H * dk, H, 0.0, num_bits=K, num_tables=L, beta_init=beta, chunk_size=chunk,
+              chunk_group_size=group).double()
+    x = lambda: torch.randn(B, T, H * dk, dtype=torch.float32).double().requires_grad_(True)
+    q, k, v = x(), x(), x()
+    att.q, att.k, att.v, att.o = _Const(q), _Const(k), _Const(v), nn.Identity()
+    mask = None
+    if masked:
+        mask = (torch.rand(B, T) > 0.25).double()
+        mask[:, 0] = 1.0
+    out, d_token = att(torch.zeros(B, T, H * dk, dtype=torch.float64), mask=mask, return_den=True)
+    dout = torch.randn(out.shape, dtype=torch.float32).double()
+    gtok = torch.randn(d_token.shape, dtype=torch.float32).double()
+    ((out * dout).sum() + (d_token * gtok).sum()).backward()
+    res = dict(
+        q=q.detach().float().numpy(), k=k.detach().float().numpy(), v=v.detach().float().numpy(),
+        planes=att.planes.detach().float().numpy(), out=out.detach().numpy(),
+        d_token=d_token.detach().numpy(), dout=dout.float().numpy(), gtok=gtok.float().numpy(),
+        dq=q.grad.numpy(), dk=k.grad.numpy(), dv=v.grad.numpy(),
+        beta=np.float64(att.log_beta.detach().exp().clamp(1e-2, 20.0)),
+        dlog_beta=np.float64(att.log_beta.grad),
+        meta=np.array([B, T, H, dk, K, L, chunk, int(masked)], np.int64),
+    )
+    if masked:
+        res["mask"] = mask.float().numpy()
+    return res
+
+
+GLOBAL_CASES = [
+    # name, B, T, H, dk, K, L, chunk_size, chunk_group_size, beta_init, masked
+    ("g_k2l4_t40", 2, 40, 2, 64, 2, 4, 16, None, 1.0, False),
+    ("g_k3l3_t37_d32_mask", 1, 37, 3, 32, 3, 3, 8, 2, 0.7, True),
+]
+
+
 def main(ref_root: str):
     vit_cls = load_class(os.path.join(ref_root, "misc/vit.py"), "BatchedACE")
     race_cls = load_class(os.path.join(ref_root, "misc/race.py"), "BatchedACE")
@@ -160,5 +212,20 @@ def main(ref_root: str):
         print("wrote", path, os.path.getsize(path))
 
 
+def main_global(ref_root: str):
+    cls = load_class(os.path.join(ref_root, "misc/elsaa_causal_complete.py"), "CausalRACEAttention",
+                     {"_HAS_TRITON_RACE": False})
+    for i, (name, B, T, H, dk, K, L, C, g, beta, masked) in enumerate(GLOBAL_CASES):
+        res = run_global_case(cls, B=B, T=T, H=H, dk=dk, K=K, L=L, chunk=C, group=g, beta=beta,
+                              masked=masked, seed=200 + i)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **res)
+        print("wrote", path, os.path.getsize(path))
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    which = sys.argv[2] if len(sys.argv) > 2 else "all"     # all | global
+    if which == "all":
+        main(root)
+    main_global(root)

@@ -10,12 +10,49 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 def golden_files():
     """Attention fixtures (the reference's BatchedACE modules)."""
     return sorted(p for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
-                  if not os.path.basename(p).startswith("probs_"))
+                  if not os.path.basename(p).startswith(("probs_", "g_")))
 
 
 def probs_files():
     """Probability-export fixtures (the reference's race_bucket_probs_from_qk)."""
     return sorted(glob.glob(os.path.join(GOLDEN_DIR, "probs_*.npz")))
+
+
+def global_files():
+    """Global-normalisation fixtures (the reference's CausalRACEAttention)."""
+    return sorted(glob.glob(os.path.join(GOLDEN_DIR, "g_*.npz")))
+
+
+def load_global(path):
+    """A CausalRACEAttention fixture as flat streams.
+
+    q, k, v, dout: [B, T, H*dk] -> [B*H, T, dk]; the mask (if any) is applied to
+    k and v as the reference does before hashing; planes [L, K, dk] ->
+    [B*H, L*K, dk]; dden: the gradient the fixture's d_token loss puts on the
+    per-stream, table-summed denominator (d_token = mean_h(den) / L), zero
+    where d_token's clamp holds."""
+    z = np.load(path)
+    B, T, H, dk, K, L, C, masked = [int(x) for x in z["meta"]]
+    g = {k: z[k] for k in z.files}
+    split = lambda x: np.ascontiguousarray(
+        x.reshape(B, T, H, dk).transpose(0, 2, 1, 3).reshape(B * H, T, dk))
+    keep = g["mask"] if masked else np.ones((B, T), np.float32)
+    keep_s = np.repeat(keep, H, axis=0)[:, :, None]                   # [B*H, T, 1]
+    gtok = g["gtok"][..., 0]                                           # [B, T]
+    live = g["d_token"][..., 0] >= 1e-6
+    dden = np.repeat(np.where(live, gtok, 0.0) / (H * L), H, axis=0)
+    g.update(B=B, T=T, H=H, hd=dk, K=K, L=L, C=C, masked=bool(masked),
+             name=os.path.basename(path)[:-4], split=split, keep_s=keep_s, dden=dden,
+             qs=split(g["q"]), ks=split(g["k"]) * keep_s, vs=split(g["v"]) * keep_s,
+             douts=split(g["dout"]),
+             planes_s=np.broadcast_to(g["planes"].reshape(1, L * K, dk), (B * H, L * K, dk)))
+    return g
+
+
+def merge_heads(xs, B, H):
+    """[B*H, T, dk] -> [B, T, H*dk]."""
+    N, T, dk = xs.shape
+    return xs.reshape(B, H, T, dk).transpose(0, 2, 1, 3).reshape(B, T, H * dk)
 
 
 def load(path):

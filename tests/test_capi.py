@@ -53,6 +53,7 @@ def test_query_sizes(lib):
     assert sz.slot_floats == (S * D + S + 3) // 4 * 4
     assert sz.state_bytes == N * sz.slot_floats * 4
     assert sz.workspace_bytes > 0
+    assert lib.race_query(desc(causal=1, tokens=1000, chunk=128, normalize=1), sz) == 0
     assert lib.race_query(desc(causal=1, tokens=1000, chunk=128), sz) == 0
     # causal: one prefix slot per token range (32-token tiles), then alpha and
     # the float64 key mass of every tile behind the gradient slots
@@ -66,7 +67,7 @@ def test_query_sizes(lib):
 @pytest.mark.parametrize("bad,code", [
     (dict(head_dim=48), 2), (dict(num_bits=3, num_tables=5), 2), (dict(num_tables=0), 1),
     (dict(dtype=7), 1), (dict(tokens=-1), 1), (dict(num_bits=6, num_tables=1), 2),
-    (dict(batch=70000), 2),
+    (dict(batch=70000), 2), (dict(normalize=1), 2), (dict(causal=1, normalize=3), 1),
 ])
 def test_query_rejects(lib, bad, code):
     sz = _lib.RaceSizes()

@@ -132,3 +132,32 @@ def test_oracle_matches_reference_probs_export(path):
         np.testing.assert_allclose(dx, g[dname], rtol=1e-9, atol=1e-11)
         dl += ds * scale
     assert math.isclose(dl, float(g["dlogit_temp"]), rel_tol=1e-9, abs_tol=1e-12)
+
+
+@pytest.mark.parametrize("path", G.global_files(), ids=lambda p: p.split("/")[-1][:-4])
+def test_oracle_matches_reference_global_causal(path):
+    """causal_global reproduces the reference's CausalRACEAttention torch path
+    (misc/elsaa_causal_complete.py:520-571: chunked, padded, table-averaged,
+    optionally masked and chunk-grouped) run under autograd in float64: out,
+    d_token and the gradients of Q, K, V and log_beta."""
+    g = G.load_global(path)
+    B, H, L, K = g["B"], g["H"], g["L"], g["K"]
+    scale = 1.0 / float(g["beta"])
+    # the torch path averages num and den over the L tables before its
+    # clamp_min(1e-6): the same as a floor of L * 1e-6 on the table sum
+    eps = L * 1e-6
+    keep = g["keep_s"]
+    out, den, dq, dk, dv, ds = O.causal_global(
+        g["qs"], g["ks"], g["vs"], g["planes_s"], K, L, scale, dout=g["douts"] * keep,
+        dden=g["dden"], eps=eps)
+    rel = lambda a, b: float(np.abs(a - b).max() / np.abs(b).max())
+    assert rel(G.merge_heads(out * keep, B, H), g["out"]) < 1e-13
+    d_token = np.maximum(den.reshape(B, H, -1).mean(1) / L, 1e-6)
+    assert rel(d_token, g["d_token"][..., 0]) < 1e-13
+    assert rel(G.merge_heads(dv * keep, B, H), g["dv"]) < 1e-13
+    # the hash gradients pass through 1 - tanh^2 of projections up to ~17,
+    # where that factor (~1e-14) carries a relative rounding error of ~1e-2 in
+    # either implementation: 1e-7 of the largest element bounds the gap
+    assert rel(G.merge_heads(dq, B, H), g["dq"]) < 1e-7
+    assert rel(G.merge_heads(dk * keep, B, H), g["dk"]) < 1e-7
+    assert math.isclose(-ds * scale, float(g["dlog_beta"]), rel_tol=1e-7)
