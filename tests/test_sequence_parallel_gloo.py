@@ -19,6 +19,7 @@ from oracle import race_oracle as O
 from race_attention_b200.sequence_parallel import exchange_backward_state, exchange_forward_state
 
 N, T, D, K, L, SCALE, EPS = 2, 60, 8, 2, 2, 0.9, 1e-6
+MODES = ("nc", "bucket", "global")   # non-causal; causal per-bucket; causal global
 
 
 def data():
@@ -28,7 +29,9 @@ def data():
     return q, k, v, do, P
 
 
-def shard_fwd_bwd(rank, world, causal):
+def shard_fwd_bwd(rank, world, mode):
+    causal = mode != "nc"
+    glob = mode == "global"
     q, k, v, do, P = data()
     lo, hi = T * rank // world, T * (rank + 1) // world
     q, k, v, do = (x[:, lo:hi] for x in (q, k, v, do))
@@ -53,7 +56,11 @@ def shard_fwd_bwd(rank, world, causal):
         B0, A0 = state[..., :D].numpy(), state[..., D].numpy()
         Acum = A0[:, None] + np.cumsum(pK, 1)
         Bcum = B0[:, None] + np.cumsum(pK[..., None] * v[:, :, None], 1)
-        out = np.einsum("nts,ntsd->ntd", pQ, Bcum / (Acum[..., None] + EPS))
+        if glob:   # one denominator per token (the ELSAA form)
+            den = (pQ * Acum).sum(-1)
+            out = np.einsum("nts,ntsd->ntd", pQ, Bcum) / np.maximum(den, EPS)[..., None]
+        else:
+            out = np.einsum("nts,ntsd->ntd", pQ, Bcum / (Acum[..., None] + EPS))
     # ---- backward
     if not causal:
         gstate = torch.tensor(np.einsum("nts,ntd->nsd", pQ, do))
@@ -65,11 +72,19 @@ def shard_fwd_bwd(rank, world, causal):
         dA = -(dB * E).sum(-1)
         dv = np.einsum("nts,nsd->ntd", pK, dB)
         dpK = np.einsum("ntd,nsd->nts", v, dB) + dA[:, None]
+    elif glob:
+        dd = np.maximum(den, EPS)
+        W = pQ / dd[..., None]
+        R = np.einsum("ntd,ntsd->nts", do, Bcum)
+        gden = -(W * R).sum(-1) / dd
+        dpQ = R / dd[..., None] + Acum * gden[..., None]
+        alpha = pQ * gden[..., None]
     else:
         invA = 1.0 / (Acum + EPS)
         W = pQ * invA
         dpQ = np.einsum("ntd,ntsd->nts", do, Bcum) * invA
         alpha = -W * dpQ
+    if causal:
         GB = np.einsum("nts,ntd->nsd", W, do)
         GA = alpha.sum(1)
         gtotal = torch.tensor(np.concatenate([GB, GA[..., None]], -1))
@@ -93,9 +108,9 @@ def worker(rank, world, port, outdir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        for causal in (False, True):
-            res = shard_fwd_bwd(rank, world, causal)
-            np.savez(os.path.join(outdir, f"r{rank}_c{int(causal)}.npz"), out=res[0], dq=res[1],
+        for mode in MODES:
+            res = shard_fwd_bwd(rank, world, mode)
+            np.savez(os.path.join(outdir, f"r{rank}_{mode}.npz"), out=res[0], dq=res[1],
                      dk=res[2], dv=res[3], ds=res[4])
     finally:
         dist.destroy_process_group()
@@ -111,11 +126,14 @@ def test_sharded_equals_full_sequence(world):
     with tempfile.TemporaryDirectory() as td:
         mp.spawn(worker, args=(world, port, td), nprocs=world, join=True)
         q, k, v, do, P = data()
-        for causal in (False, True):
-            parts = [np.load(os.path.join(td, f"r{r}_c{int(causal)}.npz")) for r in range(world)]
+        for mode in MODES:
+            parts = [np.load(os.path.join(td, f"r{r}_{mode}.npz")) for r in range(world)]
             cat = lambda key: np.concatenate([p[key] for p in parts], axis=1)
-            ref = O.forward(q, k, v, P, K, L, SCALE, causal)
-            dq, dk, dv, ds = O.backward(q, k, v, P, K, L, SCALE, causal, do)
+            if mode == "global":
+                ref, _, dq, dk, dv, ds = O.causal_global(q, k, v, P, K, L, SCALE, dout=do, eps=EPS)
+            else:
+                ref = O.forward(q, k, v, P, K, L, SCALE, mode != "nc")
+                dq, dk, dv, ds = O.backward(q, k, v, P, K, L, SCALE, mode != "nc", do)
             np.testing.assert_allclose(cat("out"), ref, rtol=1e-9, atol=1e-11)
             np.testing.assert_allclose(cat("dq"), dq, rtol=1e-9, atol=1e-11)
             np.testing.assert_allclose(cat("dk"), dk, rtol=1e-9, atol=1e-11)
