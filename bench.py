@@ -116,7 +116,7 @@ def dist_env():
 class Layer:
     """Preallocated buffers + the C-ABI calls of one fwd+bwd step."""
 
-    def __init__(self, causal, dtype, tokens, group, device, seed):
+    def __init__(self, causal, dtype, tokens, group, device, seed, normalize=0):
         from race_attention_b200 import _lib
         from race_attention_b200.functional import Buffers, make_desc, query
         self.lib = _lib.load()
@@ -128,7 +128,7 @@ class Layer:
         g0 = torch.Generator(device=device).manual_seed(0)   # identical planes on every rank
         self.planes = torch.randn((1, K * L, D), generator=g0, device=device)
         self.scale = torch.tensor(1.0, device=device)
-        self.desc = make_desc(shape, dtype, K, L, causal, 1e-6, 0, True)
+        self.desc = make_desc(shape, dtype, K, L, causal, 1e-6, 0, True, normalize)
         self.sizes = query(self.desc)
         self.buf = Buffers(self.sizes, device)
         self.out = torch.empty(shape, dtype=dtype, device=device)
@@ -326,13 +326,14 @@ def run_ours(args):
     torch.cuda.set_device(device)
     peak, peak_kind = load_peak()
 
-    configs = [(False, torch.float32), (True, torch.float32), (False, torch.bfloat16),
-               (True, torch.bfloat16)]
+    # (causal, dtype, normalize): the last is the global-normalised causal mode
+    configs = [(False, torch.float32, 0), (True, torch.float32, 0), (False, torch.bfloat16, 0),
+               (True, torch.bfloat16, 0), (True, torch.float32, 1)]
     results = []
     head = None
     clocks = None
-    for i, (causal, dtype) in enumerate(configs):
-        layer = Layer(causal, dtype, args.tokens, group, device, seed=1000 + rank)
+    for i, (causal, dtype, norm) in enumerate(configs):
+        layer = Layer(causal, dtype, args.tokens, group, device, seed=1000 + rank, normalize=norm)
         sampler = ClockSampler(device.index) if (i == 0 and rank == 0) else None
         if sampler:
             sampler.__enter__()
@@ -345,13 +346,15 @@ def run_ours(args):
         rec = {"causal": causal, "dtype": "f32" if dtype == torch.float32 else "bf16",
                "value": total_tokens / (ms / 1e3), "ms_per_step": ms,
                "step_roofline_frac": (args.tokens * 11 * D * esize / (ms / 1e3) / 1e9) / peak}
+        if norm:
+            rec["normalize"] = "global"
         if world == 1:
             ph = phase_times(layer, max(3, args.steps // 2), device)
             pb = layer.phase_bytes()
             rec["phases_ms"] = ph
             dom = max(ph, key=ph.get)
             ach = pb[dom] * args.tokens / (ph[dom] / 1e3) / 1e9
-            tr = TRAFFIC_2P18.get((causal, rec["dtype"], dom))
+            tr = None if norm else TRAFFIC_2P18.get((causal, rec["dtype"], dom))
             rec["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak,
                                "unit": "GB/s", "frac": ach / peak,
                                "traffic": None if tr is None else tr * args.tokens / 2 ** 18,
