@@ -256,13 +256,17 @@ def phase_times(layer, steps, device):
     return {n: acc[n] / steps for n in names}
 
 
-def e2e_rate(causal, dtype, tokens, steps, device, group=None):
-    """Same metric through the public autograd API with pinned HOST buffers:
-    H2D of q, k, v, dO and D2H of out, dq, dk, dv inside the timed region.
-    Every rank runs its own shard of the sequence (race_attention(...,
-    group=...)); the time is taken with CUDA events on the launching stream
-    (the copies are on it) and the maximum over ranks is used."""
+def e2e_rate(causal, dtype, tokens, steps, device, group=None, pipelined=True):
+    """Same metric through a public API with pinned HOST buffers: H2D of q, k,
+    v, dO and D2H of out, dq, dk, dv inside the timed region, every step.
+    pipelined: ``streaming.fwd_bwd_host`` (token chunks, copies on side
+    streams overlapping the kernels and each other); otherwise the autograd
+    path (``race_attention`` + ``backward``) with whole-tensor copies on the
+    launching stream.  Every rank runs its own shard of the sequence; the time
+    is taken with CUDA events on the launching stream (which waits for the
+    copy streams) and the maximum over ranks is used."""
     from race_attention_b200 import race_attention
+    from race_attention_b200.streaming import fwd_bwd_host
     world = 1 if group is None else torch.distributed.get_world_size(group)
     rank = 0 if group is None else torch.distributed.get_rank(group)
     g = torch.Generator().manual_seed(1 + rank)
@@ -272,7 +276,7 @@ def e2e_rate(causal, dtype, tokens, steps, device, group=None):
     planes = torch.randn((1, K * L, D), generator=torch.Generator().manual_seed(0)).to(device)
     lt = torch.zeros((), device=device, requires_grad=True)
 
-    def step():
+    def step_autograd():
         q, k, v, do = (h.to(device, non_blocking=True) for h in host)
         for t in (q, k, v):
             t.requires_grad_(True)
@@ -283,11 +287,23 @@ def e2e_rate(causal, dtype, tokens, steps, device, group=None):
             dst.copy_(src.detach(), non_blocking=True)
         lt.grad = None
 
+    def step_pipelined():
+        sc = lt.exp().clamp(1e-2, 20.0)
+        *_, ds = fwd_bwd_host(*host, planes, K, L, sc.detach(), causal=causal, device=device,
+                              outputs=outs, group=group)
+        # the temperature gradient through exp().clamp(), as autograd would give it
+        torch.autograd.backward(sc, ds)
+        lt.grad = None
+
+    step = step_pipelined if pipelined else step_autograd
     step()
     dt = timed(step, steps, 0, group, device) / 1e3
     nbytes = tokens * D * torch.tensor([], dtype=dtype).element_size() * 4
     return {"value": world * tokens / dt, "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
-            "d2h_bytes_per_step": nbytes, "steps": steps, "per_rank_shard_tokens": tokens}
+            "d2h_bytes_per_step": nbytes, "steps": steps, "per_rank_shard_tokens": tokens,
+            "api": ("race_attention_b200.streaming.fwd_bwd_host (pinned host buffers, "
+                    "chunked copies overlapping the kernels)") if pipelined else
+                   "race_attention autograd on device copies of pinned host buffers"}
 
 
 def cpu_rate(causal, tokens, budget_s=10.0, iters_max=50):
@@ -395,6 +411,8 @@ def run_ours(args):
     torch.cuda.empty_cache()
     if not args.no_e2e:
         line["e2e"] = e2e_rate(False, torch.float32, args.tokens, args.e2e_steps, device, group)
+        line["e2e_autograd"] = e2e_rate(False, torch.float32, args.tokens, args.e2e_steps, device,
+                                        group, pipelined=False)
     if world > 1:
         torch.distributed.barrier()
     if rank == 0 and not args.no_cpu and world == 1:
