@@ -803,11 +803,11 @@ template <int D, int SPAD>
 struct ReduceLay {
   static constexpr int NTH = 4;           // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;     // bucket columns
-  static constexpr int NFULL = 2;
+  static constexpr int NFULL = 4;                       // k slots 0, 1; v slots 2, 3
   static constexpr int KX = 0;                          // [2] k slots (landed, then 2 parts)
-  static constexpr int VX = KX + 2 * Slot<D>::FLOATS;   // [2] landed v tiles
-  static constexpr int VP = VX + 2 * Slot<D>::FLOATS;   // v parts hi, mid, lo: [TT x D] each
-  static constexpr int PK3 = VP + 3 * TT * D / 2;       // pK parts: [TT x 3 SP] = [hi | mid | lo]
+  static constexpr int VX = KX + 2 * Slot<D>::FLOATS;   // [2] v slots (landed, then hi | mid)
+  static constexpr int VL = VX + 2 * Slot<D>::FLOATS;   // [2] third part of v: [TT x D] each
+  static constexpr int PK3 = VL + TT * D;               // pK parts: [TT x 3 SP] = [hi | mid | lo]
   static constexpr int PS = PK3 + 3 * TT * SP / 2;      // bf16 [2*PJ x D] planes [hi; lo]
   static constexpr int BAR = PS + PJ * D;
   static constexpr int FLOATS = BAR + 16 + 256;
@@ -835,7 +835,6 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
   constexpr bool F32 = sizeof(T) == 4;
   T5_PROLOGUE
   (void)cur_n;
-  bf16* vp = reinterpret_cast<bf16*>(sm + LY::VP);
   bf16* pk3 = reinterpret_cast<bf16*>(sm + LY::PK3);
   bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
   for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
@@ -854,38 +853,61 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
     for (int a = 0; a < MYG; ++a)
 #pragma unroll
       for (int b = 0; b < G::GB; ++b) mass[a][b] = 0.f;
-    auto load = [&](int j) {
+    // k and v of a slot land on separate barriers: the k slot is free once
+    // the projection MMAs of its previous tile are done, the v slot (whose
+    // parts the state MMAs read in place) once the state MMAs are.
+    auto load_one = [&](int j, int which) {   // which 0: k, 1: v
       if (failed) return;
-      inflight |= 1u << (j & 1);
+      const int f = 2 * which + (j & 1);
+      inflight |= 1u << f;
       if (tid == 0) {
-        float* const dsts[2] = {sm + LY::KX + (j & 1) * Slot<D>::FLOATS,
-                                sm + LY::VX + (j & 1) * Slot<D>::FLOATS};
-        const Layout* const lay[2] = {&prm.lk, &prm.lv};
-        tma_tile<T, D, 2>(maps, dsts, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j & 1));
+        using BX = Box<T, D>;
+        const int h = n % prm.H, b = (n / prm.H) % prm.B, mm = n / (prm.H * prm.B);
+        const Layout& lay = which ? prm.lv : prm.lk;
+        char* dst = reinterpret_cast<char*>(sm + (which ? LY::VX : LY::KX) + (j & 1) * Slot<D>::FLOATS);
+        fence_async_smem();
+        bar_expect_tx(full + f, (uint32_t)BX::BYTES);
+#pragma unroll
+        for (int x = 0; x < BX::NB; ++x)
+          tma_load5(dst + x * TT * BX::IB, &maps.map[which], x * BX::IB / (int)sizeof(T),
+                    (int)(it.t0 + (int64_t)j * TT), h, b, lay.sm == 0 ? 0 : mm, full + f);
       }
     };
-    // Per tile i: k parts -> MMA proj(i) || [wait state(i-1)] v parts ->
-    // probabilities -> pK parts -> MMA state(i) || next tile
-    if (it.ntiles > 0) load(0);
+    auto landed = [&](int f) {
+      T5_WAIT(full + f, (phF >> f) & 1);
+      if (!failed) {
+        phF ^= 1u << f;
+        inflight &= ~(1u << f);
+      }
+    };
+    // Per tile i: k and v parts (v in place) -> MMA proj(i) -> [proj(i), and so
+    // state(i-1), done] load v(i+1) -> probabilities -> pK parts -> MMA state(i)
+    if (it.ntiles > 0) {
+      load_one(0, 0);
+      load_one(0, 1);
+    }
     for (int i = 0; i < it.ntiles; ++i) {
       const int64_t tile0 = it.t0 + (int64_t)i * TT;
       float* KXt = sm + LY::KX + (i & 1) * Slot<D>::FLOATS;
       float* VXt = sm + LY::VX + (i & 1) * Slot<D>::FLOATS;
-      if (i + 1 < it.ntiles) load(i + 1);
-      T5_WAIT(full + (i & 1), (phF >> (i & 1)) & 1);
-      if (!failed) {
-        phF ^= 1u << (i & 1);
-        inflight &= ~(1u << (i & 1));
-      }
+      bf16* vl = reinterpret_cast<bf16*>(sm + LY::VL) + (i & 1) * TT * D;
+      if (i + 1 < it.ntiles) load_one(i + 1, 0);
+      landed(i & 1);
+      landed(2 + (i & 1));
       const bool valid = tile0 + row < it.t1;
-      float y[W];
       {
-        float x[W];
+        float x[W], y[W];
         read_cols<T, D, W>(KXt, row, sub * W, x);
         read_cols<T, D, W>(VXt, row, sub * W, y);
+        if (!valid) {   // v rows past the range are zero
+#pragma unroll
+          for (int c = 0; c < W; ++c) y[c] = 0.f;
+        }
         __syncthreads();
         put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), nullptr, row,
                                     sub * W, x);
+        put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), vl, row,
+                                    sub * W, y);
       }
       fence_async_smem();
       fence_before();
@@ -896,18 +918,13 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
                                         Slot<D>::part(KXt, 1), nullptr, F32 ? 2 : 1, ps, false);
         commit(barA);
       }
-      if (i > 0) {   // the previous tile's state MMAs read the v and pK parts
+      T5_WAIT(barA, phA);   // MMAs complete in order: state(i-1) is done too
+      phA ^= 1;
+      if (i > 0) {
         T5_WAIT(barB, phB);
         phB ^= 1;
       }
-      // v parts (rows past the range are zero)
-      if (!valid) {
-#pragma unroll
-        for (int c = 0; c < W; ++c) y[c] = 0.f;
-      }
-      put_cols<D, W, 3>(vp, vp + TT * D, vp + 2 * TT * D, row, sub * W, y);
-      T5_WAIT(barA, phA);
-      phA ^= 1;
+      if (i + 1 < it.ntiles) load_one(i + 1, 1);
       fence_after();
       {
         static_assert(MYG == 1, "one bucket group per thread");
@@ -947,11 +964,12 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
       if (tid == 0 && !failed) {
         fence_after();
         // state^T[d][s-block j] += sum_a v_a^T . pK_j  (v_a, pK MN-major over the tile's tokens)
+        const bf16* va[3] = {Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), vl};
 #pragma unroll
-        for (int a = 0; a < 3; ++a)
+        for (int a = 0; a < (F32 ? 3 : 1); ++a)   // bf16 v is exact in its first part
 #pragma unroll
           for (int ks = 0; ks < TT / 16; ++ks)
-            mma(tbase + LY::C_ST, desc_mn<D>(vp + a * TT * D, ks), desc_mn<3 * SP>(pk3, ks),
+            mma(tbase + LY::C_ST, desc_mn<D>(va[a], ks), desc_mn<3 * SP>(pk3, ks),
                 idesc64_mn<3 * SP>(), i > 0 || a > 0 || ks > 0);
         commit(barB);
       }
