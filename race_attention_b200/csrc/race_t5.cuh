@@ -801,19 +801,20 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
 // ------------------------------------------------------------------ F1 reduce
 template <int D, int SPAD>
 struct ReduceLay {
-  static constexpr int NTH = 4;           // threads per token
+  static constexpr int NTH = 2;           // threads per token (two CTAs per SM)
   static constexpr int SP = (SPAD + 15) / 16 * 16;     // bucket columns
-  static constexpr int NFULL = 4;                       // k slots 0, 1; v slots 2, 3
-  static constexpr int KX = 0;                          // [2] k slots (landed, then 2 parts)
-  static constexpr int VX = KX + 2 * Slot<D>::FLOATS;   // [2] v slots (landed, then hi | mid)
-  static constexpr int VL = VX + 2 * Slot<D>::FLOATS;   // [2] third part of v: [TT x D] each
-  static constexpr int PK3 = VL + TT * D;               // pK parts: [TT x 3 SP] = [hi | mid | lo]
+  static constexpr int NFULL = 2;                       // k slot 0, v slot 1
+  static constexpr int KX = 0;                          // k slot (landed, then 2 parts)
+  static constexpr int VX = KX + Slot<D>::FLOATS;       // v slot (landed, then hi | mid)
+  static constexpr int VL = VX + Slot<D>::FLOATS;       // third part of v: [TT x D]
+  static constexpr int PK3 = VL + TT * D / 2;           // pK parts: [TT x 3 SP] = [hi | mid | lo]
   static constexpr int PS = PK3 + 3 * TT * SP / 2;      // bf16 [2*PJ x D] planes [hi; lo]
   static constexpr int BAR = PS + PJ * D;
   static constexpr int FLOATS = BAR + 16 + 256;
   static constexpr int TCOLS = 256;   // PROJ [0, 32), STATE [128, 128 + 3 SP) (M = 64)
   static constexpr int C_PROJ = 0, C_ST = 128;
   static_assert(3 * TT * SP / 2 >= TT * SP, "pK area doubles as the mass scratch");
+  static_assert(FLOATS * 4 <= 113 * 1024, "two CTAs per SM");
 };
 
 // Per range: B[s][d] = sum_t pK[t][s] v[t][d] and A[s] = sum_t pK[t][s] into
@@ -825,7 +826,7 @@ struct ReduceLay {
 // v . dB - dB . E loses it); the bucket mass is summed by the threads that
 // own each bucket group.
 template <typename T, int D, int SPAD, int K>
-__global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
+__global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
     k_t5_reduce(const Params prm, const __grid_constant__ TmaMaps maps) {
   using LY = ReduceLay<D, SPAD>;
   constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
@@ -853,18 +854,19 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
     for (int a = 0; a < MYG; ++a)
 #pragma unroll
       for (int b = 0; b < G::GB; ++b) mass[a][b] = 0.f;
-    // k and v of a slot land on separate barriers: the k slot is free once
-    // the projection MMAs of its previous tile are done, the v slot (whose
-    // parts the state MMAs read in place) once the state MMAs are.
+    // One slot each for k and v (two CTAs per SM hide each other's load
+    // latency), landing on separate barriers: the k slot is free once the
+    // projection MMAs of the previous tile are done, the v slot (whose parts
+    // the state MMAs read in place) once the state MMAs are.
     auto load_one = [&](int j, int which) {   // which 0: k, 1: v
       if (failed) return;
-      const int f = 2 * which + (j & 1);
+      const int f = which;
       inflight |= 1u << f;
       if (tid == 0) {
         using BX = Box<T, D>;
         const int h = n % prm.H, b = (n / prm.H) % prm.B, mm = n / (prm.H * prm.B);
         const Layout& lay = which ? prm.lv : prm.lk;
-        char* dst = reinterpret_cast<char*>(sm + (which ? LY::VX : LY::KX) + (j & 1) * Slot<D>::FLOATS);
+        char* dst = reinterpret_cast<char*>(sm + (which ? LY::VX : LY::KX));
         fence_async_smem();
         bar_expect_tx(full + f, (uint32_t)BX::BYTES);
 #pragma unroll
@@ -880,20 +882,19 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
         inflight &= ~(1u << f);
       }
     };
-    // Per tile i: k and v parts (v in place) -> MMA proj(i) -> [proj(i), and so
-    // state(i-1), done] load v(i+1) -> probabilities -> pK parts -> MMA state(i)
+    // Per tile i: k and v parts (v in place) -> MMA proj(i) -> load k(i+1) ->
+    // probabilities -> pK parts -> MMA state(i) -> [state(i) done] load v(i+1)
     if (it.ntiles > 0) {
       load_one(0, 0);
       load_one(0, 1);
     }
     for (int i = 0; i < it.ntiles; ++i) {
       const int64_t tile0 = it.t0 + (int64_t)i * TT;
-      float* KXt = sm + LY::KX + (i & 1) * Slot<D>::FLOATS;
-      float* VXt = sm + LY::VX + (i & 1) * Slot<D>::FLOATS;
-      bf16* vl = reinterpret_cast<bf16*>(sm + LY::VL) + (i & 1) * TT * D;
-      if (i + 1 < it.ntiles) load_one(i + 1, 0);
-      landed(i & 1);
-      landed(2 + (i & 1));
+      float* KXt = sm + LY::KX;
+      float* VXt = sm + LY::VX;
+      bf16* vl = reinterpret_cast<bf16*>(sm + LY::VL);
+      landed(0);
+      landed(1);
       const bool valid = tile0 + row < it.t1;
       {
         float x[W], y[W];
@@ -918,20 +919,15 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
                                         Slot<D>::part(KXt, 1), nullptr, F32 ? 2 : 1, ps, false);
         commit(barA);
       }
-      T5_WAIT(barA, phA);   // MMAs complete in order: state(i-1) is done too
+      T5_WAIT(barA, phA);
       phA ^= 1;
-      if (i > 0) {
-        T5_WAIT(barB, phB);
-        phB ^= 1;
-      }
-      if (i + 1 < it.ntiles) load_one(i + 1, 1);
+      if (i + 1 < it.ntiles) load_one(i + 1, 0);
       fence_after();
       {
-        static_assert(MYG == 1, "one bucket group per thread");
-#pragma unroll 1
-        for (int gi = sub; gi < NG; gi += NTH) {
-          const int a = 0;
-          {
+#pragma unroll
+        for (int a = 0; a < MYG; ++a) {
+          const int gi = sub + a * NTH;
+          if (gi < NG) {
             float pj[G::GK], p[G::GB], h[G::GK];
             const bool has = gi * G::GK < PJ;
             tld_group<G::GK, 2>(tlane + LY::C_PROJ, has ? gi * G::GK : 0, pj);
@@ -973,6 +969,11 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
                 idesc64_mn<3 * SP>(), i > 0 || a > 0 || ks > 0);
         commit(barB);
       }
+      if (i + 1 < it.ntiles) {   // the state MMAs read the v slot in place
+        T5_WAIT(barB, phB);
+        phB ^= 1;
+        load_one(i + 1, 1);
+      }
       if (T5_VOTE()) break;
     }
     if (failed) break;
@@ -997,9 +998,11 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 1)
       fence_before();
       // bucket mass: per-thread sums -> scratch (pK area is free) -> fixed-order sum
       float* ms = sm + LY::PK3;
-      if (sub < NG)
 #pragma unroll
-        for (int b = 0; b < G::GB; ++b) ms[row * SP + sub * G::GB + b] = mass[0][b];
+      for (int a = 0; a < MYG; ++a)
+        if (sub + a * NTH < NG)
+#pragma unroll
+          for (int b = 0; b < G::GB; ++b) ms[row * SP + (sub + a * NTH) * G::GB + b] = mass[a][b];
       __syncthreads();
       if (tid < prm.S) {
         float tot = 0.f;
