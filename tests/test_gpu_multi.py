@@ -1,7 +1,8 @@
 """Sequence sharding over NCCL on 2 GPUs (skipped with fewer than 2).
 
 Each rank runs the library on its contiguous token range through the public
-``race_attention(..., group=pg)`` call; the exchange between the split entry
+``race_attention(..., group=pg)`` call (and, non-causal, the host-buffer
+``streaming.fwd_bwd_host(..., group=pg)``); the exchange between the split entry
 points is one NCCL collective per direction.  The concatenated shards must
 match the float64 oracle on the whole sequence (1e-4 relative L2), and the
 temperature gradient must agree on every rank.
@@ -52,6 +53,15 @@ def _worker(rank, world, port, outdir):
             f = lambda x: x.detach().squeeze(3).squeeze(0).double().cpu().numpy()
             np.savez(os.path.join(outdir, f"r{rank}_c{int(causal)}.npz"), out=f(out),
                      dq=f(qt.grad), dk=f(kt.grad), dv=f(vt.grad), ds=float(sc.grad))
+        # the host-buffer pipeline, sharded the same way (non-causal)
+        from race_attention_b200.streaming import fwd_bwd_host
+        h = lambda a: torch.tensor(a[:, lo:hi]).unsqueeze(0).unsqueeze(3).contiguous().pin_memory()
+        out, dq, dk, dv, ds = fwd_bwd_host(h(q), h(k), h(v), h(dout), torch.tensor(planes), K, L,
+                                           1.3, device=dev, chunks=3, group=dist.group.WORLD)
+        torch.cuda.current_stream(dev).synchronize()
+        g = lambda x: x.squeeze(3).squeeze(0).double().numpy()
+        np.savez(os.path.join(outdir, f"r{rank}_host.npz"), out=g(out), dq=g(dq), dk=g(dk),
+                 dv=g(dv), ds=float(ds))
         torch.cuda.synchronize()
     finally:
         dist.destroy_process_group()
@@ -67,9 +77,9 @@ def test_two_gpu_sharded_matches_oracle():
     q, k, v, dout, planes = _data()
     with tempfile.TemporaryDirectory() as td:
         mp.spawn(_worker, args=(2, port, td), nprocs=2, join=True)
-        for causal in (False, True):
+        for causal, tag in ((False, "c0"), (True, "c1"), (False, "host")):
             scale = 8.0 if causal else 1.3
-            parts = [np.load(os.path.join(td, f"r{r}_c{int(causal)}.npz")) for r in range(2)]
+            parts = [np.load(os.path.join(td, f"r{r}_{tag}.npz")) for r in range(2)]
             cat = lambda key: np.concatenate([p[key] for p in parts], axis=1)
             P = np.broadcast_to(planes, (N,) + planes.shape[1:])
             if causal:
