@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define RACE_ABI_VERSION 2
+#define RACE_ABI_VERSION 3
 
 typedef enum {
   RACE_OK = 0,
@@ -59,8 +59,22 @@ typedef enum {
   RACE_ERR_ALIGN = 3,        /* pointer or stride breaks the vector alignment   */
   RACE_ERR_WORKSPACE = 4,    /* workspace smaller than race_query() asked for   */
   RACE_ERR_CUDA = 5,         /* a CUDA launch failed (see race_last_cuda_error) */
-  RACE_ERR_TOO_LARGE = 6     /* shape needs more than the static scratch holds  */
+  RACE_ERR_TOO_LARGE = 6,    /* shape needs more than the static scratch holds  */
+  RACE_ERR_DEVICE = 7        /* a kernel gave up on a bounded device-side wait  */
 } race_status_t;
+
+/* race_desc_t.flags bits. */
+#define RACE_FLAG_STRICT_TMA 1u   /* never fall back to the mma.sync kernels: a layout
+                                     the copy engine cannot map (a broadcast batch or
+                                     head axis) returns RACE_ERR_UNSUPPORTED instead */
+#define RACE_FLAG_NORMALIZE_QK 2u /* hash L2-normalised q and k (q/|q|, k/|k|); the
+                                     values and the output are unchanged.  Off by
+                                     default: the reference never normalises on the
+                                     RACE path, and tanh is not scale-invariant */
+
+/* Bits of the device status word (race_device_status). */
+#define RACE_DEV_TIMEOUT 1u  /* a bounded wait ran out; outputs of that call are partial */
+#define RACE_DEV_STUCK 2u    /* after a timeout, copies or MMAs in flight did not drain */
 
 typedef enum { RACE_F32 = 0, RACE_BF16 = 1 } race_dtype_t;
 
@@ -86,7 +100,7 @@ typedef struct {
   int32_t causal;         /* 0: non-causal (misc/vit.py), 1: prefix mean         */
   int32_t head_dim;       /* d: 32 or 64                                         */
   int32_t num_bits;       /* K hyperplanes per table (R = 2^K)                   */
-  int32_t num_tables;     /* L tables; S = L * 2^K <= 32, L*K <= 16              */
+  int32_t num_tables;     /* L tables; S = L * 2^K <= 64, L*K <= 16              */
   int32_t ensembles;      /* M                                                   */
   int32_t batch;          /* B                                                   */
   int32_t heads;          /* H                                                   */
@@ -96,6 +110,10 @@ typedef struct {
   float eps;              /* added to the bucket mass (reference: 1e-6); GLOBAL:
                              the floor of the per-token denominator             */
   int32_t normalize;      /* race_norm_t (0 = BUCKET)                            */
+  uint32_t flags;         /* RACE_FLAG_* bits (0 = default behaviour)            */
+  int32_t wait_polls;     /* polls of each bounded device wait before a kernel
+                             gives up (0 = the library default, 2^22).  A small
+                             value exists to test the timeout path.             */
 } race_desc_t;
 
 typedef struct {
@@ -112,6 +130,26 @@ const char* race_version(void);
 const char* race_strerror(int status);
 /* Text of the last CUDA error seen by this library on the calling thread. */
 const char* race_last_cuda_error(void);
+
+/* Comma-separated names of the kernels launched by the most recent
+ * entry-point call in this process (e.g. "t5_reduce,sum_partials,t5_readout";
+ * process-wide because frameworks often run the backward on a thread of
+ * their own; with concurrent callers it is one of the latest calls).  A
+ * launch that fell back from the tcgen05 + TMA kernels to the mma.sync ones is
+ * listed with the reason, e.g. "tc_bwd_q(fallback: dout: broadcast axis)". */
+const char* race_last_kernels(void);
+
+/* Device status word.  Every tcgen05 kernel bounds its waits on the copy
+ * engine and the tensor core; a wait that runs out ends the kernel early (its
+ * outputs are then partial) and ORs RACE_DEV_* bits into a status word kept
+ * in the last 64 bytes of the workspace the caller passed.  race_forward,
+ * race_backward and race_forward_static clear the word when they start;
+ * callers of the split phases clear it with race_status_clear at the start of
+ * their step.  race_device_status copies the word (one uint32) to `status`
+ * (device or pinned host memory) in stream order, without synchronising. */
+int race_status_clear(void* workspace, size_t workspace_bytes, cudaStream_t stream);
+int race_device_status(const void* workspace, size_t workspace_bytes, uint32_t* status,
+                       cudaStream_t stream);
 
 /* Validates the descriptor and reports the buffer sizes for it. */
 int race_query(const race_desc_t* desc, race_sizes_t* sizes);
@@ -244,7 +282,9 @@ int race_probs_backward(const race_desc_t* desc, race_tensor_t x, const float* p
  * capture.  All calls share the array: two calls that overlap on the GPU
  * (different streams, or different host threads) race and corrupt each other;
  * serialize them.  Every value a call reads from the array is written earlier
- * in the same call, so nothing is cleared between calls.  No saved state is
+ * in the same call; the only value cleared at the start of a call is the
+ * device status word at the array's end (read it with race_device_status on
+ * the array: pass workspace = NULL, workspace_bytes = 0).  No saved state is
  * returned, so there is no matching backward: use race_forward for training. */
 #define RACE_STATIC_SCRATCH_BYTES (8u << 20)
 int race_forward_static(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,

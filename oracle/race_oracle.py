@@ -56,6 +56,20 @@ def soft_hash(x, planes, K, L, scale):
     return p.reshape(N, T, L * (1 << K)), h
 
 
+# Sums of |du h| / scale^2 of the soft_hash_backward calls since the last
+# dscale_magnitude() -- the size of the terms the (heavily cancelling)
+# temperature gradient adds up, i.e. the scale of its rounding error.
+_DSCALE_ABS = []
+
+
+def dscale_magnitude(fn, *args, **kw):
+    """Runs a backward function and returns (its result, sum over its
+    soft_hash_backward calls of |du h| / scale^2)."""
+    _DSCALE_ABS.clear()
+    res = fn(*args, **kw)
+    return res, float(sum(_DSCALE_ABS))
+
+
 def soft_hash_backward(dp, p, h, planes, K, L, scale):
     """Back-propagate d(probs) through softmax, the corner matmul, /scale and tanh.
 
@@ -70,6 +84,7 @@ def soft_hash_backward(dp, p, h, planes, K, L, scale):
     du = g @ c                                            # [N,T,L,K]; u = h/scale
     dh = du / scale
     dscale = float(-(du * h).sum() / scale / scale)
+    _DSCALE_ABS.append(float(np.abs(du * h).sum() / scale / scale))
     dproj = (dh * (1.0 - h * h)).reshape(N, T, L * K)
     dx = np.einsum("ntj,njd->ntd", dproj, np.asarray(planes, np.float64), optimize=True)
     return dx, dscale

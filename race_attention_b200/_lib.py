@@ -14,6 +14,11 @@ LIB_PATH = os.path.join(_HERE, "librace_b200.so")
 
 RACE_OK = 0
 RACE_ERR_TOO_LARGE = 6
+RACE_ERR_DEVICE = 7
+RACE_FLAG_STRICT_TMA = 1
+RACE_FLAG_NORMALIZE_QK = 2
+RACE_DEV_TIMEOUT = 1
+RACE_DEV_STUCK = 2
 RACE_F32 = 0
 RACE_BF16 = 1
 RACE_NORM_BUCKET = 0
@@ -25,6 +30,7 @@ SYMBOLS = (
     "race_backward_q", "race_backward_kv", "race_add_offset", "race_forward_static",
     "race_probs", "race_probs_workspace", "race_probs_backward",
     "race_forward_ex", "race_forward_readout_ex", "race_backward_ex", "race_backward_q_ex",
+    "race_last_kernels", "race_status_clear", "race_device_status",
 )
 
 
@@ -41,7 +47,8 @@ class RaceDesc(ctypes.Structure):
                 ("batch", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("tokens", ctypes.c_int64), ("chunk", ctypes.c_int32),
                 ("shared_planes", ctypes.c_int32), ("eps", ctypes.c_float),
-                ("normalize", ctypes.c_int32)]
+                ("normalize", ctypes.c_int32), ("flags", ctypes.c_uint32),
+                ("wait_polls", ctypes.c_int32)]
 
 
 class RaceSizes(ctypes.Structure):
@@ -64,6 +71,9 @@ _SIGS = {
     "race_version": ([], ctypes.c_char_p),
     "race_strerror": ([ctypes.c_int], ctypes.c_char_p),
     "race_last_cuda_error": ([], ctypes.c_char_p),
+    "race_last_kernels": ([], ctypes.c_char_p),
+    "race_status_clear": ([_P, ctypes.c_size_t, _P], ctypes.c_int),
+    "race_device_status": ([_P, ctypes.c_size_t, _P, _P], ctypes.c_int),
     "race_query": ([ctypes.POINTER(RaceDesc), ctypes.POINTER(RaceSizes)], ctypes.c_int),
     "race_forward": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _T, _P, _P, ctypes.c_size_t, _P],
                      ctypes.c_int),
@@ -113,10 +123,18 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         return lib
 
 
+def last_kernels() -> list:
+    """Kernels the most recent entry-point call on this thread launched."""
+    txt = load().race_last_kernels().decode()
+    return [k for k in txt.split(",") if k] if txt else []
+
+
 def check(rc: int) -> None:
     if rc != RACE_OK:
         lib = load()
         msg = lib.race_strerror(rc).decode()
-        if rc == 5:
-            msg += ": " + lib.race_last_cuda_error().decode()
+        if rc in (2, 5):
+            extra = lib.race_last_cuda_error().decode()
+            if extra:
+                msg += ": " + extra
         raise RaceError(f"race_b200 error {rc}: {msg}")

@@ -57,8 +57,19 @@ def build(force: bool = False, verbose: bool = False) -> str:
             print(r.stderr, file=sys.stderr)
         return obj
 
-    with cf.ThreadPoolExecutor(len(SOURCES)) as ex:
-        objs = list(ex.map(compile_one, SOURCES))
+    hdrs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if not f.endswith(".cu")]
+    hdrs.append(os.path.join(ROOT, "include", "race_b200.h"))
+    newest_hdr = max(os.path.getmtime(h) for h in hdrs)
+
+    def fresh(src):
+        obj = os.path.join(objdir, src.replace(".cu", ".o"))
+        return (not force and os.path.exists(obj) and
+                os.path.getmtime(obj) > max(newest_hdr, os.path.getmtime(os.path.join(CSRC, src))))
+
+    todo = [s for s in SOURCES if not fresh(s)]
+    with cf.ThreadPoolExecutor(max(1, len(todo))) as ex:
+        list(ex.map(compile_one, todo))
+    objs = [os.path.join(objdir, s.replace(".cu", ".o")) for s in SOURCES]
     tmp = OUT + ".tmp"
     cmd = [cc, *ARCH, "-shared", "-o", tmp, *objs]   # cudart linked statically
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -12,6 +12,41 @@ namespace race {
 namespace {
 
 thread_local char g_cuda_err[256] = "";
+// Names of the kernels the most recent entry-point call launched
+// (race_last_kernels).  Process-wide, because frameworks often run the
+// backward on a thread of their own; the log is built per call on the
+// calling thread and published when the outermost entry point returns.
+std::mutex g_log_mu;
+char g_kernels_last[512] = "";
+char g_kernels_copy[512] = "";
+thread_local char g_kernels[512] = "";
+thread_local int g_api_depth = 0;
+
+// Clears the calling thread's log when the outermost entry point of a call
+// starts and publishes it when that entry point returns.
+struct ApiScope {
+  ApiScope() {
+    if (g_api_depth++ == 0) {
+      g_kernels[0] = '\0';
+      g_cuda_err[0] = '\0';
+    }
+  }
+  ~ApiScope() {
+    if (--g_api_depth == 0) {
+      std::lock_guard<std::mutex> lock(g_log_mu);
+      std::memcpy(g_kernels_last, g_kernels, sizeof(g_kernels));
+    }
+  }
+};
+
+void log_kernel(const char* name, const char* note = nullptr) {
+  const size_t n = std::strlen(g_kernels);
+  if (n + 2 >= sizeof(g_kernels)) return;
+  if (note != nullptr)
+    std::snprintf(g_kernels + n, sizeof(g_kernels) - n, "%s%s(%s)", n ? "," : "", name, note);
+  else
+    std::snprintf(g_kernels + n, sizeof(g_kernels) - n, "%s%s", n ? "," : "", name);
+}
 
 int cuda_fail(cudaError_t e) {
   std::snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", cudaGetErrorName(e),
@@ -181,7 +216,9 @@ int make_plan(const race_desc_t* d, Plan* p) {
   if (d->num_bits > 5) return RACE_ERR_UNSUPPORTED;
   const int S = d->num_tables << d->num_bits;
   const int LK = d->num_tables * d->num_bits;
-  if (S > 32 || LK > kLKMax) return RACE_ERR_UNSUPPORTED;
+  if (S > 64 || LK > kLKMax) return RACE_ERR_UNSUPPORTED;
+  // above 32 buckets only the tcgen05 non-causal kernels are built
+  if (S > 32 && d->causal) return RACE_ERR_UNSUPPORTED;
   const int64_t N64 = (int64_t)d->ensembles * d->batch * d->heads;
   if (N64 > 65535) return RACE_ERR_UNSUPPORTED;   // streams map to gridDim.y
   p->N = (int)N64;
@@ -230,7 +267,16 @@ size_t ws_bytes(const Plan& p) {
   return (p.part_floats + (p.dscale_floats + 3) / 4 * 4 + 64) * sizeof(float);
 }
 
+// The device status word: the last 64 bytes of the workspace the caller
+// passed (ws_bytes() keeps 256 bytes of slack behind the partial slots, so the
+// word never overlaps them whatever the shape).
+unsigned* status_word(void* ws, size_t bytes) {
+  const uintptr_t end = reinterpret_cast<uintptr_t>(ws) + bytes;
+  return reinterpret_cast<unsigned*>((end - 64) & ~uintptr_t(15));
+}
+
 struct Call {
+  bool strict = false;
   Plan plan;
   Params prm;
   float* part = nullptr;
@@ -274,8 +320,9 @@ int prepare(const race_desc_t* d, const float* planes, const float* scale, void*
   p.scale = scale;
   p.part = c->part;
   p.dscale_part = c->dscale_part;
-  // the last 16 floats of the workspace hold the sticky device error word
-  p.err = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + ws_bytes(c->plan) - 64);
+  p.err = status_word(ws, ws_bytes_given);
+  p.wait_polls = d->wait_polls > 0 ? d->wait_polls : (1 << 22);
+  c->strict = (d->flags & RACE_FLAG_STRICT_TMA) != 0;
   p.P = c->plan.P;
   p.CL = c->plan.CL;
   p.NC = c->plan.NC;
@@ -310,19 +357,33 @@ EncodeTiledFn encode_fn() {
 // t5::Box.  Returns false when the layout cannot be mapped (a broadcast batch
 // or head axis); the caller then uses the mma.sync kernels.
 bool encode_map(CUtensorMap* m, const void* base, const Layout& l, int dtype, const Params& p,
-                int D) {
+                int D, const char* name, char* why, size_t why_len) {
   const EncodeTiledFn fn = encode_fn();
-  if (fn == nullptr) return false;
+  if (fn == nullptr) {
+    std::snprintf(why, why_len, "cuTensorMapEncodeTiled not found");
+    return false;
+  }
   const int64_t es = dtype == RACE_F32 ? 4 : 2;
   const int64_t ext[5] = {D, p.T, p.H, p.B, l.sm == 0 ? 1 : p.M};
   const int64_t str[4] = {l.st, l.sh, l.sb, l.sm};
   cuuint64_t dims[5], strides[4];
   for (int i = 0; i < 5; ++i) dims[i] = (cuuint64_t)ext[i];
+  static const char* const axis[4] = {"token", "head", "batch", "ensemble"};
   for (int i = 0; i < 4; ++i) {
-    if (str[i] == 0 && ext[i + 1] > 1) return false;
+    if (str[i] == 0 && ext[i + 1] > 1) {
+      std::snprintf(why, why_len, "%s: broadcast %s axis", name, axis[i]);
+      return false;
+    }
     strides[i] = str[i] == 0 ? 16 : (cuuint64_t)(str[i] * es);
+    if (str[i] < 0) {
+      std::snprintf(why, why_len, "%s: negative %s stride", name, axis[i]);
+      return false;
+    }
   }
-  if (p.T >= (int64_t(1) << 31)) return false;
+  if (p.T >= (int64_t(1) << 31)) {
+    std::snprintf(why, why_len, "%s: more than 2^31 tokens", name);
+    return false;
+  }
   const int ib = (int)(D * es < 128 ? D * es : 128);
   const cuuint32_t box[5] = {(cuuint32_t)(ib / es), 128, 1, 1, 1};
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
@@ -331,20 +392,38 @@ bool encode_map(CUtensorMap* m, const void* base, const Layout& l, int dtype, co
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                         ib == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(why, why_len,
+                  "%s: encode error %d (strides %llu %llu %llu %llu B, dims %llu %llu %llu %llu %llu)",
+                  name, (int)r, (unsigned long long)strides[0], (unsigned long long)strides[1],
+                  (unsigned long long)strides[2], (unsigned long long)strides[3],
+                  (unsigned long long)dims[0], (unsigned long long)dims[1],
+                  (unsigned long long)dims[2], (unsigned long long)dims[3],
+                  (unsigned long long)dims[4]);
+    return false;
+  }
+  return true;
 }
 
-int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream) {
-  // RACE_MMA_SYNC=1 selects the warp-level mma.sync generation of the
-  // non-causal readout / key-value backward (for comparisons)
-  static const bool mma_sync = [] {
-    const char* e = std::getenv("RACE_MMA_SYNC");
-    return e != nullptr && e[0] == '1';
-  }();
-  if (mma_sync && id == K_NC_READOUT) id = K_NC_READOUT_SYNC;
-  if (mma_sync && id == K_NC_BWD_KV) id = K_NC_BWD_KV_SYNC;
-  if (mma_sync && id == K_NC_REDUCE) id = K_C_TOTALS;
-  if (mma_sync && id == K_NC_BWD_Q) id = K_NC_BWD_Q_SYNC;
+const char* kernel_name(KernelId id) {
+  switch (id) {
+    case K_NC_REDUCE: return "t5_reduce";
+    case K_NC_READOUT: return "t5_readout";
+    case K_NC_BWD_Q: return "t5_bwd_q";
+    case K_NC_BWD_KV: return "t5_bwd_kv";
+    case K_C_FWD: return "ctc_fwd";
+    case K_C_BWD_Q: return "ctc_bwd_q";
+    case K_C_BWD_KV: return "ctc_bwd_kv";
+    case K_NC_READOUT_SYNC: return "tc_readout";
+    case K_C_TOTALS: return "tc_reduce";
+    case K_NC_BWD_Q_SYNC: return "tc_bwd_q";
+    case K_NC_BWD_KV_SYNC: return "tc_bwd_kv";
+    default: return "?";
+  }
+}
+
+int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream,
+           const char* note = nullptr) {
   KernelInfo ki;
   const int K = d->num_bits, sp = c.plan.spad;
   bool ok;
@@ -365,27 +444,36 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
   if (ki.tma > 0) {
     bool ok_map = false;
     const int hd = d->head_dim;
+    char why[200] = "";
+    const size_t wl = sizeof(why);
     if (id == K_NC_READOUT)
-      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, hd) &&
-               encode_map(&maps.map[1], prm.out, prm.lo, d->dtype, prm, hd);
+      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, hd, "q", why, wl) &&
+               encode_map(&maps.map[1], prm.out, prm.lo, d->dtype, prm, hd, "out", why, wl);
     else if (id == K_NC_BWD_Q)
-      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, hd) &&
-               encode_map(&maps.map[1], prm.dout, prm.ldo, d->dtype, prm, hd) &&
-               encode_map(&maps.map[2], prm.dq, prm.ldq, d->dtype, prm, hd);
+      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, hd, "q", why, wl) &&
+               encode_map(&maps.map[1], prm.dout, prm.ldo, d->dtype, prm, hd, "dout", why, wl) &&
+               encode_map(&maps.map[2], prm.dq, prm.ldq, d->dtype, prm, hd, "dq", why, wl);
     else if (id == K_NC_BWD_KV)
-      ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, hd) &&
-               encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, hd) &&
-               encode_map(&maps.map[2], prm.dk, prm.ldk, d->dtype, prm, hd) &&
-               encode_map(&maps.map[3], prm.dv, prm.ldv, d->dtype, prm, hd);
+      ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, hd, "k", why, wl) &&
+               encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, hd, "v", why, wl) &&
+               encode_map(&maps.map[2], prm.dk, prm.ldk, d->dtype, prm, hd, "dk", why, wl) &&
+               encode_map(&maps.map[3], prm.dv, prm.ldv, d->dtype, prm, hd, "dv", why, wl);
     else if (id == K_NC_REDUCE)
-      ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, hd) &&
-               encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, hd);
+      ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, hd, "k", why, wl) &&
+               encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, hd, "v", why, wl);
     if (!ok_map) {   // layouts the copy engine cannot walk: warp-level kernels
+      char note[220];
+      std::snprintf(note, sizeof(note), "fallback: %s", why);
+      if (c.strict || c.plan.S > 32) {
+        log_kernel(kernel_name(id), note);
+        std::snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", kernel_name(id), why);
+        return RACE_ERR_UNSUPPORTED;
+      }
       const KernelId alt = id == K_NC_READOUT  ? K_NC_READOUT_SYNC
                            : id == K_NC_BWD_KV ? K_NC_BWD_KV_SYNC
                            : id == K_NC_BWD_Q  ? K_NC_BWD_Q_SYNC
                                                : K_C_TOTALS;
-      return launch(d, c, alt, stream);
+      return launch(d, c, alt, stream, note);
     }
   }
   void* args[] = {&prm, &maps};
@@ -396,6 +484,7 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
   }
   const cudaError_t e = cudaLaunchKernel(ki.fn, grid, dim3(ki.threads), args, ki.smem_bytes, stream);
   if (e != cudaSuccess) return cuda_fail(e);
+  log_kernel(kernel_name(id), note);
   return RACE_OK;
 }
 
@@ -405,12 +494,14 @@ int post(cudaStream_t) {
 }
 
 int sum_partials(const Call& c, float* out, cudaStream_t stream) {
+  log_kernel("sum_partials");
   dim3 grid((c.plan.SS + 31) / 32, c.plan.N), block(32, 32);
   k_sum_partials<<<grid, block, 0, stream>>>(c.part, c.plan.P, c.plan.SS, out);
   return post(stream);
 }
 
 int chunk_scan(const Call& c, float* slots, int reverse, float* total, cudaStream_t stream) {
+  log_kernel("chunk_scan");
   dim3 grid((c.plan.width + 31) / 32, c.plan.N), block(32, 32);
   k_chunk_scan<<<grid, block, 0, stream>>>(slots, c.plan.NC, c.plan.SS, c.plan.width, reverse,
                                            total);
@@ -418,6 +509,7 @@ int chunk_scan(const Call& c, float* slots, int reverse, float* total, cudaStrea
 }
 
 int dscale_final(const Call& c, int count, float* dscale, int accumulate, cudaStream_t stream) {
+  log_kernel("dscale_final");
   k_dscale_final<<<1, 1024, 0, stream>>>(c.dscale_part, count, c.prm.scale, dscale, accumulate);
   return post(stream);
 }
@@ -482,6 +574,7 @@ extern "C" {
 
 int race_probs(const race_desc_t* desc, race_tensor_t x, const float* planes, const float* scale,
                float* probs, cudaStream_t stream) {
+  ApiScope scope_;
   Plan plan;
   Params p;
   RACE_TRY(probs_params(desc, x, planes, scale, &plan, &p));
@@ -502,6 +595,7 @@ int race_probs_backward(const race_desc_t* desc, race_tensor_t x, const float* p
                         const float* scale, const float* dprobs, race_tensor_t dx, float* dscale,
                         int accumulate, void* workspace, size_t workspace_bytes,
                         cudaStream_t stream) {
+  ApiScope scope_;
   Plan plan;
   Params p;
   RACE_TRY(probs_params(desc, x, planes, scale, &plan, &p));
@@ -535,19 +629,32 @@ const char* race_strerror(int status) {
   switch (status) {
     case RACE_OK: return "ok";
     case RACE_ERR_INVALID: return "invalid argument";
-    case RACE_ERR_UNSUPPORTED: return "unsupported shape (d in {32,64}, L*2^K <= 32, L*K <= 16, K <= 5)";
+    case RACE_ERR_UNSUPPORTED: return "unsupported shape or layout (d in {32,64}, L*2^K <= 64, L*K <= 16, K <= 6; see race_last_cuda_error)";
     case RACE_ERR_ALIGN: return "pointer or stride not 16-byte aligned for vector access";
     case RACE_ERR_WORKSPACE: return "workspace missing or smaller than race_query() reported";
     case RACE_ERR_CUDA: return "CUDA error (see race_last_cuda_error)";
     case RACE_ERR_TOO_LARGE:
       return "state + scratch exceed RACE_STATIC_SCRATCH_BYTES (use race_forward with caller buffers)";
+    case RACE_ERR_DEVICE: return "a kernel gave up on a bounded device-side wait (outputs partial)";
     default: return "unknown status";
   }
 }
 
 const char* race_last_cuda_error(void) { return g_cuda_err; }
 
+const char* race_last_kernels(void) {
+  std::lock_guard<std::mutex> lock(g_log_mu);
+  std::memcpy(g_kernels_copy, g_kernels_last, sizeof(g_kernels_last));
+  return g_kernels_copy;
+}
+
+int race_status_clear(void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (workspace == nullptr || workspace_bytes < 64) return RACE_ERR_WORKSPACE;
+  return zero_fill(status_word(workspace, workspace_bytes), sizeof(unsigned), stream);
+}
+
 int race_query(const race_desc_t* desc, race_sizes_t* sizes) {
+  ApiScope scope_;
   if (sizes == nullptr) return RACE_ERR_INVALID;
   Plan p;
   RACE_TRY(make_plan(desc, &p));
@@ -564,6 +671,7 @@ int race_query(const race_desc_t* desc, race_sizes_t* sizes) {
 int race_forward_reduce(const race_desc_t* desc, race_tensor_t k, race_tensor_t v,
                         const float* planes, const float* scale, float* state, float* total,
                         void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  ApiScope scope_;
   Call c;
   RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
   if (state == nullptr) return RACE_ERR_INVALID;
@@ -599,6 +707,7 @@ int race_forward_readout_ex(const race_desc_t* desc, race_tensor_t q, race_tenso
                             race_tensor_t v, const float* planes, const float* scale,
                             const float* state, race_tensor_t out, float* den, void* workspace,
                             size_t workspace_bytes, cudaStream_t stream) {
+  ApiScope scope_;
   Call c;
   RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
   if (state == nullptr) return RACE_ERR_INVALID;
@@ -630,6 +739,7 @@ int race_forward_readout(const race_desc_t* desc, race_tensor_t q, race_tensor_t
                          const float* planes, const float* scale, const float* state,
                          race_tensor_t out, void* workspace, size_t workspace_bytes,
                          cudaStream_t stream) {
+  ApiScope scope_;
   return race_forward_readout_ex(desc, q, k, v, planes, scale, state, out, nullptr, workspace,
                                  workspace_bytes, stream);
 }
@@ -637,6 +747,8 @@ int race_forward_readout(const race_desc_t* desc, race_tensor_t q, race_tensor_t
 int race_forward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
                     const float* planes, const float* scale, race_tensor_t out, float* den,
                     float* state, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  ApiScope scope_;
+  RACE_TRY(race_status_clear(workspace, workspace_bytes, stream));
   RACE_TRY(race_forward_reduce(desc, k, v, planes, scale, state, nullptr, workspace,
                                workspace_bytes, stream));
   return race_forward_readout_ex(desc, q, k, v, planes, scale, state, out, den, workspace,
@@ -646,6 +758,7 @@ int race_forward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, r
 int race_forward(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
                  const float* planes, const float* scale, race_tensor_t out, float* state,
                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  ApiScope scope_;
   return race_forward_ex(desc, q, k, v, planes, scale, out, nullptr, state, workspace,
                          workspace_bytes, stream);
 }
@@ -655,6 +768,7 @@ int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k
                        race_tensor_t dout, const float* dden, race_tensor_t dq, float* dscale,
                        float* gstate, float* total, void* workspace, size_t workspace_bytes,
                        cudaStream_t stream) {
+  ApiScope scope_;
   Call c;
   RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
   if (state == nullptr || gstate == nullptr || dscale == nullptr) return RACE_ERR_INVALID;
@@ -704,6 +818,7 @@ int race_backward_q(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, r
                     const float* planes, const float* scale, const float* state,
                     race_tensor_t dout, race_tensor_t dq, float* dscale, float* gstate,
                     float* total, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  ApiScope scope_;
   return race_backward_q_ex(desc, q, k, v, planes, scale, state, dout, nullptr, dq, dscale, gstate,
                             total, workspace, workspace_bytes, stream);
 }
@@ -712,6 +827,7 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
                      const float* planes, const float* scale, const float* state,
                      const float* gstate, race_tensor_t dout, race_tensor_t dk, race_tensor_t dv,
                      float* dscale, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  ApiScope scope_;
   Call c;
   RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
   if (state == nullptr || gstate == nullptr || dscale == nullptr) return RACE_ERR_INVALID;
@@ -751,6 +867,7 @@ int race_backward(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, rac
                   const float* planes, const float* scale, const float* state, race_tensor_t dout,
                   race_tensor_t dq, race_tensor_t dk, race_tensor_t dv, float* dscale,
                   float* gstate, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  ApiScope scope_;
   return race_backward_ex(desc, q, k, v, planes, scale, state, dout, nullptr, dq, dk, dv, dscale,
                           gstate, workspace, workspace_bytes, stream);
 }
@@ -760,6 +877,8 @@ int race_backward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
                      race_tensor_t dout, const float* dden, race_tensor_t dq, race_tensor_t dk,
                      race_tensor_t dv, float* dscale, float* gstate, void* workspace,
                      size_t workspace_bytes, cudaStream_t stream) {
+  ApiScope scope_;
+  RACE_TRY(race_status_clear(workspace, workspace_bytes, stream));
   RACE_TRY(race_backward_q_ex(desc, q, k, v, planes, scale, state, dout, dden, dq, dscale, gstate,
                               nullptr, workspace, workspace_bytes, stream));
   return race_backward_kv(desc, q, k, v, planes, scale, state, gstate, dout, dk, dv, dscale,
@@ -768,6 +887,7 @@ int race_backward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
 
 int race_add_offset(const race_desc_t* desc, float* slots, const float* offset, int is_gradient,
                     cudaStream_t stream) {
+  ApiScope scope_;
   Plan p;
   RACE_TRY(make_plan(desc, &p));
   (void)is_gradient;  // both slot kinds carry [S][d] sums then [S] masses up front
@@ -815,6 +935,7 @@ int static_scratch(float** out) {
 extern "C" int race_forward_static(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
                                    race_tensor_t v, const float* planes, const float* scale,
                                    race_tensor_t out, cudaStream_t stream) {
+  ApiScope scope_;
   race_sizes_t sz;
   RACE_TRY(race_query(desc, &sz));
   const size_t state_bytes = (sz.state_bytes + 255) / 256 * 256;
@@ -825,4 +946,20 @@ extern "C" int race_forward_static(const race_desc_t* desc, race_tensor_t q, rac
   void* ws = reinterpret_cast<char*>(base) + state_bytes;
   return race_forward(desc, q, k, v, planes, scale, out, state, ws,
                       RACE_STATIC_SCRATCH_BYTES - state_bytes, stream);
+}
+
+extern "C" int race_device_status(const void* workspace, size_t workspace_bytes,
+                                  uint32_t* status, cudaStream_t stream) {
+  if (status == nullptr) return RACE_ERR_INVALID;
+  if (workspace == nullptr) {   // the allocation-free forward's array
+    float* base = nullptr;
+    RACE_TRY(static_scratch(&base));
+    workspace = base;
+    workspace_bytes = RACE_STATIC_SCRATCH_BYTES;
+  }
+  if (workspace_bytes < 64) return RACE_ERR_WORKSPACE;
+  const cudaError_t e =
+      cudaMemcpyAsync(status, status_word(const_cast<void*>(workspace), workspace_bytes),
+                      sizeof(uint32_t), cudaMemcpyDefault, stream);
+  return e == cudaSuccess ? RACE_OK : cuda_fail(e);
 }

@@ -29,7 +29,7 @@ struct KernelInfo {
 };
 
 // Padded bucket counts the kernels are instantiated for.
-constexpr int kSpadList[] = {8, 16, 20, 24, 32};
+constexpr int kSpadList[] = {8, 16, 20, 24, 32, 64};
 
 inline int spad_for(int S) {
   for (int s : kSpadList)

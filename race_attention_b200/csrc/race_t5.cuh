@@ -27,8 +27,8 @@
 // columns is bf16 number (r/8)*8C + (c/8)*64 + (r%8)*8 + c%8 -- 8-row x 16-byte
 // core matrices; descriptor leading offset 128 B (next 8 columns), stride
 // offset 16C B (next 8 rows); a K = 16 step advances the start by 256 B.
-// fp32 tiles are staged by cp.async in the same arrangement of 16-byte chunks
-// (chunk i of a tile at byte 16 i), then converted in place to hi | lo.
+// fp32 tiles land by TMA (box layout, see Box below) and are converted in
+// place to their bf16 parts.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -43,8 +43,9 @@ using bf16 = __nv_bfloat16;
 
 constexpr int TT = 128;   // tokens per tile = MMA M = TMEM lanes
 constexpr int PJ = 16;    // projection columns (L*K <= 16)
-constexpr int kWaitPolls = 1 << 22;   // bounded mbarrier polls before giving up
-constexpr unsigned kErrTimeout = 1u;  // device error bit: an MMA wait timed out
+constexpr int kWaitPolls = 1 << 22;   // polls of the drain waits after a timeout
+constexpr unsigned kErrTimeout = 1u;  // status bit: a main-loop wait ran out (RACE_DEV_TIMEOUT)
+constexpr unsigned kErrStuck = 2u;    // status bit: in-flight work did not drain (RACE_DEV_STUCK)
 
 __device__ __forceinline__ uint32_t saddr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -162,13 +163,32 @@ __device__ __forceinline__ bool bar_try(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking probe of the same phase (try_wait may suspend the thread for a
+// hardware-defined interval; this never does).
+__device__ __forceinline__ bool bar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(saddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
   for (int i = 0; i < kWaitPolls; ++i)
     if (bar_try(bar, parity)) return true;
   return false;
 }
-__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
-  for (int i = 0; i < kWaitPolls; ++i) {
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
+                                         int polls) {
+  if (polls < 64) {   // a short bound (the timeout test) counts non-blocking probes
+    for (int i = 0; i < polls; ++i)
+      if (bar_test(bar, parity)) return true;
+    *abort = 1;
+    return false;
+  }
+  for (int i = 0; i < polls; ++i) {
     if (bar_try(bar, parity)) return true;
     if ((i & 63) == 63 && *abort != 0) return false;
   }
@@ -599,13 +619,18 @@ struct ReadoutLay {
   static constexpr int C_PROJ = 0, C_OUT = 128;
 };
 
+// Up to 32 buckets: two k and two v slots (tile i+1 loads as tile i starts);
+// above 32 (LATE) one of each, reloaded once dk, dv of tile i-1 have left
+// through them.
 template <int D, int SPAD>
 struct BwdKVLay {
   static constexpr int NTH = 4;           // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;    // bucket columns (MMA K and N)
-  static constexpr int KX = 0;                         // [2] k slots (landed, then hi | mid)
-  static constexpr int VX = KX + 2 * Slot<D>::FLOATS;  // [2] v slots (landed, then hi | mid)
-  static constexpr int KL = VX + 2 * Slot<D>::FLOATS;  // bf16 [TT x D] third part of k
+  static constexpr bool LATE = SP > 32;
+  static constexpr int NS = LATE ? 1 : 2;              // k and v slots
+  static constexpr int KX = 0;                         // [NS] k slots (landed, then hi | mid)
+  static constexpr int VX = KX + NS * Slot<D>::FLOATS; // [NS] v slots (landed, then hi | mid)
+  static constexpr int KL = VX + NS * Slot<D>::FLOATS; // bf16 [TT x D] third part of k
   static constexpr int VL = KL + TT * D / 2;           // bf16 [TT x D] third part of v
   static constexpr int PK = VL + TT * D / 2;           // bf16 [TT x SP] hi, then lo
   static constexpr int DJ = PK + TT * SP;              // bf16 [TT x PJ] hi, then lo
@@ -613,14 +638,17 @@ struct BwdKVLay {
   static constexpr int PT = PS + 3 * PJ * D / 2;       // bf16 [2*D x PJ] planes^T [hi; lo]
   static constexpr int DB = PT + D * PJ;               // bf16 [3*SP x D] dB [hi; mid; lo]
   static constexpr int DBT = DB + 3 * SP * D / 2;      // bf16 [2*D x SP] dB^T [hi; lo]
-  static constexpr int DA = DBT + D * SP;              // [32] dA
-  static constexpr int RED = DA + 32;                  // [16] reductions
-  static constexpr int NFULL = 2;                       // tile-landed barriers
+  static constexpr int DA = DBT + D * SP;              // [SP] dA
+  static constexpr int RED = DA + SP;                  // [16] reductions
+  static constexpr int NFULL = NS;                      // tile-landed barriers
   static constexpr int BAR = RED + 16;                 // mbarriers + TMEM base slot
   static constexpr int FLOATS = BAR + 16 + 256;        // + slack for 1 KB alignment
-  // PROJ [0, 48), DPK [64, 64 + 3SP), DV [160, 160 + 2D), DK [288, 288 + 2D)
+  // PROJ [0, 48), DPK [64, 64 + 3SP), DV [C_DV, C_DV + 2D), DK [C_DK, C_DK + 2D)
   static constexpr int TCOLS = 512;
-  static constexpr int C_PROJ = 0, C_DPK = 64, C_DV = 160, C_DK = 288;
+  static constexpr int C_PROJ = 0, C_DPK = 64, C_DV = LATE ? 256 : 160, C_DK = LATE ? 384 : 288;
+  static_assert(C_DPK + 3 * SP <= C_DV && C_DV + 2 * D <= C_DK && C_DK + 2 * D <= TCOLS,
+                "tensor-memory columns");
+  static_assert(FLOATS * 4 <= 227 * 1024, "shared memory");
 };
 
 // A wait that times out sets the CTA's abort word (so the other threads'
@@ -630,7 +658,7 @@ struct BwdKVLay {
 // waits for its own copies in flight and frees its tensor memory.
 #define T5_WAIT(bar_, ph_)                                       \
   do {                                                           \
-    if (!bar_wait(bar_, ph_, abort_flag)) failed = true;         \
+    if (!bar_wait(bar_, ph_, abort_flag, prm.wait_polls)) failed = true; \
   } while (0)
 #define T5_VOTE()                                                \
   (__syncthreads_or(failed) ? (failed = true) : false)
@@ -663,13 +691,28 @@ struct BwdKVLay {
   const uint32_t tlane = tbase + ((uint32_t)((warp & 3) * 32) << 16);        \
   uint32_t phA = 0, phB = 0, phF = 0; /* phF bit s: parity of full[s] */   \
   uint32_t inflight = 0;              /* bit s: a tile of slot s in flight */\
+  uint32_t issA = 0, issB = 0;        /* thread 0: MMA commits issued     */\
   bool failed = false;                                                       \
   int cur_n = -1, cur_m = -1;
 
+// On the way out every thread waits (full poll count) for the tiles it saw
+// issued into its slots, thread 0 for its bulk stores and for the last MMA
+// commit of each barrier (MMAs complete in issue order, and at most one
+// commit per barrier is ever outstanding), so no copy or MMA still targets
+// this CTA's shared or tensor memory when it is freed.
 #define T5_EPILOGUE                                                          \
-  if (tid == 0) bulk_wait_all();                                             \
-  for (int s_ = 0; s_ < LY::NFULL; ++s_)                                     \
-    if ((inflight >> s_) & 1) bar_wait(full + s_, (phF >> s_) & 1);          \
+  {                                                                          \
+    bool drained_ = true;                                                    \
+    if (tid == 0) {                                                          \
+      bulk_wait_all();                                                       \
+      if (issA > 0 && !bar_wait(barA, (issA - 1) & 1)) drained_ = false;     \
+      if (issB > 0 && !bar_wait(barB, (issB - 1) & 1)) drained_ = false;     \
+    }                                                                        \
+    for (int s_ = 0; s_ < LY::NFULL; ++s_)                                   \
+      if ((inflight >> s_) & 1)                                              \
+        if (!bar_wait(full + s_, (phF >> s_) & 1)) drained_ = false;         \
+    if (!drained_) atomicOr(prm.err, kErrStuck);                             \
+  }                                                                          \
   if (tid == 0 && *abort_flag != 0) atomicOr(prm.err, kErrTimeout);          \
   fence_before();                                                            \
   __syncthreads();                                                           \
@@ -758,7 +801,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
         fence_after();
         gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(X, 0),
                                         Slot<D>::part(X, 1), nullptr, F32 ? 2 : 1, ps, false);
-        commit(barA);
+        { commit(barA); ++issA; }
       }
       T5_WAIT(barA, phA);   // also covers the previous tile's output MMAs
       phA ^= 1;
@@ -786,7 +829,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
         fence_after();
         gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_OUT, pq, pq + TT * SP, nullptr, 2, et,
                                           false);
-        commit(barB);
+        { commit(barB); ++issB; }
       }
       if (T5_VOTE()) break;
     }
@@ -811,10 +854,12 @@ struct ReduceLay {
   static constexpr int PS = PK3 + 3 * TT * SP / 2;      // bf16 [2*PJ x D] planes [hi; lo]
   static constexpr int BAR = PS + PJ * D;
   static constexpr int FLOATS = BAR + 16 + 256;
-  static constexpr int TCOLS = 256;   // PROJ [0, 32), STATE [128, 128 + 3 SP) (M = 64)
-  static constexpr int C_PROJ = 0, C_ST = 128;
+  // PROJ [0, 32), STATE [C_ST, C_ST + 3 SP) (M = 64)
+  static constexpr int TCOLS = 256;
+  static constexpr int C_PROJ = 0, C_ST = SP > 32 ? 64 : 128;
   static_assert(3 * TT * SP / 2 >= TT * SP, "pK area doubles as the mass scratch");
-  static_assert(FLOATS * 4 <= 113 * 1024, "two CTAs per SM");
+  static_assert(C_ST + 3 * SP <= TCOLS, "tensor-memory columns");
+  static_assert(FLOATS * 4 <= 227 * 1024, "shared memory");
 };
 
 // Per range: B[s][d] = sum_t pK[t][s] v[t][d] and A[s] = sum_t pK[t][s] into
@@ -917,7 +962,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
         fence_after();
         gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
                                         Slot<D>::part(KXt, 1), nullptr, F32 ? 2 : 1, ps, false);
-        commit(barA);
+        { commit(barA); ++issA; }
       }
       T5_WAIT(barA, phA);
       phA ^= 1;
@@ -967,7 +1012,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
           for (int ks = 0; ks < TT / 16; ++ks)
             mma(tbase + LY::C_ST, desc_mn<D>(va[a], ks), desc_mn<3 * SP>(pk3, ks),
                 idesc64_mn<3 * SP>(), i > 0 || a > 0 || ks > 0);
-        commit(barB);
+        { commit(barB); ++issB; }
       }
       if (i + 1 < it.ntiles) {   // the state MMAs read the v slot in place
         T5_WAIT(barB, phB);
@@ -982,17 +1027,21 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
       phB ^= 1;
       if (T5_VOTE()) break;
       fence_after();
-      // state: lane 32 q + l (l < 16) of warps 0..3 holds row d = 16 q + l
+      // state: lane 32 q + l (l < 16) of warps 0..3 holds row d = 16 q + l;
+      // eight bucket columns of the three part blocks at a time
       if (sub == 0) {
-        float st[3 * SP];
-#pragma unroll
-        for (int c = 0; c < 3 * SP; c += 8) tld8(tlane + LY::C_ST + c, st + c);
-        tld_wait();
         const int l = tid & 31, d = 16 * (warp & 3) + l;
-        if (l < 16 && d < D) {
 #pragma unroll
-          for (int sidx = 0; sidx < SP; ++sidx)
-            if (sidx < prm.S) dst[sidx * D + d] = st[sidx] + st[SP + sidx] + st[2 * SP + sidx];
+        for (int c = 0; c < SP; c += 8) {
+          float st[3][8];
+#pragma unroll
+          for (int j = 0; j < 3; ++j) tld8(tlane + LY::C_ST + j * SP + c, st[j]);
+          tld_wait();
+          if (l < 16 && d < D) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (c + e < prm.S) dst[(c + e) * D + d] = st[0][e] + st[1][e] + st[2][e];
+          }
         }
       }
       fence_before();
@@ -1017,14 +1066,20 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
 }
 
 // ------------------------------------------------------------------ B1 query backward
+// Up to 32 buckets: two q slots and three dO slots, and tile i+1 is loaded as
+// tile i starts.  Above 32 buckets (LATE) the larger pQ / E operands leave
+// room for one q slot and two dO slots: tile i+1 is then loaded once tile i's
+// projections are done and dq of tile i-1 has left through the q slot.
 template <int D, int SPAD>
 struct BwdQLay {
   static constexpr int NTH = 4;           // threads per token
   static constexpr int SP = (SPAD + 15) / 16 * 16;     // bucket columns
-  static constexpr int NFULL = 3;                      // dO slots in rotation
-  static constexpr int QX = 0;                          // [2] q slots (landed, then hi | mid)
-  static constexpr int GX = QX + 2 * Slot<D>::FLOATS;   // [3] dO slots (landed, then hi | lo)
-  static constexpr int QL = GX + 3 * Slot<D>::FLOATS;   // bf16 [TT x D] third part of q
+  static constexpr bool LATE = SP > 32;
+  static constexpr int NQ = LATE ? 1 : 2;               // q slots
+  static constexpr int NFULL = LATE ? 2 : 3;            // dO slots in rotation (one barrier each)
+  static constexpr int QX = 0;                          // [NQ] q slots (landed, then hi | mid)
+  static constexpr int GX = QX + NQ * Slot<D>::FLOATS;  // [NFULL] dO slots (landed, then hi | lo)
+  static constexpr int QL = GX + NFULL * Slot<D>::FLOATS;   // bf16 [TT x D] third part of q
   static constexpr int PQ = QL + TT * D / 2;            // pQ parts [TT x 2 SP] = [hi | lo]
   static constexpr int DJ = PQ + TT * SP;               // bf16 [TT x PJ] hi, then lo
   static constexpr int PS = DJ + TT * PJ;               // bf16 [3*PJ x D] planes [hi; mid; lo]
@@ -1033,9 +1088,12 @@ struct BwdQLay {
   static constexpr int RED = ET + 3 * SP * D / 2;       // [16] reductions
   static constexpr int BAR = RED + 16;
   static constexpr int FLOATS = BAR + 16 + 256;
-  // PROJ [0, 48), DPQ [64, 64 + 3SP), DQ [160, 160 + 2D), DE [384, 384 + 2SP) (M = 64)
+  // PROJ [0, 48), DPQ [64, 64 + 3SP), DQ [C_DQ, C_DQ + 2D), DE [384, 384 + 2SP) (M = 64)
   static constexpr int TCOLS = 512;
-  static constexpr int C_PROJ = 0, C_DPQ = 64, C_DQ = 160, C_DE = 384;
+  static constexpr int C_PROJ = 0, C_DPQ = 64, C_DQ = LATE ? 256 : 160, C_DE = 384;
+  static_assert(C_DPQ + 3 * SP <= C_DQ && C_DQ + 2 * D <= C_DE && C_DE + 2 * SP <= TCOLS,
+                "tensor-memory columns");
+  static_assert(FLOATS * 4 <= 227 * 1024, "shared memory");
 };
 
 // dq = dproj(pQ, dO . E^T) . P per token; per range the partial dE[s][d] =
@@ -1099,13 +1157,13 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
       };
       auto load = [&](int j) {
         if (failed) return;
-        inflight |= 1u << (j % 3);
+        inflight |= 1u << (j % LY::NFULL);
         if (tid == 0) {
           bulk_wait_read();   // a store may still be reading the q slot
-          float* const dsts[2] = {sm + LY::QX + (j & 1) * Slot<D>::FLOATS,
-                                  sm + LY::GX + (j % 3) * Slot<D>::FLOATS};
+          float* const dsts[2] = {sm + LY::QX + (j % LY::NQ) * Slot<D>::FLOATS,
+                                  sm + LY::GX + (j % LY::NFULL) * Slot<D>::FLOATS};
           const Layout* const lay[2] = {&prm.lq, &prm.ldo};
-          tma_tile<T, D, 2>(maps, dsts, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j % 3));
+          tma_tile<T, D, 2>(maps, dsts, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j % LY::NFULL));
         }
       };
       // Per tile i: q, dO parts -> MMA proj, dpQ (i) || store dq(i-1) -> hash
@@ -1113,14 +1171,15 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
       load(0);
       for (int i = 0; i < it.ntiles; ++i) {
         const int64_t tile0 = it.t0 + (int64_t)i * TT;
-        float* QXt = sm + LY::QX + (i & 1) * Slot<D>::FLOATS;
-        float* GXt = sm + LY::GX + (i % 3) * Slot<D>::FLOATS;
+        float* QXt = sm + LY::QX + (i % LY::NQ) * Slot<D>::FLOATS;
+        float* GXt = sm + LY::GX + (i % LY::NFULL) * Slot<D>::FLOATS;
+        const int fb = i % LY::NFULL;
         bf16* ql = reinterpret_cast<bf16*>(sm + LY::QL);
-        if (i + 1 < it.ntiles) load(i + 1);
-        T5_WAIT(full + (i % 3), (phF >> (i % 3)) & 1);
+        if (!LY::LATE && i + 1 < it.ntiles) load(i + 1);
+        T5_WAIT(full + fb, (phF >> fb) & 1);
         if (!failed) {
-          phF ^= 1u << (i % 3);
-          inflight &= ~(1u << (i % 3));
+          phF ^= 1u << fb;
+          inflight &= ~(1u << fb);
         }
         const bool valid = tile0 + row < it.t1;
         {
@@ -1150,11 +1209,14 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
                                           Slot<D>::part(QXt, 1), ql, F32 ? 3 : 1, ps, false);
           gemm_parts<SP, 3, D / 16, D, D>(tbase + LY::C_DPQ, Slot<D>::part(GXt, 0),
                                           Slot<D>::part(GXt, 1), nullptr, F32 ? 2 : 1, et, false);
-          commit(barA);
+          { commit(barA); ++issA; }
         }
         T5_WAIT(barA, phA);   // also covers the previous tile's dE / dq MMAs
         phA ^= 1;
         if (i > 0) store_prev(tile0 - TT, QXt);
+        // LATE: the q slot is free (projections done, dq(i-1) read by its
+        // store) and so is dO slot i+1 (dE(i-1) done)
+        if (LY::LATE && i + 1 < it.ntiles) load(i + 1);
         fence_after();
         {
 
@@ -1215,26 +1277,30 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
                   idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
           gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DQ, dj, dj + TT * PJ, nullptr, 2, pt,
                                             false);
-          commit(barB);
+          { commit(barB); ++issB; }
         }
         if (T5_VOTE()) break;
       }
       if (!failed)
         store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT,
-                   sm + LY::QX + ((it.ntiles - 1) & 1) * Slot<D>::FLOATS);
+                   sm + LY::QX + ((it.ntiles - 1) % LY::NQ) * Slot<D>::FLOATS);
       if (T5_VOTE()) break;
       fence_after();
-      // dE: lane 32 q + l (l < 16) of warps 0..3 holds row d = 16 q + l
+      // dE: lane 32 q + l (l < 16) of warps 0..3 holds row d = 16 q + l;
+      // eight bucket columns of both part blocks at a time
       if (sub == 0) {
-        float e[2 * SP];
-#pragma unroll
-        for (int c = 0; c < 2 * SP; c += 8) tld8(tlane + LY::C_DE + c, e + c);
-        tld_wait();
         const int l = tid & 31, d = 16 * (warp & 3) + l;
-        if (l < 16 && d < D) {
 #pragma unroll
-          for (int sidx = 0; sidx < SP; ++sidx)
-            if (sidx < prm.S) dst[sidx * D + d] = e[sidx] + e[SP + sidx];
+        for (int c = 0; c < SP; c += 8) {
+          float e[2][8];
+          tld8(tlane + LY::C_DE + c, e[0]);
+          tld8(tlane + LY::C_DE + SP + c, e[1]);
+          tld_wait();
+          if (l < 16 && d < D) {
+#pragma unroll
+            for (int x = 0; x < 8; ++x)
+              if (c + x < prm.S) dst[(c + x) * D + d] = e[0][x] + e[1][x];
+          }
         }
       }
       fence_before();
@@ -1300,7 +1366,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         put_stack<D, SP, 2, NTHR>(dbt, [&](int d, int s) {
           return s < prm.S ? gs[s * D + d] / (mass[s] + prm.eps) : 0.f;
         });
-        if (tid < 32) {
+        if (tid < SP) {
           float a = 0.f;
           if (tid < prm.S) {
             const float inv = 1.f / (mass[tid] + prm.eps);
@@ -1337,27 +1403,28 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
       };
       auto load = [&](int j) {
         if (failed) return;
-        inflight |= 1u << (j & 1);
+        inflight |= 1u << (j % LY::NS);
         if (tid == 0) {
           bulk_wait_read();   // stores may still be reading these slots
-          float* const dst[2] = {sm + LY::KX + (j & 1) * Slot<D>::FLOATS,
-                                 sm + LY::VX + (j & 1) * Slot<D>::FLOATS};
+          float* const dst[2] = {sm + LY::KX + (j % LY::NS) * Slot<D>::FLOATS,
+                                 sm + LY::VX + (j % LY::NS) * Slot<D>::FLOATS};
           const Layout* const lay[2] = {&prm.lk, &prm.lv};
-          tma_tile<T, D, 2>(maps, dst, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j & 1));
+          tma_tile<T, D, 2>(maps, dst, lay, prm, n, it.t0 + (int64_t)j * TT, full + (j % LY::NS));
         }
       };
       load(0);
       for (int i = 0; i < it.ntiles; ++i) {
         const int64_t tile0 = it.t0 + (int64_t)i * TT;
-        float* KXt = sm + LY::KX + (i & 1) * Slot<D>::FLOATS;
-        float* VXt = sm + LY::VX + (i & 1) * Slot<D>::FLOATS;
+        float* KXt = sm + LY::KX + (i % LY::NS) * Slot<D>::FLOATS;
+        float* VXt = sm + LY::VX + (i % LY::NS) * Slot<D>::FLOATS;
+        const int fb = i % LY::NS;
         bf16* kl = reinterpret_cast<bf16*>(sm + LY::KL);
         bf16* vl = reinterpret_cast<bf16*>(sm + LY::VL);
-        if (i + 1 < it.ntiles) load(i + 1);
-        T5_WAIT(full + (i & 1), (phF >> (i & 1)) & 1);
+        if (!LY::LATE && i + 1 < it.ntiles) load(i + 1);
+        T5_WAIT(full + fb, (phF >> fb) & 1);
         if (!failed) {
-          phF ^= 1u << (i & 1);
-          inflight &= ~(1u << (i & 1));
+          phF ^= 1u << fb;
+          inflight &= ~(1u << fb);
         }
         {
           float x[W], y[W];
@@ -1384,11 +1451,13 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
                                           Slot<D>::part(KXt, 1), kl, F32 ? 3 : 1, ps, false);
           gemm_parts<SP, 3, D / 16, D, D>(tbase + LY::C_DPK, Slot<D>::part(VXt, 0),
                                           Slot<D>::part(VXt, 1), vl, F32 ? 3 : 1, db, false);
-          commit(barA);
+          { commit(barA); ++issA; }
         }
         T5_WAIT(barA, phA);   // also covers the previous tile's dv / dk MMAs
         phA ^= 1;
         if (i > 0) store_prev(tile0 - TT, KXt, VXt);
+        // LATE: the single k / v slots are free once dv, dk of tile i-1 have been read out of them
+        if (LY::LATE && i + 1 < it.ntiles) load(i + 1);
         fence_after();
         {
 
@@ -1431,12 +1500,12 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
                                             false);
           gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DK, dj, dj + TT * PJ, nullptr, 2, pt,
                                             false);
-          commit(barB);
+          { commit(barB); ++issB; }
         }
         if (T5_VOTE()) break;
       }
       if (!failed) {
-        const int lt = (it.ntiles - 1) & 1;
+        const int lt = (it.ntiles - 1) % LY::NS;
         store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT, sm + LY::KX + lt * Slot<D>::FLOATS,
                    sm + LY::VX + lt * Slot<D>::FLOATS);
       }

@@ -60,12 +60,70 @@ def _stream():
     return torch.cuda.current_stream().cuda_stream
 
 
+def _mappable(*xs) -> bool:
+    """True when the copy engine can walk every tensor (no broadcast batch or
+    head axis): the library is then told to fail rather than fall back."""
+    for x in xs:
+        if x is None:
+            continue
+        M, B, T, H, _ = x.shape
+        s = x.stride()
+        if (s[1] == 0 and B > 1) or (s[2] == 0 and T > 1) or (s[3] == 0 and H > 1) or min(s) < 0:
+            return False
+    return True
+
+
+class DeviceStatus:
+    """Stream-ordered check of the library's device status word.
+
+    After a forward or backward the word is copied into pinned host memory
+    on the launching stream and an event is recorded; completed copies are
+    inspected at the next call (no forced synchronisation), and
+    ``check(wait=True)`` waits for all of them.  A nonzero word means a kernel
+    gave up on a bounded wait and that call's outputs are partial."""
+
+    def __init__(self):
+        self.pending = []
+
+    def push(self, lib, ws: torch.Tensor) -> None:
+        host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        check(lib.race_device_status(ws.data_ptr(), ws.numel(), host.data_ptr(), _stream()))
+        ev = torch.cuda.Event()
+        ev.record()
+        self.pending.append((host, ev))
+        self.check(wait=False)
+
+    def check(self, wait: bool = True) -> None:
+        while self.pending:
+            host, ev = self.pending[0]
+            if not wait and not ev.query():
+                return
+            ev.synchronize()
+            self.pending.pop(0)
+            word = int(host.item())
+            if word:
+                self.pending.clear()
+                raise _lib.RaceError(
+                    f"race_b200 device status 0x{word:x}: a kernel gave up on a bounded wait "
+                    "(timeout); the outputs of that call are incomplete")
+
+
+device_status = DeviceStatus()
+
+
+def check_device_status() -> None:
+    """Waits for the outstanding status reads and raises RaceError if any
+    forward or backward since the last check ended a kernel early."""
+    device_status.check(wait=True)
+
+
 _NORMS = {"bucket": _lib.RACE_NORM_BUCKET, "global": _lib.RACE_NORM_GLOBAL}
 
 
-def make_desc(shape, dtype, K, L, causal, eps, chunk, shared_planes, normalize=0) -> RaceDesc:
+def make_desc(shape, dtype, K, L, causal, eps, chunk, shared_planes, normalize=0,
+              flags=0) -> RaceDesc:
     M, B, T, H, d = shape
-    return RaceDesc(
+    return RaceDesc(flags=int(flags),
         dtype=_lib.RACE_F32 if dtype == torch.float32 else _lib.RACE_BF16,
         causal=int(bool(causal)), head_dim=d, num_bits=K, num_tables=L, ensembles=M,
         batch=B, heads=H, tokens=T, chunk=int(chunk), shared_planes=int(bool(shared_planes)),
@@ -103,7 +161,7 @@ def _scale_tensor(scale, device) -> torch.Tensor:
 class _RaceFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, planes, scale, K, L, causal, eps, chunk, shared_planes, group,
-                normalize):
+                normalize, head_major_out):
         ctx.set_materialize_grads(False)
         if not q.is_cuda:
             raise RuntimeError("race_attention runs on CUDA devices only (no CPU fallback)")
@@ -112,12 +170,17 @@ class _RaceFunction(torch.autograd.Function):
         q, k, v = (_prep(t, dtype) for t in (q, k, v))
         planes = planes.detach().to(torch.float32).contiguous()
         scale_d = scale.detach().to(torch.float32).reshape(()).contiguous()
-        desc = make_desc(tuple(q.shape), dtype, K, L, causal, eps, chunk, shared_planes, normalize)
+        flags = _lib.RACE_FLAG_STRICT_TMA if _mappable(q, k, v) else 0
+        desc = make_desc(tuple(q.shape), dtype, K, L, causal, eps, chunk, shared_planes, normalize,
+                         flags)
         sizes = query(desc)
         buf = Buffers(sizes, q.device)
         lib = _lib.load()
-        out = torch.empty(q.shape, dtype=dtype, device=q.device)
-        M, B, T, H, _ = q.shape
+        M, B, T, H, dh = q.shape
+        if head_major_out:   # [M, B, H, T, d] memory seen as [M, B, T, H, d]
+            out = torch.empty((M, B, H, T, dh), dtype=dtype, device=q.device).permute(0, 1, 3, 2, 4)
+        else:
+            out = torch.empty(q.shape, dtype=dtype, device=q.device)
         # the per-token denominator of the global mode, [M, B, H, T] float32
         den = (torch.empty((M, B, H, T), dtype=torch.float32, device=q.device) if normalize
                else torch.empty(0, dtype=torch.float32, device=q.device))
@@ -127,6 +190,7 @@ class _RaceFunction(torch.autograd.Function):
             check(lib.race_forward_ex(desc, _rt(q), _rt(k), _rt(v), _ptr(planes), _ptr(scale_d),
                                       _rt(out), _ptr(den) if normalize else None, _ptr(state),
                                       _ptr(ws), ws.numel(), _stream()))
+            device_status.push(lib, ws)
         else:
             from .sequence_parallel import sharded_forward
             sharded_forward(lib, desc, sizes, buf, q, k, v, planes, scale_d, out, state, ws, group,
@@ -147,6 +211,8 @@ class _RaceFunction(torch.autograd.Function):
         if dout is None:
             dout = torch.zeros(q.shape, dtype=dtype, device=q.device)
         dout = _prep(dout, dtype)
+        if not _mappable(dout):
+            dout = dout.contiguous()
         if dden is not None and desc.normalize:
             dden = dden.to(torch.float32).contiguous()
         else:
@@ -166,19 +232,21 @@ class _RaceFunction(torch.autograd.Function):
                                        _ptr(state), _rt(dout), _ptr(dden), _rt(dq), _rt(dk),
                                        _rt(dv), _ptr(dscale), _ptr(gstate), _ptr(ws), ws.numel(),
                                        _stream()))
+            device_status.push(lib, ws)
         else:
             from .sequence_parallel import sharded_backward
             sharded_backward(lib, desc, sizes, buf, q, k, v, planes, scale_d, state, dout,
                              dq, dk, dv, dscale, gstate, ws, ctx.group, dden)
         dq, dk, dv = (g.to(t) for g, t in zip((dq, dk, dv), ctx.in_dtypes))
         return (dq, dk, dv, None, dscale.reshape(ctx.scale_shape), None, None, None, None, None,
-                None, None, None)
+                None, None, None, None)
 
 
 def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: torch.Tensor,
                    num_bits: int, num_tables: int, scale=1.0, causal: bool = False,
                    eps: float = 1e-6, chunk: int = 0, shared_planes: Optional[bool] = None,
-                   group=None, normalize: str = "bucket", return_den: bool = False):
+                   group=None, normalize: str = "bucket", return_den: bool = False,
+                   head_major_out: bool = False):
     """RACE attention forward (autograd-aware) on [M, B, T, H, d] inputs.
 
     Args:
@@ -205,6 +273,10 @@ def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: to
       return_den: global mode only: also return den, the unclamped per-token
         denominator [M, B, H, T] float32 (differentiable; 4-D inputs give
         [B, H, T]).
+      head_major_out: lay the output out in memory as [M, B, H, T, d] (the
+        returned tensor is still indexed [M, B, T, H, d]), so that the
+        reference modules' head merge ``permute(0, 2, 1, 3).reshape(B, T,
+        H*d)`` is a view rather than a copy.
     """
     squeeze = False
     if q.dim() == 4:
@@ -232,7 +304,7 @@ def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: to
     scale_t = _scale_tensor(scale, q.device)
     out, den = _RaceFunction.apply(q, k, v, planes, scale_t, int(num_bits), int(num_tables),
                                    bool(causal), float(eps), int(chunk), bool(shared_planes),
-                                   group, norm)
+                                   group, norm, bool(head_major_out))
     if squeeze:
         out, den = out.squeeze(0), (den.squeeze(0) if norm else den)
     return (out, den) if return_den else out

@@ -40,18 +40,30 @@ class BatchedACE(nn.Module):
             pt = pt.unsqueeze(0)
         return pt.transpose(1, 2)
 
-    def forward(self, Khf, Vhf, Qhf):
+    def forward(self, Khf, Vhf, Qhf, head_major_out: bool = False):
         M, B, T, H, dk = Khf.shape
         assert M == self.M and dk == self.d_k
         return race_attention(Qhf, Khf, Vhf, self.planes(), self.K, self.L, self._scale,
-                              causal=True, eps=1e-6, shared_planes=self.share_planes)
+                              causal=True, eps=1e-6, shared_planes=self.share_planes,
+                              head_major_out=head_major_out)
 
 
 class RACEAttention(nn.Module):
-    """misc/race.py:144-173."""
+    """misc/race.py:144-173.
 
-    def __init__(self, d, h, K, L, M, drop=0.1, qkv_bias=False, device="cpu"):
+    Head merge as in the reference, ``mean(0).permute(0, 2, 1, 3)
+    .contiguous().view(B, T, -1)`` (misc/race.py:171), by default
+    (``merge_heads="reference"``): the rows of the merged tensor hold head
+    h's tokens side by side.  ``merge_heads="concat"`` concatenates the heads
+    of each token instead (a different model, for new training only).
+    """
+
+    def __init__(self, d, h, K, L, M, drop=0.1, qkv_bias=False, device="cpu",
+                 merge_heads: str = "reference"):
         super().__init__()
+        if merge_heads not in ("reference", "concat"):
+            raise ValueError("merge_heads must be 'reference' or 'concat'")
+        self.merge_heads = merge_heads
         assert d % h == 0
         self.h, self.d_k, self.M = h, d // h, M
         self.q = nn.Linear(d, d, bias=qkv_bias)
@@ -67,8 +79,11 @@ class RACEAttention(nn.Module):
         K = self.k(x).view(B, T, self.h, self.d_k)
         V = self.v(x).view(B, T, self.h, self.d_k)
         pack = lambda z: z.unsqueeze(0).expand(self.M, -1, -1, -1, -1)
-        out_h = self.ace(pack(K), pack(V), pack(Q))
-        out = out_h[0] if self.M == 1 else out_h.mean(0)
+        ref = self.merge_heads == "reference"
+        out_h = self.ace(pack(K), pack(V), pack(Q), head_major_out=ref)
+        out = out_h[0] if self.M == 1 else out_h.mean(0)      # [B, T, H, d_k]
+        if ref:
+            out = out.permute(0, 2, 1, 3)                      # misc/race.py:171
         return self.drop(self.o(out.reshape(B, T, -1)))
 
 

@@ -47,18 +47,32 @@ class BatchedACE(nn.Module):
     def scale(self) -> torch.Tensor:
         return self.logit_temp.exp().clamp(1e-2, self.temp_max)
 
-    def forward(self, Khf, Vhf, Qhf, eps: float = 1e-6):
+    def forward(self, Khf, Vhf, Qhf, eps: float = 1e-6, head_major_out: bool = False):
         M, B, T, H, dk = Khf.shape
         assert M == self.M and dk == self.d_k
         return race_attention(Qhf, Khf, Vhf, self.planes(), self.K, self.L, self.scale(),
-                              causal=False, eps=eps, shared_planes=self.share_planes)
+                              causal=False, eps=eps, shared_planes=self.share_planes,
+                              head_major_out=head_major_out)
 
 
 class RACEAttention(nn.Module):
-    """misc/vit.py:994-1038: q/k/v projections, RACE, ensemble mean, out-proj."""
+    """misc/vit.py:994-1038: q/k/v projections, RACE, ensemble mean, out-proj.
 
-    def __init__(self, d_in, d_out, dropout, num_heads, L, K, N_M, qkv_bias=False, device="cpu"):
+    Head merge: the reference merges the [B, T, H, d_k] ensemble mean with
+    ``permute(0, 2, 1, 3).reshape(B, T, H * d_k)`` (misc/vit.py:1034-1035),
+    which lays head h's tokens side by side in the rows of the output rather
+    than concatenating the heads of each token.  That is reproduced by
+    default (``merge_heads="reference"``), so reference checkpoints give the
+    reference's outputs; ``merge_heads="concat"`` selects the per-token
+    concatenation (a different model, for new training only).
+    """
+
+    def __init__(self, d_in, d_out, dropout, num_heads, L, K, N_M, qkv_bias=False, device="cpu",
+                 merge_heads: str = "reference"):
         super().__init__()
+        if merge_heads not in ("reference", "concat"):
+            raise ValueError("merge_heads must be 'reference' or 'concat'")
+        self.merge_heads = merge_heads
         assert d_in % num_heads == 0
         self.H = num_heads
         self.d_k = d_in // num_heads
@@ -79,8 +93,12 @@ class RACEAttention(nn.Module):
         K = self.k_proj(x).view(B, T, H, d_k)
         V = self.v_proj(x).view(B, T, H, d_k)
         pack = lambda Z: Z.unsqueeze(0).expand(M, -1, -1, -1, -1)
-        out_hm = self.ace(pack(K), pack(V), pack(Q))
-        out = out_hm[0] if M == 1 else out_hm.mean(dim=0)
+        ref = self.merge_heads == "reference"
+        # reference merge: the output is written head-major, so the merge is a view for M = 1
+        out_hm = self.ace(pack(K), pack(V), pack(Q), head_major_out=ref)
+        out = out_hm[0] if M == 1 else out_hm.mean(dim=0)     # [B, T, H, d_k]
+        if ref:
+            out = out.permute(0, 2, 1, 3)                      # misc/vit.py:1035
         return self.drop(self.out(out.reshape(B, T, H * d_k)))
 
 

@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference project is mounted read-only:
 
-    python tests/golden/make_golden.py /path/to/reference [all|global]
+    python tests/golden/make_golden.py /path/to/reference [all|global|modules]
 
 It extracts the class definitions ``BatchedACE`` from ``misc/vit.py``
 (non-causal, lines 888-978) and from ``misc/race.py`` (causal, lines 26-142)
@@ -212,6 +212,65 @@ def main(ref_root: str):
         print("wrote", path, os.path.getsize(path))
 
 
+def run_module_case(cls, cfg_or_args, *, kind, B, T, d_model, seed):
+    """A reference attention module or block (random init drawn in float32,
+    run in float64, dropout 0): x -> out, then the gradients of x and of every
+    parameter for a random upstream gradient.  The state_dict is saved under
+    ``sd/<name>`` so the drop-in modules load it unchanged."""
+    torch.manual_seed(seed)
+    if kind == "block":
+        mod = cls(cfg_or_args, device="cpu")
+    else:
+        mod = cls(**cfg_or_args, device="cpu")
+    mod = mod.double().eval()
+    x = torch.randn(B, T, d_model, dtype=torch.float32).double().requires_grad_(True)
+    out = mod(x)
+    dout = torch.randn(out.shape, dtype=torch.float32).double()
+    out.backward(dout)
+    # float32 storage keeps the fixtures small: the state_dict and inputs are
+    # float32 values, and rounding the float64 results to float32 (2^-24) is far
+    # below the 1e-4 parity bar
+    res = dict(x=x.detach().float().numpy(), dout=dout.float().numpy(),
+               out=out.detach().float().numpy(), dx=x.grad.float().numpy())
+    for name, t in mod.state_dict().items():
+        res["sd/" + name] = t.detach().float().numpy()
+    for name, prm in mod.named_parameters():
+        if prm.grad is not None:
+            res["grad/" + name] = prm.grad.float().numpy()
+    return res
+
+
+# name, file, class, kind, constructor args (or block cfg), B, T, d_model
+MODULE_CASES = [
+    ("mod_vit_attn_h2_m2", "misc/vit.py", "RACEAttention", "attn",
+     dict(d_in=64, d_out=64, dropout=0.0, num_heads=2, L=5, K=2, N_M=2), 2, 37, 64),
+    ("mod_vit_attn_h3_k4l4", "misc/vit.py", "RACEAttention", "attn",
+     dict(d_in=96, d_out=64, dropout=0.0, num_heads=3, L=4, K=4, N_M=1), 2, 29, 96),
+    ("mod_vit_block_h2", "misc/vit.py", "RACEBlock", "block",
+     dict(embed_dim=64, num_heads=2, drop_rate=0.0, qkv_bias=True, L=5, K=2, M=1), 2, 41, 64),
+    ("mod_race_attn_h2_m2", "misc/race.py", "RACEAttention", "attn",
+     dict(d=64, h=2, K=2, L=5, M=2, drop=0.0), 2, 33, 64),
+    ("mod_race_block_h2", "misc/race.py", "RACEBlock", "block",
+     dict(emb_dim=64, n_heads=2, drop_rate=0.0, qkv_bias=False, K=3, L=3, M=1), 1, 45, 64),
+]
+
+
+def main_modules(ref_root: str):
+    for i, (name, rel, clsname, kind, args, B, T, dm) in enumerate(MODULE_CASES):
+        path = os.path.join(ref_root, rel)
+        ace = load_class(path, "BatchedACE")
+        extra = {"BatchedACE": ace}
+        attn = load_class(path, "RACEAttention", extra)
+        extra["RACEAttention"] = attn
+        cls = attn if clsname == "RACEAttention" else load_class(path, clsname, extra)
+        res = run_module_case(cls, args, kind=kind, B=B, T=T, d_model=dm, seed=300 + i)
+        meta = dict(file=rel, cls=clsname, kind=kind, B=B, T=T, d_model=dm, **args)
+        res["meta_json"] = np.array(__import__("json").dumps(meta))
+        out = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(out, **res)
+        print("wrote", out, os.path.getsize(out))
+
+
 def main_global(ref_root: str):
     cls = load_class(os.path.join(ref_root, "misc/elsaa_causal_complete.py"), "CausalRACEAttention",
                      {"_HAS_TRITON_RACE": False})
@@ -224,8 +283,13 @@ def main_global(ref_root: str):
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-    which = sys.argv[2] if len(sys.argv) > 2 else "all"     # all | global
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT [all|global|modules]")
+    root = sys.argv[1]
+    which = sys.argv[2] if len(sys.argv) > 2 else "all"     # all | global | modules
     if which == "all":
         main(root)
-    main_global(root)
+    if which in ("all", "global"):
+        main_global(root)
+    if which in ("all", "modules"):
+        main_modules(root)

@@ -10,7 +10,34 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 def golden_files():
     """Attention fixtures (the reference's BatchedACE modules)."""
     return sorted(p for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
-                  if not os.path.basename(p).startswith(("probs_", "g_")))
+                  if not os.path.basename(p).startswith(("probs_", "g_", "mod_")))
+
+
+def module_files():
+    """Module fixtures (the reference's RACEAttention / RACEBlock, both files)."""
+    return sorted(glob.glob(os.path.join(GOLDEN_DIR, "mod_*.npz")))
+
+
+def load_module(path):
+    """(meta dict, state_dict of float32 tensors, fixture arrays) of a module fixture."""
+    import json
+
+    import torch
+    z = np.load(path)
+    meta = json.loads(str(z["meta_json"]))
+    sd = {k[3:]: torch.tensor(z[k]) for k in z.files if k.startswith("sd/")}
+    return meta, sd, {k: z[k] for k in z.files}
+
+
+def build_module(meta, device="cpu"):
+    """The drop-in module matching a fixture's reference class and arguments."""
+    from race_attention_b200 import race as R, vit as V
+    mod = V if meta["file"] == "misc/vit.py" else R
+    skip = {"file", "cls", "kind", "B", "T", "d_model"}
+    args = {k: v for k, v in meta.items() if k not in skip}
+    if meta["kind"] == "block":
+        return mod.RACEBlock(args, device=device)
+    return mod.RACEAttention(**args, device=device)
 
 
 def probs_files():

@@ -65,7 +65,8 @@ def test_query_sizes(lib):
 
 
 @pytest.mark.parametrize("bad,code", [
-    (dict(head_dim=48), 2), (dict(num_bits=3, num_tables=5), 2), (dict(num_tables=0), 1),
+    (dict(head_dim=48), 2), (dict(num_bits=5, num_tables=3), 2),
+    (dict(num_bits=3, num_tables=5, causal=1), 2), (dict(num_tables=0), 1),
     (dict(dtype=7), 1), (dict(tokens=-1), 1), (dict(num_bits=6, num_tables=1), 2),
     (dict(batch=70000), 2), (dict(normalize=1), 2), (dict(causal=1, normalize=3), 1),
 ])
