@@ -35,7 +35,8 @@ D, K, L = 64, 2, 5
 S = L << K
 TOKENS = 1 << 20
 METRIC = "RACE attn fwd+bwd tokens/s at N=1M (d=64, K=2, L=5)"
-CPU_SAMPLE_TOKENS = 1 << 16
+STRONG_TOKENS = 1 << 26          # the 64M-token sequence, sharded over the GPUs
+VARIANT_STEPS = 200              # timed steps of each variant (the headline uses --steps)
 
 
 # --------------------------------------------------------------------------- helpers
@@ -105,6 +106,17 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
+def cpu_model():
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for ln in out.splitlines():
+            if ln.startswith("Model name:"):
+                return ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -169,10 +181,10 @@ class Layer:
                 sp.exchange_backward_state(slots, gtotal, self.causal, self.group, add)
 
         def b_kv():
+            # dscale stays rank-local (this rank's tokens), as the C ABI defines it: a
+            # training step sums it with the model's other parameter gradients
             check(lib.race_backward_kv(d, q, k, v, P, sc, st, gs, _rt(self.dout), _rt(self.dk),
                                        _rt(self.dv), _ptr(self.dscale), ws, n, _stream()))
-            if self.group is not None:
-                torch.distributed.all_reduce(self.dscale, group=self.group)
 
         return [("forward_reduce", f_reduce), ("forward_readout", f_readout),
                 ("backward_q", b_q), ("backward_kv", b_kv)]
@@ -306,8 +318,9 @@ def e2e_rate(causal, dtype, tokens, steps, device, group=None, pipelined=True):
                    "race_attention autograd on device copies of pinned host buffers"}
 
 
-def cpu_rate(causal, tokens, budget_s=10.0, iters_max=50):
-    """Reference op sequence on the host cores (float32, all threads)."""
+def cpu_rate(causal, tokens, budget_s=20.0, iters_max=50, iters_min=3):
+    """Reference op sequence on the host cores (float32, all threads), on the
+    full workload: at least ``iters_min`` steps, then until ``budget_s``."""
     from oracle import torch_ref
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -320,12 +333,14 @@ def cpu_rate(causal, tokens, budget_s=10.0, iters_max=50):
     torch_ref.fwd_bwd(q, k, v, planes_T, K, L, scale, protos, dout, causal)   # warm-up
     times = []
     t_start = time.perf_counter()
-    while len(times) < iters_max and (time.perf_counter() - t_start) < budget_s:
+    while len(times) < iters_min or (len(times) < iters_max and
+                                     (time.perf_counter() - t_start) < budget_s):
         t0 = time.perf_counter()
         torch_ref.fwd_bwd(q, k, v, planes_T, K, L, scale, protos, dout, causal)
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
     return {"value": tokens / med, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "cpu": cpu_model(),
             "sample": f"{'causal' if causal else 'non-causal'} fp32 fwd+bwd, B1 H1 T={tokens} "
                       f"d{D} K{K} L{L}, torch CPU restatement of the reference op sequence, "
                       f"median of {len(times)}"}
@@ -351,9 +366,10 @@ def run_ours(args):
     for i, (causal, dtype, norm) in enumerate(configs):
         layer = Layer(causal, dtype, args.tokens, group, device, seed=1000 + rank, normalize=norm)
         sampler = ClockSampler(device.index) if (i == 0 and rank == 0) else None
+        steps = args.steps if i == 0 else min(args.steps, VARIANT_STEPS)
         if sampler:
             sampler.__enter__()
-        ms = timed(layer.step, args.steps, args.warmup, group, device)
+        ms = timed(layer.step, steps, args.warmup, group, device)
         if sampler:
             sampler.__exit__()
             clocks = sampler.summary()
@@ -364,8 +380,9 @@ def run_ours(args):
                "step_roofline_frac": (args.tokens * 11 * D * esize / (ms / 1e3) / 1e9) / peak}
         if norm:
             rec["normalize"] = "global"
+        rec["steps"] = steps
         if world == 1:
-            ph = phase_times(layer, max(3, args.steps // 2), device)
+            ph = phase_times(layer, max(3, min(args.steps, VARIANT_STEPS) // 2), device)
             pb = layer.phase_bytes()
             rec["phases_ms"] = ph
             dom = max(ph, key=ph.get)
@@ -388,6 +405,9 @@ def run_ours(args):
             del layer
         torch.cuda.empty_cache()
 
+    strong = None if args.no_strong else strong_scaling(args, world, group, device)
+    parity = sharded_parity(group, device) if world > 1 else None
+
     layer, rec = head
     line = {
         "metric": METRIC, "value": rec["value"], "unit": "tokens/s", "n_gpus": world,
@@ -403,7 +423,13 @@ def run_ours(args):
         "clocks": clocks,
         "variants": results[1:],
         "step_roofline_frac": rec["step_roofline_frac"],
+        "dscale": "rank-local per step (each rank's tokens); a training step sums it with the "
+                  "model's other parameter gradients, so the timed step runs 2 collectives",
     }
+    if strong is not None:
+        line["strong_64M"] = strong
+    if parity is not None:
+        line["sharded_parity"] = parity
     if world == 1:
         line["roofline"] = rec["roofline"]
         line["phases_ms"] = rec["phases_ms"]
@@ -416,18 +442,80 @@ def run_ours(args):
     if world > 1:
         torch.distributed.barrier()
     if rank == 0 and not args.no_cpu and world == 1:
-        line["cpu_baseline"] = cpu_rate(False, CPU_SAMPLE_TOKENS)
+        line["cpu_baseline"] = cpu_rate(False, args.tokens)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
 
 
+def strong_scaling(args, world, group, device):
+    """One fixed 64M-token sequence (STRONG_TOKENS) sharded over the ranks:
+    2^26 / N tokens per GPU, non-causal fp32 fwd+bwd, the same 2 collectives
+    per step.  Efficiency against N = 1 is (t1 / tN) / N across the lines of
+    a 1/2/4/8 sweep."""
+    tokens = STRONG_TOKENS // world
+    need = tokens * D * 4 * 8 + (1 << 30)          # 8 token tensors + state / slack
+    free, _ = torch.cuda.mem_get_info(device)
+    ok = torch.tensor([1.0 if free > need else 0.0], device=device)
+    if group is not None:
+        torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN, group=group)
+    if ok.item() < 1.0:
+        return {"skipped": f"needs {need / 2**30:.0f} GiB per GPU, {free / 2**30:.0f} GiB free"}
+    layer = Layer(False, torch.float32, tokens, group, device, seed=2000 + (0 if group is None
+                                                                             else dist_env()[1]))
+    steps = 10
+    ms = timed(layer.step, steps, 3, group, device)
+    del layer
+    torch.cuda.empty_cache()
+    return {"tokens_total": STRONG_TOKENS, "tokens_per_gpu": tokens, "steps": steps,
+            "ms_per_step": ms, "value": STRONG_TOKENS / (ms / 1e3), "unit": "tokens/s",
+            "scaling": "strong"}
+
+
+def sharded_parity(group, device):
+    """Correctness of the sequence-sharded path on this run's GPUs: two
+    streams of 20480 tokens (non-causal and causal, fp32) through
+    race_attention(group=...), every rank holding its contiguous token range;
+    rank 0 gathers out, dq, dk, dv and compares them with the same sequence
+    run unsharded on its own GPU.  Returns the worst relative L2 per mode."""
+    from race_attention_b200 import race_attention
+    world = torch.distributed.get_world_size(group)
+    rank = torch.distributed.get_rank(group)
+    T = 20480
+    g = torch.Generator(device=device).manual_seed(77)
+    full = [torch.randn((1, 2, T, 1, D), generator=g, device=device) for _ in range(4)]
+    planes = torch.randn((1, K * L, D), generator=g, device=device)
+    per = T // world
+    res = {}
+    for causal in (False, True):
+        def run(xs, grp):
+            leaves = [x.clone().requires_grad_(True) for x in xs[:3]]
+            out = race_attention(*leaves, planes, K, L, 1.1, causal=causal, group=grp)
+            out.backward(xs[3])
+            return [out.detach()] + [x.grad.detach() for x in leaves]
+        shard = [x[:, :, rank * per:(rank + 1) * per].contiguous() for x in full]
+        got = run(shard, group)
+        gathered = []
+        for t in got:
+            parts = [torch.empty_like(t) for _ in range(world)]
+            torch.distributed.all_gather(parts, t.contiguous(), group=group)
+            gathered.append(torch.cat(parts, dim=2))
+        if rank == 0:
+            ref = run(full, None)
+            errs = [float((a - b).norm() / b.norm()) for a, b in zip(gathered, ref)]
+            res["causal" if causal else "noncausal"] = max(errs)
+    torch.distributed.barrier(group)
+    if rank == 0:
+        res["streams"], res["tokens"] = 2, T
+    return res if rank == 0 else None
+
+
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    tokens = CPU_SAMPLE_TOKENS
+    tokens = args.tokens
     from oracle import torch_ref
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -437,17 +525,21 @@ def run_reference(args):
     planes_T = torch.randn(K * L, D, generator=g).T
     protos = torch_ref.protos_T(K)
     scale = torch.tensor(1.0)
-    for _ in range(args.warmup):
+    for _ in range(min(args.warmup, 3)):
         torch_ref.fwd_bwd(q, k, v, planes_T, K, L, scale, protos, dout, False)
+    # every step is the full 2^20-token workload; the run stops after --steps
+    # steps or once 60 s have been timed, whichever comes first
+    done = 0
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    while done < args.steps and (done < 3 or time.perf_counter() - t0 < 60.0):
         torch_ref.fwd_bwd(q, k, v, planes_T, K, L, scale, protos, dout, False)
-    dt = (time.perf_counter() - t0) / args.steps
+        done += 1
+    dt = (time.perf_counter() - t0) / done
     val = tokens / dt
-    sample = (f"non-causal fp32 fwd+bwd, B1 H1 T={tokens} (bounded sample of the 2^20-token "
-              f"workload) d{D} K{K} L{L}: torch CPU restatement of the reference op sequence")
+    sample = (f"non-causal fp32 fwd+bwd, B1 H1 T={tokens} (the full workload) d{D} K{K} L{L}: "
+              f"torch CPU restatement of the reference op sequence, {done} timed steps")
     line = {
-        "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world, "steps": done,
         "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
         "data": "synthetic: q,k,v,dO ~ N(0,1), seed 0",
@@ -456,7 +548,7 @@ def run_reference(args):
                    "K": K, "L": L, "parallelism": f"seq{world}",
                    "l2": "host run"},
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "cpu": cpu_model(), "sample": sample},
         "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
@@ -467,11 +559,12 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=1200)   # ~1.1 s timed at 2^20 tokens
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=TOKENS)
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-strong", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

@@ -308,6 +308,29 @@ def causal_global(q, k, v, planes, K, L, scale, dout=None, dden=None, eps=1e-6):
     return out, den, dq, dk, dv, dsq + dsk
 
 
+def l2_normalize(x, floor=1e-12):
+    """x / max(|x|, floor) over the head dimension: torch.nn.functional.normalize
+    (dim=-1), as the reference's angular baselines apply it to q and k
+    (misc/vit.py:2559-2560, misc/classification.py:370-371).  The RACE path's
+    optional normalize_qk flag hashes these instead of q and k."""
+    x = np.asarray(x, np.float64)
+    n = np.linalg.norm(x, axis=-1, keepdims=True)
+    return x / np.maximum(n, floor)
+
+
+def l2_normalize_backward(x, g, floor=1e-12):
+    """Gradient through l2_normalize: (g - xn (xn . g)) / |x| (g / floor where
+    |x| < floor, where the clamp has zero derivative)."""
+    x = np.asarray(x, np.float64)
+    g = np.asarray(g, np.float64)
+    n = np.linalg.norm(x, axis=-1, keepdims=True)
+    clamp = n < floor
+    nn_ = np.where(clamp, floor, n)
+    xn = x / nn_
+    c = np.where(clamp, 0.0, (xn * g).sum(-1, keepdims=True))
+    return (g - xn * c) / nn_
+
+
 def forward(q, k, v, planes, K, L, scale, causal, eps=1e-6):
     if causal:
         return causal_forward(q, k, v, planes, K, L, scale, eps)

@@ -155,6 +155,86 @@ __global__ void __launch_bounds__(1024) k_chunk_scan(float* __restrict__ slots, 
   }
 }
 
+// L2 normalisation of the head-dim rows of one [M, B, T, H, D] tensor (the
+// hashing input of normalize_qk): xn = x / max(|x|, 1e-12), the semantics of
+// torch.nn.functional.normalize.  One warp per row, dst contiguous [N][T][D].
+template <typename T>
+__device__ __forceinline__ float to_f(T x) {
+  if constexpr (sizeof(T) == 4) return x; else return __bfloat162float(x);
+}
+template <typename T>
+__device__ __forceinline__ T from_f(float x) {
+  if constexpr (sizeof(T) == 4) return x; else return __float2bfloat16_rn(x);
+}
+constexpr float kNormFloor = 1e-12f;
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_l2norm_rows(const T* __restrict__ x, Layout l, int B,
+                                                     int H, int64_t Tn, int D, int64_t rows,
+                                                     T* __restrict__ dst) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < rows;
+       r += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int n = (int)(r / Tn);
+    const int64_t t = r % Tn;
+    const T* src = x + stream_offset(l, n, B, H) + t * l.st;
+    float v[2], ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = c < D ? to_f(src[c]) : 0.f;
+      ss = fmaf(v[i], v[i], ss);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.f / fmaxf(sqrtf(ss), kNormFloor);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = lane + 32 * i;
+      if (c < D) dst[r * D + c] = from_f<T>(v[i] * inv);
+    }
+  }
+}
+
+// Backward of k_l2norm_rows in place: g holds dL/dxn on entry and dL/dx on
+// exit, dx = (g - xn (xn . g)) / |x| (g / floor where |x| < floor).
+template <typename T>
+__global__ void __launch_bounds__(256) k_l2norm_rows_bwd(const T* __restrict__ x, Layout l,
+                                                         T* __restrict__ g, Layout lg, int B,
+                                                         int H, int64_t Tn, int D, int64_t rows) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < rows;
+       r += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int n = (int)(r / Tn);
+    const int64_t t = r % Tn;
+    const T* src = x + stream_offset(l, n, B, H) + t * l.st;
+    T* gr = g + stream_offset(lg, n, B, H) + t * lg.st;
+    float v[2], gv[2], ss = 0.f, xg = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = c < D ? to_f(src[c]) : 0.f;
+      gv[i] = c < D ? to_f(gr[c]) : 0.f;
+      ss = fmaf(v[i], v[i], ss);
+      xg = fmaf(v[i], gv[i], xg);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      xg += __shfl_xor_sync(0xffffffffu, xg, o);
+    }
+    const float nrm = sqrtf(ss);
+    const bool clamp = nrm < kNormFloor;
+    const float inv = 1.f / (clamp ? kNormFloor : nrm);
+    const float c2 = clamp ? 0.f : xg * inv * inv;   // (xn . g) / |x|
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = lane + 32 * i;
+      if (c < D) gr[c] = from_f<T>((gv[i] - v[i] * c2) * inv);
+    }
+  }
+}
+
 // slots[n][chunk][e] += offset[n][e] for e < width.
 __global__ void k_add_offset(float* __restrict__ slots, const float* __restrict__ offset,
                              int64_t NC, int SS, int width, int64_t total) {
@@ -192,6 +272,7 @@ struct Plan {
   int N, S, LK, SS, width, spad, P, CL;
   int64_t NC;
   size_t state_floats, gstate_floats, part_floats, dscale_floats, tile_doubles;
+  size_t norm_bytes;   // normalize_qk: one normalised [N][T][D] copy (q, then k)
 };
 
 bool tensor_ok(const race_tensor_t& t, int elem_bytes) {
@@ -210,6 +291,7 @@ int make_plan(const race_desc_t* d, Plan* p) {
       d->tokens < 0 || d->head_dim < 1 || d->chunk < 0 || !(d->eps >= 0.f) ||
       (d->normalize != RACE_NORM_BUCKET && d->normalize != RACE_NORM_GLOBAL))
     return RACE_ERR_INVALID;
+  if (d->flags & ~(RACE_FLAG_STRICT_TMA | RACE_FLAG_NORMALIZE_QK)) return RACE_ERR_INVALID;
   // the global denominator exists only for the causal form (misc/race_kernel.py)
   if (d->normalize == RACE_NORM_GLOBAL && !d->causal) return RACE_ERR_UNSUPPORTED;
   if (d->head_dim != 32 && d->head_dim != 64) return RACE_ERR_UNSUPPORTED;
@@ -240,6 +322,9 @@ int make_plan(const race_desc_t* d, Plan* p) {
   if (P < 1) P = 1;
   p->P = (int)P;
   p->dscale_floats = (size_t)p->N * p->P;
+  const size_t es = d->dtype == RACE_F32 ? 4 : 2;
+  p->norm_bytes = (d->flags & RACE_FLAG_NORMALIZE_QK)
+                      ? ((size_t)p->N * (size_t)T * D * es + 255) / 256 * 256 : 0;
   if (!d->causal) {
     p->CL = 0;
     p->NC = 0;
@@ -264,7 +349,7 @@ int make_plan(const race_desc_t* d, Plan* p) {
 }
 
 size_t ws_bytes(const Plan& p) {
-  return (p.part_floats + (p.dscale_floats + 3) / 4 * 4 + 64) * sizeof(float);
+  return 2 * p.norm_bytes + (p.part_floats + (p.dscale_floats + 3) / 4 * 4 + 64) * sizeof(float);
 }
 
 // The device status word: the last 64 bytes of the workspace the caller
@@ -277,6 +362,9 @@ unsigned* status_word(void* ws, size_t bytes) {
 
 struct Call {
   bool strict = false;
+  bool normalize_qk = false;
+  char* norm_q = nullptr;   // normalised copies in the workspace (normalize_qk)
+  char* norm_k = nullptr;
   Plan plan;
   Params prm;
   float* part = nullptr;
@@ -299,7 +387,10 @@ int prepare(const race_desc_t* d, const float* planes, const float* scale, void*
   const size_t need = ws_bytes(c->plan);
   if (ws == nullptr || ws_bytes_given < need) return RACE_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(ws) % 16 != 0) return RACE_ERR_ALIGN;
-  c->part = static_cast<float*>(ws);
+  c->normalize_qk = (d->flags & RACE_FLAG_NORMALIZE_QK) != 0;
+  c->norm_q = static_cast<char*>(ws);
+  c->norm_k = c->norm_q + c->plan.norm_bytes;
+  c->part = reinterpret_cast<float*>(c->norm_k + c->plan.norm_bytes);
   c->dscale_part = c->part + c->plan.part_floats;
   Params& p = c->prm;
   std::memset(&p, 0, sizeof(p));
@@ -528,6 +619,63 @@ int zero_fill(void* p, size_t bytes, cudaStream_t stream) {
   return e == cudaSuccess ? RACE_OK : cuda_fail(e);
 }
 
+int launch_rows(int64_t rows) {
+  const int64_t blocks = (rows + 7) / 8;   // 8 rows (warps) per 256-thread block
+  return (int)std::min<int64_t>(blocks, (int64_t)sm_count() * 16);
+}
+
+// normalize_qk: replaces `t` by its row-normalised copy in `dst` (contiguous
+// [M, B, T, H, D] order of the streams, i.e. [N][T][D]).
+int normalize_into(const race_desc_t* d, const Call& c, race_tensor_t* t, char* dst,
+                   cudaStream_t stream) {
+  const int64_t T = d->tokens, D = d->head_dim;
+  const int64_t rows = (int64_t)c.plan.N * T;
+  if (rows == 0) return RACE_OK;
+  Layout l;
+  fill_layout(l, *t);
+  if (d->dtype == RACE_F32)
+    k_l2norm_rows<float><<<launch_rows(rows), 256, 0, stream>>>(
+        static_cast<const float*>(t->data), l, d->batch, d->heads, T, (int)D, rows,
+        reinterpret_cast<float*>(dst));
+  else
+    k_l2norm_rows<__nv_bfloat16><<<launch_rows(rows), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(t->data), l, d->batch, d->heads, T, (int)D, rows,
+        reinterpret_cast<__nv_bfloat16*>(dst));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  log_kernel("l2norm");
+  t->data = dst;
+  t->stride_t = D;
+  t->stride_h = T * D;
+  t->stride_b = (int64_t)d->heads * T * D;
+  t->stride_m = (int64_t)d->batch * d->heads * T * D;
+  return RACE_OK;
+}
+
+// normalize_qk backward: g (the gradient of the normalised copy, written by
+// the kernels into the caller's dq / dk) becomes the gradient of x, in place.
+int normalize_backward(const race_desc_t* d, const Call& c, const race_tensor_t& x,
+                       const race_tensor_t& g, cudaStream_t stream) {
+  const int64_t T = d->tokens;
+  const int64_t rows = (int64_t)c.plan.N * T;
+  if (rows == 0) return RACE_OK;
+  Layout lx, lg;
+  fill_layout(lx, x);
+  fill_layout(lg, g);
+  if (d->dtype == RACE_F32)
+    k_l2norm_rows_bwd<float><<<launch_rows(rows), 256, 0, stream>>>(
+        static_cast<const float*>(x.data), lx, static_cast<float*>(g.data), lg, d->batch,
+        d->heads, T, d->head_dim, rows);
+  else
+    k_l2norm_rows_bwd<__nv_bfloat16><<<launch_rows(rows), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x.data), lx, static_cast<__nv_bfloat16*>(g.data), lg,
+        d->batch, d->heads, T, d->head_dim, rows);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  log_kernel("l2norm_bwd");
+  return RACE_OK;
+}
+
 #define RACE_TRY(x)                  \
   do {                               \
     const int rc_ = (x);             \
@@ -682,6 +830,7 @@ int race_forward_reduce(const race_desc_t* desc, race_tensor_t k, race_tensor_t 
   }
   RACE_TRY(check_tensor(desc, k));
   RACE_TRY(check_tensor(desc, v));
+  if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &k, c.norm_k, stream));
   fill_layout(c.prm.lk, k);
   fill_layout(c.prm.lv, v);
   c.prm.k = k.data;
@@ -716,6 +865,7 @@ int race_forward_readout_ex(const race_desc_t* desc, race_tensor_t q, race_tenso
   if (desc->tokens == 0) return RACE_OK;
   RACE_TRY(check_tensor(desc, q));
   RACE_TRY(check_tensor(desc, out));
+  if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &q, c.norm_q, stream));
   fill_layout(c.prm.lq, q);
   fill_layout(c.prm.lo, out);
   c.prm.q = q.data;
@@ -726,6 +876,7 @@ int race_forward_readout_ex(const race_desc_t* desc, race_tensor_t q, race_tenso
   } else {
     RACE_TRY(check_tensor(desc, k));
     RACE_TRY(check_tensor(desc, v));
+    if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &k, c.norm_k, stream));
     fill_layout(c.prm.lk, k);
     fill_layout(c.prm.lv, v);
     c.prm.k = k.data;
@@ -782,6 +933,8 @@ int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k
   RACE_TRY(check_tensor(desc, q));
   RACE_TRY(check_tensor(desc, dout));
   RACE_TRY(check_tensor(desc, dq));
+  const race_tensor_t q_in = q;
+  if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &q, c.norm_q, stream));
   fill_layout(c.prm.lq, q);
   fill_layout(c.prm.ldo, dout);
   fill_layout(c.prm.ldq, dq);
@@ -801,6 +954,7 @@ int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k
   } else {
     RACE_TRY(check_tensor(desc, k));
     RACE_TRY(check_tensor(desc, v));
+    if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &k, c.norm_k, stream));
     fill_layout(c.prm.lk, k);
     fill_layout(c.prm.lv, v);
     c.prm.k = k.data;
@@ -811,6 +965,7 @@ int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k
     RACE_TRY(chunk_scan(c, gstate, 1, total, stream));
     RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 0, stream));
   }
+  if (c.normalize_qk) RACE_TRY(normalize_backward(desc, c, q_in, dq, stream));
   return RACE_OK;
 }
 
@@ -836,6 +991,8 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
   RACE_TRY(check_tensor(desc, v));
   RACE_TRY(check_tensor(desc, dk));
   RACE_TRY(check_tensor(desc, dv));
+  const race_tensor_t k_in = k;
+  if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &k, c.norm_k, stream));
   fill_layout(c.prm.lk, k);
   fill_layout(c.prm.lv, v);
   fill_layout(c.prm.ldk, dk);
@@ -852,6 +1009,7 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
   } else {
     RACE_TRY(check_tensor(desc, q));
     RACE_TRY(check_tensor(desc, dout));
+    if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &q, c.norm_q, stream));
     fill_layout(c.prm.lq, q);
     fill_layout(c.prm.ldo, dout);
     c.prm.q = q.data;
@@ -860,6 +1018,7 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
     RACE_TRY(launch(desc, c, K_C_BWD_KV, stream));
     RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 1, stream));
   }
+  if (c.normalize_qk) RACE_TRY(normalize_backward(desc, c, k_in, dk, stream));
   return RACE_OK;
 }
 

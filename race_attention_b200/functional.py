@@ -161,7 +161,7 @@ def _scale_tensor(scale, device) -> torch.Tensor:
 class _RaceFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, planes, scale, K, L, causal, eps, chunk, shared_planes, group,
-                normalize, head_major_out):
+                normalize, head_major_out, normalize_qk):
         ctx.set_materialize_grads(False)
         if not q.is_cuda:
             raise RuntimeError("race_attention runs on CUDA devices only (no CPU fallback)")
@@ -171,6 +171,8 @@ class _RaceFunction(torch.autograd.Function):
         planes = planes.detach().to(torch.float32).contiguous()
         scale_d = scale.detach().to(torch.float32).reshape(()).contiguous()
         flags = _lib.RACE_FLAG_STRICT_TMA if _mappable(q, k, v) else 0
+        if normalize_qk:
+            flags |= _lib.RACE_FLAG_NORMALIZE_QK
         desc = make_desc(tuple(q.shape), dtype, K, L, causal, eps, chunk, shared_planes, normalize,
                          flags)
         sizes = query(desc)
@@ -239,14 +241,14 @@ class _RaceFunction(torch.autograd.Function):
                              dq, dk, dv, dscale, gstate, ws, ctx.group, dden)
         dq, dk, dv = (g.to(t) for g, t in zip((dq, dk, dv), ctx.in_dtypes))
         return (dq, dk, dv, None, dscale.reshape(ctx.scale_shape), None, None, None, None, None,
-                None, None, None, None)
+                None, None, None, None, None)
 
 
 def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: torch.Tensor,
                    num_bits: int, num_tables: int, scale=1.0, causal: bool = False,
                    eps: float = 1e-6, chunk: int = 0, shared_planes: Optional[bool] = None,
                    group=None, normalize: str = "bucket", return_den: bool = False,
-                   head_major_out: bool = False):
+                   head_major_out: bool = False, normalize_qk: bool = False):
     """RACE attention forward (autograd-aware) on [M, B, T, H, d] inputs.
 
     Args:
@@ -273,6 +275,10 @@ def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: to
       return_den: global mode only: also return den, the unclamped per-token
         denominator [M, B, H, T] float32 (differentiable; 4-D inputs give
         [B, H, T]).
+      normalize_qk: hash q / |q| and k / |k| instead of q and k (the values and
+        the output are unchanged; gradients flow through the normalisation).
+        Off by default: the reference's RACE path never normalises, and tanh
+        is not scale-invariant, so turning it on changes the model.
       head_major_out: lay the output out in memory as [M, B, H, T, d] (the
         returned tensor is still indexed [M, B, T, H, d]), so that the
         reference modules' head merge ``permute(0, 2, 1, 3).reshape(B, T,
@@ -304,7 +310,7 @@ def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: to
     scale_t = _scale_tensor(scale, q.device)
     out, den = _RaceFunction.apply(q, k, v, planes, scale_t, int(num_bits), int(num_tables),
                                    bool(causal), float(eps), int(chunk), bool(shared_planes),
-                                   group, norm, bool(head_major_out))
+                                   group, norm, bool(head_major_out), bool(normalize_qk))
     if squeeze:
         out, den = out.squeeze(0), (den.squeeze(0) if norm else den)
     return (out, den) if return_den else out

@@ -214,3 +214,39 @@ def test_broadcast_layout_is_logged_as_fallback():
     log = _lib.last_kernels()
     assert any("fallback: q: broadcast batch axis" in e or "fallback: k: broadcast batch axis" in e
                for e in log), log
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("causal", [False, True], ids=["noncausal", "causal"])
+def test_normalize_qk(causal, dtype):
+    """normalize_qk=True hashes q/|q| and k/|k|: the oracle on the normalised
+    inputs, its gradients taken back through the normalisation; inputs with
+    a wide spread of row norms so that the flag matters."""
+    from race_attention_b200 import race_attention
+    rng = np.random.default_rng(11 + causal)
+    N, T, d, K, L = 2, 1500, 64, 2, 5
+    q, k, v, dout = (rng.standard_normal((N, T, d)).astype(np.float32) for _ in range(4))
+    q *= rng.uniform(0.1, 20.0, (N, T, 1)).astype(np.float32)
+    k *= rng.uniform(0.1, 20.0, (N, T, 1)).astype(np.float32)
+    if dtype == torch.bfloat16:
+        q, k, v, dout = (bf16_round(a) for a in (q, k, v, dout))
+    planes = rng.standard_normal((1, K * L, d)).astype(np.float32)
+    dev = "cuda"
+    to = lambda a: torch.tensor(a, device=dev).to(dtype)[None, :, :, None]
+    qt, kt, vt = (to(a).requires_grad_(True) for a in (q, k, v))
+    out = race_attention(qt, kt, vt, torch.tensor(planes, device=dev), K, L, 1.0, causal=causal,
+                         normalize_qk=True)
+    out.backward(to(dout))
+    f = lambda t: t.detach().float()[0, :, :, 0].cpu().numpy().astype(np.float64)
+    P = np.broadcast_to(planes, (N, K * L, d))
+    qn, kn = O.l2_normalize(q), O.l2_normalize(k)
+    ref = O.forward(qn, kn, v, P, K, L, 1.0, causal)
+    dqn, dkn, dv, _ = O.backward(qn, kn, v, P, K, L, 1.0, causal, dout)
+    dq, dk = O.l2_normalize_backward(q, dqn), O.l2_normalize_backward(k, dkn)
+    tol = TOL[dtype]
+    for name, a, b in (("out", out, ref), ("dq", qt.grad, dq), ("dk", kt.grad, dk),
+                       ("dv", vt.grad, dv)):
+        assert O.rel_l2(f(a), b) < tol, (name, O.rel_l2(f(a), b))
+    # the flag changes the result (tanh is not scale-invariant)
+    plain = O.forward(q, k, v, P, K, L, 1.0, causal)
+    assert O.rel_l2(plain, ref) > 10 * tol

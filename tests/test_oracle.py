@@ -161,3 +161,18 @@ def test_oracle_matches_reference_global_causal(path):
     assert rel(G.merge_heads(dq, B, H), g["dq"]) < 1e-7
     assert rel(G.merge_heads(dk * keep, B, H), g["dk"]) < 1e-7
     assert math.isclose(-ds * scale, float(g["dlog_beta"]), rel_tol=1e-7)
+
+
+def test_l2_normalize_matches_torch():
+    """The oracle's normalisation (used by the normalize_qk flag) against
+    torch.nn.functional.normalize and its autograd, zero rows included."""
+    import torch
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((3, 17, 64))
+    x[1, 4] = 0.0
+    g = rng.standard_normal(x.shape)
+    xt = torch.tensor(x, requires_grad=True)
+    y = torch.nn.functional.normalize(xt, dim=-1)
+    y.backward(torch.tensor(g))
+    assert np.allclose(O.l2_normalize(x), y.detach().numpy(), rtol=1e-12, atol=1e-14)
+    assert np.allclose(O.l2_normalize_backward(x, g), xt.grad.numpy(), rtol=1e-10, atol=1e-12)
