@@ -179,6 +179,11 @@ int race_backward(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
  * forward:  race_forward_reduce -> [caller collective] -> race_forward_readout
  *   non-causal: state holds this rank's bucket sums; the caller all-reduces
  *               the whole state buffer (sum) before the readout.
+ *   causal (per-bucket): forward_reduce also stores the key projections and
+ *               forward_readout the query projections in the state (the
+ *               backward reads them instead of q and k), so the readout
+ *               writes to `state` as well; only the leading slots are
+ *               exchanged between ranks.
  *   causal:     state holds rank-local chunk prefixes and `total` (N slots)
  *               the rank's totals; the caller gathers all ranks' totals, sums
  *               those of LOWER ranks into an offset (N slots) and calls
@@ -198,7 +203,7 @@ int race_forward_reduce(const race_desc_t* desc, race_tensor_t k,
                         cudaStream_t stream);
 int race_forward_readout(const race_desc_t* desc, race_tensor_t q,
                          race_tensor_t k, race_tensor_t v, const float* planes,
-                         const float* scale, const float* state,
+                         const float* scale, float* state,
                          race_tensor_t out, void* workspace,
                          size_t workspace_bytes, cudaStream_t stream);
 int race_backward_q(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
@@ -227,7 +232,7 @@ int race_forward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
 int race_forward_readout_ex(const race_desc_t* desc, race_tensor_t q,
                             race_tensor_t k, race_tensor_t v,
                             const float* planes, const float* scale,
-                            const float* state, race_tensor_t out, float* den,
+                            float* state, race_tensor_t out, float* den,
                             void* workspace, size_t workspace_bytes,
                             cudaStream_t stream);
 int race_backward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,

@@ -270,7 +270,12 @@ __global__ void __launch_bounds__(1024) k_dscale_final(const float* __restrict__
 // ------------------------------------------------------------ host helpers
 struct Plan {
   int N, S, LK, SS, width, spad, P, CL;
+  bool c5;             // causal per-bucket mode on the chunkwise tcgen05 kernels
   int64_t NC;
+  size_t proj_off;     // c5: floats of the state before the q / k projections
+  size_t alpha_off;    // c5: floats of the gradient state before alpha [N][T][SA]
+  size_t mass_off;     // c5: floats of the gradient state before the tile key masses
+  int SA;              // c5: floats per token of alpha
   size_t state_floats, gstate_floats, part_floats, dscale_floats, tile_doubles;
   size_t norm_bytes;   // normalize_qk: one normalised [N][T][D] copy (q, then k)
 };
@@ -283,6 +288,8 @@ bool tensor_ok(const race_tensor_t& t, int elem_bytes) {
   const int64_t q = 16 / elem_bytes;
   return t.stride_m % q == 0 && t.stride_b % q == 0 && t.stride_h % q == 0 && t.stride_t % q == 0;
 }
+
+constexpr int PJW = 16;   // projection columns kept per token (L K <= 16)
 
 int make_plan(const race_desc_t* d, Plan* p) {
   if (d == nullptr || p == nullptr) return RACE_ERR_INVALID;
@@ -304,6 +311,9 @@ int make_plan(const race_desc_t* d, Plan* p) {
   const int64_t N64 = (int64_t)d->ensembles * d->batch * d->heads;
   if (N64 > 65535) return RACE_ERR_UNSUPPORTED;   // streams map to gridDim.y
   p->N = (int)N64;
+  p->c5 = false;
+  p->proj_off = p->alpha_off = p->mass_off = 0;
+  p->SA = 0;
   p->S = S;
   p->LK = LK;
   p->spad = spad_for(S);
@@ -341,8 +351,21 @@ int make_plan(const race_desc_t* d, Plan* p) {
     const size_t slots = (size_t)p->N * p->P;
     const int64_t tiles = (T + 31) / 32;
     p->state_floats = slots * p->SS;
+    // per-bucket mode: the forward also keeps the fp32 projections of q and k
+    // ([N][T][16] each) behind the prefix slots
+    p->c5 = d->normalize == RACE_NORM_BUCKET;
+    p->proj_off = (p->state_floats + 63) / 64 * 64;
+    if (p->c5) p->state_floats = p->proj_off + 2 * (size_t)p->N * T * PJW;
+    // per-bucket mode: gradient slots, then alpha [N][T][SA] and the float64
+    // key mass at every 128-token tile start [N][tiles][SP]
+    p->SA = round_up(S, 4);
+    p->alpha_off = ((size_t)p->N * p->P * p->SS + 63) / 64 * 64;
+    p->mass_off = (p->alpha_off + (size_t)p->N * T * p->SA + 63) / 64 * 64;
     p->tile_doubles = (size_t)p->N * tiles * round_up(S, 8);
     p->gstate_floats = slots * p->SS + (size_t)p->N * T * S + 2 * p->tile_doubles + 2;
+    if (p->c5)
+      p->gstate_floats =
+          p->mass_off + 2 * (size_t)p->N * ((T + 127) / 128) * round_up(p->spad, 16) + 2;
     p->part_floats = 0;
   }
   return RACE_OK;
@@ -496,6 +519,31 @@ bool encode_map(CUtensorMap* m, const void* base, const Layout& l, int dtype, co
   return true;
 }
 
+// Maps a float32 [N][T][C] array (C * 4 bytes a multiple of 16) as 3-D
+// (C, T, N) with boxes of 128 whole rows.
+bool encode_map3(CUtensorMap* m, const float* base, int64_t N, int64_t T, int C, const char* name,
+                 char* why, size_t why_len) {
+  const EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) {
+    std::snprintf(why, why_len, "cuTensorMapEncodeTiled not found");
+    return false;
+  }
+  const cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)T, (cuuint64_t)N};
+  const cuuint64_t strides[2] = {(cuuint64_t)C * 4, (cuuint64_t)(T * C * 4)};
+  const cuuint32_t box[3] = {(cuuint32_t)C, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(why, why_len, "%s: encode error %d ([%lld][%lld][%d] float32)", name, (int)r,
+                  (long long)N, (long long)T, C);
+    return false;
+  }
+  return true;
+}
+
 const char* kernel_name(KernelId id) {
   switch (id) {
     case K_NC_REDUCE: return "t5_reduce";
@@ -509,6 +557,10 @@ const char* kernel_name(KernelId id) {
     case K_C_TOTALS: return "tc_reduce";
     case K_NC_BWD_Q_SYNC: return "tc_bwd_q";
     case K_NC_BWD_KV_SYNC: return "tc_bwd_kv";
+    case K_C5_PROJ: return "c5_proj";
+    case K_C5_FWD: return "c5_fwd";
+    case K_C5_BWD_Q: return "c5_bwd_q";
+    case K_C5_BWD_KV: return "c5_bwd_kv";
     default: return "?";
   }
 }
@@ -552,10 +604,29 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
     else if (id == K_NC_REDUCE)
       ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, hd, "k", why, wl) &&
                encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, hd, "v", why, wl);
+    else if (id == K_C5_BWD_Q)
+      ok_map = encode_map3(&maps.map[0], prm.projq, prm.N, prm.T, PJW, "projq", why, wl) &&
+               encode_map3(&maps.map[1], prm.projk, prm.N, prm.T, PJW, "projk", why, wl) &&
+               encode_map(&maps.map[2], prm.v, prm.lv, d->dtype, prm, hd, "v", why, wl) &&
+               encode_map(&maps.map[3], prm.dout, prm.ldo, d->dtype, prm, hd, "dout", why, wl) &&
+               encode_map(&maps.map[4], prm.dq, prm.ldq, d->dtype, prm, hd, "dq", why, wl) &&
+               encode_map3(&maps.map[5], prm.alpha, prm.N, prm.T, prm.SA, "alpha", why, wl);
+    else if (id == K_C5_BWD_KV)
+      ok_map = encode_map3(&maps.map[0], prm.projq, prm.N, prm.T, PJW, "projq", why, wl) &&
+               encode_map3(&maps.map[1], prm.projk, prm.N, prm.T, PJW, "projk", why, wl) &&
+               encode_map(&maps.map[2], prm.v, prm.lv, d->dtype, prm, hd, "v", why, wl) &&
+               encode_map(&maps.map[3], prm.dout, prm.ldo, d->dtype, prm, hd, "dout", why, wl) &&
+               encode_map(&maps.map[5], prm.dk, prm.ldk, d->dtype, prm, hd, "dk", why, wl) &&
+               encode_map(&maps.map[6], prm.dv, prm.ldv, d->dtype, prm, hd, "dv", why, wl);
+    else if (id == K_C5_FWD)
+      ok_map = encode_map3(&maps.map[0], prm.projq, prm.N, prm.T, PJW, "projq", why, wl) &&
+               encode_map3(&maps.map[1], prm.projk, prm.N, prm.T, PJW, "projk", why, wl) &&
+               encode_map(&maps.map[2], prm.v, prm.lv, d->dtype, prm, hd, "v", why, wl) &&
+               encode_map(&maps.map[3], prm.out, prm.lo, d->dtype, prm, hd, "out", why, wl);
     if (!ok_map) {   // layouts the copy engine cannot walk: warp-level kernels
       char note[220];
       std::snprintf(note, sizeof(note), "fallback: %s", why);
-      if (c.strict || c.plan.S > 32) {
+      if (c.strict || c.plan.S > 32 || id == K_C5_FWD || id == K_C5_BWD_Q || id == K_C5_BWD_KV) {
         log_kernel(kernel_name(id), note);
         std::snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", kernel_name(id), why);
         return RACE_ERR_UNSUPPORTED;
@@ -576,6 +647,29 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
   const cudaError_t e = cudaLaunchKernel(ki.fn, grid, dim3(ki.threads), args, ki.smem_bytes, stream);
   if (e != cudaSuccess) return cuda_fail(e);
   log_kernel(kernel_name(id), note);
+  return RACE_OK;
+}
+
+// causal pre-pass: fp32 projections of x (q or k) into proj [N][T][16]
+int launch_proj(const race_desc_t* d, const Call& c, const race_tensor_t& x, float* proj,
+                cudaStream_t stream) {
+  KernelInfo ki;
+  const int K = d->num_bits, sp = c.plan.spad;
+  bool ok;
+  if (d->dtype == RACE_F32)
+    ok = d->head_dim == 32 ? kernels_f32_d32(sp, K, K_C5_PROJ, &ki) : kernels_f32_d64(sp, K, K_C5_PROJ, &ki);
+  else
+    ok = d->head_dim == 32 ? kernels_bf16_d32(sp, K, K_C5_PROJ, &ki) : kernels_bf16_d64(sp, K, K_C5_PROJ, &ki);
+  if (!ok) return RACE_ERR_UNSUPPORTED;
+  Params prm = c.prm;
+  const void* xp = x.data;
+  Layout lx;
+  fill_layout(lx, x);
+  void* args[] = {&prm, &xp, &lx, &proj};
+  const dim3 grid((unsigned)((d->tokens + ki.threads - 1) / ki.threads), (unsigned)c.plan.N);
+  const cudaError_t e = cudaLaunchKernel(ki.fn, grid, dim3(ki.threads), args, 0, stream);
+  if (e != cudaSuccess) return cuda_fail(e);
+  log_kernel("c5_proj");
   return RACE_OK;
 }
 
@@ -603,6 +697,18 @@ int dscale_final(const Call& c, int count, float* dscale, int accumulate, cudaSt
   log_kernel("dscale_final");
   k_dscale_final<<<1, 1024, 0, stream>>>(c.dscale_part, count, c.prm.scale, dscale, accumulate);
   return post(stream);
+}
+
+// c5: the projections behind the prefix slots of the state; alpha and the
+// tile key masses behind the gradient slots
+void c5_pointers(Call& c, const float* state, const float* gstate, int64_t T) {
+  float* st = const_cast<float*>(state);
+  c.prm.projq = st + c.plan.proj_off;
+  c.prm.projk = c.prm.projq + (size_t)c.plan.N * T * PJW;
+  float* gs = const_cast<float*>(gstate);
+  c.prm.alpha = gs + c.plan.alpha_off;
+  c.prm.range_mass = reinterpret_cast<double*>(gs + c.plan.mass_off);
+  c.prm.SA = c.plan.SA;
 }
 
 // alpha and the per-tile key mass live behind the gradient slots
@@ -843,6 +949,14 @@ int race_forward_reduce(const race_desc_t* desc, race_tensor_t k, race_tensor_t 
                                             cudaMemcpyDeviceToDevice, stream);
       if (e != cudaSuccess) return cuda_fail(e);
     }
+  } else if (c.plan.c5) {
+    // the key projections (kept for the readout and the backward), the range
+    // totals straight into the state slots, then the exclusive scan
+    float* projk = state + c.plan.proj_off + (size_t)c.plan.N * desc->tokens * PJW;
+    RACE_TRY(launch_proj(desc, c, k, projk, stream));
+    c.prm.part = state;
+    RACE_TRY(launch(desc, c, K_NC_REDUCE, stream));
+    RACE_TRY(chunk_scan(c, state, 0, total, stream));
   } else {
     // range totals straight into the state slots, then the exclusive scan
     c.prm.part = state;
@@ -854,7 +968,7 @@ int race_forward_reduce(const race_desc_t* desc, race_tensor_t k, race_tensor_t 
 
 int race_forward_readout_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k,
                             race_tensor_t v, const float* planes, const float* scale,
-                            const float* state, race_tensor_t out, float* den, void* workspace,
+                            float* state, race_tensor_t out, float* den, void* workspace,
                             size_t workspace_bytes, cudaStream_t stream) {
   ApiScope scope_;
   Call c;
@@ -881,13 +995,21 @@ int race_forward_readout_ex(const race_desc_t* desc, race_tensor_t q, race_tenso
     fill_layout(c.prm.lv, v);
     c.prm.k = k.data;
     c.prm.v = v.data;
-    RACE_TRY(launch(desc, c, K_C_FWD, stream));
+    if (c.plan.c5) {
+      float* projq = const_cast<float*>(state) + c.plan.proj_off;
+      RACE_TRY(launch_proj(desc, c, q, projq, stream));
+      c.prm.projq = projq;
+      c.prm.projk = projq + (size_t)c.plan.N * desc->tokens * PJW;
+      RACE_TRY(launch(desc, c, K_C5_FWD, stream));
+    } else {
+      RACE_TRY(launch(desc, c, K_C_FWD, stream));
+    }
   }
   return RACE_OK;
 }
 
 int race_forward_readout(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, race_tensor_t v,
-                         const float* planes, const float* scale, const float* state,
+                         const float* planes, const float* scale, float* state,
                          race_tensor_t out, void* workspace, size_t workspace_bytes,
                          cudaStream_t stream) {
   ApiScope scope_;
@@ -934,7 +1056,8 @@ int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k
   RACE_TRY(check_tensor(desc, dout));
   RACE_TRY(check_tensor(desc, dq));
   const race_tensor_t q_in = q;
-  if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &q, c.norm_q, stream));
+  // (the chunkwise causal kernels read the saved projections, not q or k)
+  if (c.normalize_qk && !c.plan.c5) RACE_TRY(normalize_into(desc, c, &q, c.norm_q, stream));
   fill_layout(c.prm.lq, q);
   fill_layout(c.prm.ldo, dout);
   fill_layout(c.prm.ldq, dq);
@@ -950,6 +1073,15 @@ int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k
                                             cudaMemcpyDeviceToDevice, stream);
       if (e != cudaSuccess) return cuda_fail(e);
     }
+    RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 0, stream));
+  } else if (c.plan.c5) {
+    RACE_TRY(check_tensor(desc, v));
+    fill_layout(c.prm.lv, v);
+    c.prm.v = v.data;
+    c.prm.gstate_out = gstate;
+    c5_pointers(c, state, gstate, desc->tokens);
+    RACE_TRY(launch(desc, c, K_C5_BWD_Q, stream));
+    RACE_TRY(chunk_scan(c, gstate, 1, total, stream));
     RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 0, stream));
   } else {
     RACE_TRY(check_tensor(desc, k));
@@ -992,7 +1124,7 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
   RACE_TRY(check_tensor(desc, dk));
   RACE_TRY(check_tensor(desc, dv));
   const race_tensor_t k_in = k;
-  if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &k, c.norm_k, stream));
+  if (c.normalize_qk && !c.plan.c5) RACE_TRY(normalize_into(desc, c, &k, c.norm_k, stream));
   fill_layout(c.prm.lk, k);
   fill_layout(c.prm.lv, v);
   fill_layout(c.prm.ldk, dk);
@@ -1005,6 +1137,13 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
   c.prm.gstate_in = gstate;
   if (!desc->causal) {
     RACE_TRY(launch(desc, c, K_NC_BWD_KV, stream));
+    RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 1, stream));
+  } else if (c.plan.c5) {
+    RACE_TRY(check_tensor(desc, dout));
+    fill_layout(c.prm.ldo, dout);
+    c.prm.dout = dout.data;
+    c5_pointers(c, state, gstate, desc->tokens);
+    RACE_TRY(launch(desc, c, K_C5_BWD_KV, stream));
     RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 1, stream));
   } else {
     RACE_TRY(check_tensor(desc, q));

@@ -1,0 +1,1344 @@
+// race_causal5.cuh -- causal (per-bucket prefix mean) RACE attention on the
+// 5th-generation tensor cores, chunkwise.
+//
+// Per stream n, with W_s(t) = pQ_s(t) / (A_s(t) + eps), A_s(t) = sum_{tau<=t}
+// pK_s(tau) and B_s(t) = sum_{tau<=t} pK_s(tau) v(tau) (misc/race.py:108-138),
+//
+//   out(t) = sum_s W_s(t) B_s(t).
+//
+// The token axis of a stream is cut into P contiguous ranges of whole
+// 128-token tiles; the exclusive prefix (B0, A0) of every range comes from the
+// range totals (the non-causal tcgen05 reduce) and a float64 scan over ranges.
+// A persistent CTA walks its range tile by tile and, inside a tile,
+//
+//   out = W . B0^T + mask(W . pK^T) . V         (mask: tau <= t)
+//
+// with B0 the prefix at the tile start: the 128 x 128 intra-tile matrix
+// G = W pK^T, masked and split into bf16 parts in shared memory, is the A
+// operand of the second product.  The state B0 is carried from tile to tile
+// by the tensor core (B0 += V^T pK accumulates in tensor memory over the
+// range); A(t) is a warp scan of pK over the tile's tokens.
+//
+// The soft hash reads fp32 projections x . P^T of q and k computed once by a
+// pre-pass (k_c5_proj) and kept in the forward's saved state, so the backward
+// passes never read q or k again (16 floats per token instead of D).
+//
+// Precision: split bf16 as in race_t5.cuh -- W, pK, V, B0 and the masked G in
+// two parts (hi + lo, 16 significant bits), every product accumulated in fp32
+// (hi.hi + hi.lo + lo.hi).
+#pragma once
+
+#include "race_t5.cuh"
+
+namespace race {
+namespace c5 {
+
+using namespace t5;
+
+// ------------------------------------------------------------------ pre-pass
+// proj[n][t][j] = x[n][t] . planes[m][j] (j < L K; columns up to 16 are zero),
+// float32 FMAs, one thread per token, the stream's planes in shared memory.
+constexpr int kProjThreads = 128;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kProjThreads) k_c5_proj(const Params prm, const void* x,
+                                                         Layout lx, float* __restrict__ proj) {
+  __shared__ __align__(16) float pl[PJ * D];
+  const int n = blockIdx.y;
+  const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
+  const float* src = prm.planes + (size_t)m * prm.LK * D;
+  for (int i = threadIdx.x; i < PJ * D; i += kProjThreads) pl[i] = i < prm.LK * D ? src[i] : 0.f;
+  __syncthreads();
+  const int64_t t = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
+  if (t >= prm.T) return;
+  const T* row = static_cast<const T*>(x) + stream_offset(lx, n, prm.B, prm.H) + t * lx.st;
+  float xv[D];
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < D / 4; ++i) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(row) + i);
+      xv[4 * i] = v.x; xv[4 * i + 1] = v.y; xv[4 * i + 2] = v.z; xv[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(row) + i);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        xv[8 * i + 2 * j] = f.x;
+        xv[8 * i + 2 * j + 1] = f.y;
+      }
+    }
+  }
+  float out[PJ];
+#pragma unroll
+  for (int j = 0; j < PJ; ++j) {
+    const float4* p4 = reinterpret_cast<const float4*>(pl + j * D);
+    float a = 0.f;
+#pragma unroll
+    for (int i = 0; i < D / 4; ++i) {
+      const float4 w = p4[i];
+      a = fmaf(xv[4 * i], w.x, a);
+      a = fmaf(xv[4 * i + 1], w.y, a);
+      a = fmaf(xv[4 * i + 2], w.z, a);
+      a = fmaf(xv[4 * i + 3], w.w, a);
+    }
+    out[j] = a;
+  }
+  float4* dst = reinterpret_cast<float4*>(proj + ((size_t)n * prm.T + t) * PJ);
+#pragma unroll
+  for (int i = 0; i < PJ / 4; ++i)
+    dst[i] = make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
+}
+
+// ------------------------------------------------------------------ TMA, 3-D
+// [N][T][C] float32 arrays (projections, alpha) are mapped as (C, T, N) with
+// 128-row boxes of whole rows (C * 4 bytes, a multiple of 16, no swizzle).
+__device__ __forceinline__ void tma_load3(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3, %4}], [%5];" ::"r"(saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(saddr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_store3(const CUtensorMap* map, const void* src, int c0, int c1,
+                                           int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(saddr(src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// 5-D tile of one [M, B, T, H, D] tensor onto `bar` (the caller arms it).
+template <typename T, int D>
+__device__ __forceinline__ void tma_rows5(const CUtensorMap* map, void* dst, const Layout& lay,
+                                          const Params& prm, int n, int64_t t0, uint64_t* bar) {
+  using BX = Box<T, D>;
+  const int h = n % prm.H, b = (n / prm.H) % prm.B, m = n / (prm.H * prm.B);
+#pragma unroll
+  for (int x = 0; x < BX::NB; ++x)
+    tma_load5(static_cast<char*>(dst) + x * TT * BX::IB, map, x * BX::IB / (int)sizeof(T), (int)t0,
+              h, b, lay.sm == 0 ? 0 : m, bar);
+}
+
+// instruction descriptor, M = 128, A K-major, B MN-major
+template <int N>
+__host__ __device__ constexpr uint32_t idesc_bmn() {
+  static_assert(N % 16 == 0 && N >= 16 && N <= 256, "M = 128 needs N % 16 == 0, N <= 256");
+  return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(128 >> 4) << 24);
+}
+
+// Inclusive scan over the 32 tokens of a warp (lane = token); returns the
+// warp total in `tot`.
+__device__ __forceinline__ float warp_scan(float x, float& tot) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  tot = __shfl_sync(0xffffffffu, x, 31);
+  return x;
+}
+
+// Writes the 8 bf16 values of one 16-byte chunk (columns 8 c8 .. of row r) of
+// an operand with C columns.
+template <int C>
+__device__ __forceinline__ void put_chunk(bf16* op, int r, int c8, const uint4& u) {
+  reinterpret_cast<uint4*>(op)[chunk<C>(r, c8)] = u;
+}
+
+// hi / lo parts of 8 floats as two 16-byte chunks
+__device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
+  split2(v[0], v[1], hi.x, lo.x);
+  split2(v[2], v[3], hi.y, lo.y);
+  split2(v[4], v[5], hi.z, lo.z);
+  split2(v[6], v[7], hi.w, lo.w);
+}
+
+// ------------------------------------------------------------------ F2 forward
+template <int D, int SPAD>
+struct FwdLay {
+  static constexpr int NTH = 4;                         // threads per token
+  static constexpr int SP = (SPAD + 15) / 16 * 16;      // bucket columns
+  static constexpr int NFULL = 2;                       // input slots (projections + v)
+  static constexpr int VX = 0;                          // [2] v slots (landed, then hi | lo)
+  static constexpr int PJX = VX + 2 * Slot<D>::FLOATS;  // [2] projQ [TT][16] then projK [TT][16]
+  static constexpr int PJF = 2 * TT * PJ;               // floats per projection slot
+  static constexpr int GM = PJX + 2 * PJF;              // bf16 [TT x TT] masked G, hi then lo;
+                                                        // later the out tile's staging
+  static constexpr int PK = GM + TT * TT;               // bf16 [TT x 2SP] pK (hi | lo)
+  static constexpr int WH = PK + TT * SP;               // bf16 [TT x 2SP] W (hi | hi)
+  static constexpr int WL = WH + TT * SP;               // bf16 [TT x SP] W lo
+  static constexpr int B0 = WL + TT * SP / 2;           // bf16 [D x 2SP] B0^T (hi | lo)
+  static constexpr int B0F = B0 + D * SP;               // fp32 [SP][D] prefix at the range start
+  static constexpr int A0 = B0F + SP * D;               // double [SP] key mass at the tile start
+  static constexpr int SCAN = A0 + 2 * SP;              // [SP][4] per-warp token totals
+  static constexpr int BAR = SCAN + 4 * SP;
+  static constexpr int FLOATS = BAR + 16 + 256;         // + slack for 1 KB alignment
+  static constexpr int TCOLS = 256;                     // G [0, 128), OUT [128, 128 + D), ST
+  static constexpr int C_G = 0, C_OUT = 128, C_ST = 128 + D;   // ST: M = 64, 2 SP columns
+  static_assert(C_ST + 2 * SP <= TCOLS, "tensor-memory columns");
+  static_assert(GM % 256 == 0 && VX % 256 == 0, "1 KB aligned TMA boxes");
+  static_assert(FLOATS * 4 <= 227 * 1024, "shared memory");
+};
+
+// Forward readout of one causal range per work item (maps: 0 projQ, 1 projK,
+// 2 v, 3 out).
+template <typename T, int D, int SPAD, int K>
+__global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
+    k_c5_fwd(const Params prm, const __grid_constant__ TmaMaps maps) {
+  using LY = FwdLay<D, SPAD>;
+  constexpr int SP = LY::SP, NTH = LY::NTH, W = D / NTH;
+  using G = Groups<K>;
+  constexpr int NG = SP / G::GB;                       // bucket groups
+  constexpr int MYG = (NG + NTH - 1) / NTH;            // groups per thread (at most)
+  constexpr int GC = TT / NTH;                         // G columns per thread
+  T5_PROLOGUE
+  (void)cur_m;
+  (void)cur_n;
+  bf16* pk = reinterpret_cast<bf16*>(sm + LY::PK);
+  bf16* wh = reinterpret_cast<bf16*>(sm + LY::WH);
+  bf16* wl = reinterpret_cast<bf16*>(sm + LY::WL);
+  bf16* b0 = reinterpret_cast<bf16*>(sm + LY::B0);
+  bf16* gm_hi = reinterpret_cast<bf16*>(sm + LY::GM);
+  bf16* gm_lo = gm_hi + TT * TT;
+  float* b0f = sm + LY::B0F;
+  double* a0 = reinterpret_cast<double*>(sm + LY::A0);
+  float* scan = sm + LY::SCAN;
+  const int lane = tid & 31, quad = warp & 3;
+  for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
+    const Item it = item_of(prm, w);
+    if (it.ntiles <= 0) continue;
+    const int n = it.n;
+    __syncthreads();   // the previous item's MMAs and stores are done with shared memory
+    {
+      // the range's exclusive prefix: B0 [S][D] (fp32) and A0 [S] (float64)
+      const float* st = prm.state + ((size_t)n * prm.P + it.part) * prm.SS;
+      for (int e = tid; e < SP * D; e += TT * NTH) {
+        const int s = e / D;
+        b0f[e] = s < prm.S ? st[e] : 0.f;
+      }
+      for (int s = tid; s < SP; s += TT * NTH) a0[s] = s < prm.S ? (double)st[prm.S * D + s] : 0.0;
+    }
+    __syncthreads();
+    // B0 operand of the first tile: the range prefix
+    if (tid < D) {
+      for (int s8 = 0; s8 < SP / 8; ++s8) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = b0f[(s8 * 8 + e) * D + tid];
+        uint4 hi, lo;
+        split8(v, hi, lo);
+        put_chunk<2 * SP>(b0, tid, s8, hi);
+        put_chunk<2 * SP>(b0, tid, SP / 8 + s8, lo);
+      }
+    }
+    auto load = [&](int j) {
+      if (failed) return;
+      const int f = j & 1;
+      inflight |= 1u << f;
+      if (tid == 0) {
+        const int64_t t0 = it.t0 + (int64_t)j * TT;
+        float* pj = sm + LY::PJX + f * LY::PJF;
+        fence_async_smem();
+        bar_expect_tx(full + f, (uint32_t)(Box<T, D>::BYTES + 2 * TT * PJ * 4));
+        tma_load3(pj, &maps.map[0], 0, (int)t0, n, full + f);
+        tma_load3(pj + TT * PJ, &maps.map[1], 0, (int)t0, n, full + f);
+        tma_rows5<T, D>(&maps.map[2], sm + LY::VX + f * Slot<D>::FLOATS, prm.lv, prm, n, t0,
+                        full + f);
+      }
+    };
+    load(0);
+    for (int i = 0; i < it.ntiles; ++i) {
+      const int64_t tile0 = it.t0 + (int64_t)i * TT;
+      const int f = i & 1;
+      float* VXt = sm + LY::VX + f * Slot<D>::FLOATS;
+      const float* pj = sm + LY::PJX + f * LY::PJF;
+      if (i + 1 < it.ntiles) load(i + 1);
+      T5_WAIT(full + f, (phF >> f) & 1);
+      if (!failed) {
+        phF ^= 1u << f;
+        inflight &= ~(1u << f);
+      }
+      const bool valid = tile0 + row < it.t1;
+      {
+        float y[W];
+        read_cols<T, D, W>(VXt, row, sub * W, y);
+        // hash of this thread's bucket groups, then the key-mass scan
+        float pq[MYG][G::GB], pkv[MYG][G::GB];
+#pragma unroll
+        for (int a = 0; a < MYG; ++a) {
+          const int gi = sub + a * NTH;
+          if (gi < NG) {
+            float pj_[G::GK], h[G::GK];
+            const bool has = gi * G::GK < PJ;
+#pragma unroll
+            for (int k = 0; k < G::GK; ++k) pj_[k] = has ? pj[row * PJ + gi * G::GK + k] : 0.f;
+            group_probs<K>(pj_, gi * G::GT, has ? L : 0, inv_scale, pq[a], h);
+#pragma unroll
+            for (int k = 0; k < G::GK; ++k)
+              pj_[k] = has ? pj[TT * PJ + row * PJ + gi * G::GK + k] : 0.f;
+            group_probs<K>(pj_, gi * G::GT, has ? L : 0, inv_scale, pkv[a], h);
+            if (!valid) {
+#pragma unroll
+              for (int b = 0; b < G::GB; ++b) pq[a][b] = pkv[a][b] = 0.f;
+            }
+          }
+        }
+        __syncthreads();   // v slot read; scan scratch free
+        put_cols<D, W, sizeof(T) == 4 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1),
+                                               nullptr, row, sub * W, y);
+        float incl[MYG][G::GB];
+#pragma unroll
+        for (int a = 0; a < MYG; ++a) {
+          const int gi = sub + a * NTH;
+          if (gi < NG) {
+#pragma unroll
+            for (int b = 0; b < G::GB; ++b) {
+              float tot;
+              incl[a][b] = warp_scan(pkv[a][b], tot);
+              if (lane == 31) scan[(gi * G::GB + b) * 4 + quad] = tot;
+            }
+          }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int a = 0; a < MYG; ++a) {
+          const int gi = sub + a * NTH;
+          if (gi < NG) {
+            float wv[G::GB];
+#pragma unroll
+            for (int b = 0; b < G::GB; ++b) {
+              const int s = gi * G::GB + b;
+              float before = 0.f;
+              for (int q2 = 0; q2 < quad; ++q2) before += scan[s * 4 + q2];
+              const float A = (float)(a0[s] + (double)(before + incl[a][b]));
+              wv[b] = pq[a][b] / (A + prm.eps);
+            }
+            // pK (hi | lo), W (hi | hi) and W lo, 8 buckets per chunk
+#pragma unroll
+            for (int c8 = 0; c8 < G::GB / 8; ++c8) {
+              const int c = gi * G::GB / 8 + c8;
+              uint4 hi, lo;
+              split8(pkv[a] + 8 * c8, hi, lo);
+              put_chunk<2 * SP>(pk, row, c, hi);
+              put_chunk<2 * SP>(pk, row, SP / 8 + c, lo);
+              split8(wv + 8 * c8, hi, lo);
+              put_chunk<2 * SP>(wh, row, c, hi);
+              put_chunk<2 * SP>(wh, row, SP / 8 + c, hi);
+              put_chunk<SP>(wl, row, c, lo);
+            }
+          }
+        }
+      }
+      // padding buckets (>= the groups' columns) of pK / W stay zero: every
+      // group column below SP is written above
+      fence_async_smem();
+      fence_before();
+      __syncthreads();
+      if (tid == 0 && !failed) {
+        fence_after();
+        // the previous tile's out store has left the staging area (the masked
+        // G written after this barrier): no thread passes barA before this
+        bulk_wait_read();
+        // G = W . pK^T (hi.hi + hi.lo through the duplicated W hi, lo.hi)
+#pragma unroll
+        for (int ks = 0; ks < 2 * SP / 16; ++ks)
+          mma(tbase + LY::C_G, desc<2 * SP>(wh, ks), desc<2 * SP>(pk, ks), idesc<TT>(), ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < SP / 16; ++ks)
+          mma(tbase + LY::C_G, desc<SP>(wl, ks), desc<2 * SP>(pk, ks), idesc<TT>(), true);
+        // OUT = W . B0^T
+#pragma unroll
+        for (int ks = 0; ks < 2 * SP / 16; ++ks)
+          mma(tbase + LY::C_OUT, desc<2 * SP>(wh, ks), desc<2 * SP>(b0, ks), idesc<D>(), ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < SP / 16; ++ks)
+          mma(tbase + LY::C_OUT, desc<SP>(wl, ks), desc<2 * SP>(b0, ks), idesc<D>(), true);
+        { commit(barA); ++issA; }
+      }
+      // the tile's key mass moves the prefix on (every thread has read a0)
+      if (sub == 0 && tid < SP) {
+        float tot = 0.f;
+        for (int q2 = 0; q2 < 4; ++q2) tot += scan[tid * 4 + q2];
+        a0[tid] += (double)tot;
+      }
+      T5_WAIT(barA, phA);
+      phA ^= 1;
+      fence_after();
+      {
+        // masked G row: columns [GC sub, GC sub + GC) of token `row`
+#pragma unroll
+        for (int c0 = 0; c0 < GC; c0 += 16) {
+          float g[16];
+          tld16(tlane + LY::C_G + GC * sub + c0, g);
+          tld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (GC * sub + c0 + e > row) g[e] = 0.f;
+#pragma unroll
+          for (int c8 = 0; c8 < 2; ++c8) {
+            uint4 hi, lo;
+            split8(g + 8 * c8, hi, lo);
+            const int c = (GC * sub + c0) / 8 + c8;
+            put_chunk<TT>(gm_hi, row, c, hi);
+            put_chunk<TT>(gm_lo, row, c, lo);
+          }
+        }
+      }
+      fence_async_smem();
+      fence_before();
+      __syncthreads();
+      if (tid == 0 && !failed) {
+        fence_after();
+        const bf16* vp[2] = {Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1)};
+        const bf16* gp[2] = {gm_hi, gm_lo};
+        // OUT += mask(G) . V  (hi.hi, hi.lo, lo.hi; bf16 v is exact in its first part)
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            if (a + b == 2 || (sizeof(T) == 2 && b == 1)) continue;
+#pragma unroll
+            for (int ks = 0; ks < TT / 16; ++ks)
+              mma(tbase + LY::C_OUT, desc<TT>(gp[a], ks), desc_mn<D>(vp[b], ks), idesc_bmn<D>(),
+                  true);
+          }
+        // ST[d][s] += sum_t v[t][d] pK[t][s] over the range (both parts of pK along N)
+#pragma unroll
+        for (int a = 0; a < (sizeof(T) == 4 ? 2 : 1); ++a)
+#pragma unroll
+          for (int ks = 0; ks < TT / 16; ++ks)
+            mma(tbase + LY::C_ST, desc_mn<D>(vp[a], ks), desc_mn<2 * SP>(pk, ks),
+                idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
+        { commit(barB); ++issB; }
+      }
+      T5_WAIT(barB, phB);
+      phB ^= 1;
+      fence_after();
+      {
+        float o[W];
+        tld_sum<W, 1>(tlane + LY::C_OUT + sub * W, 0, o);
+        // staging of the out tile in the (consumed) masked-G area
+        put_tile_cols<T, D, W>(sm + LY::GM, row, sub * W, o);
+      }
+      // B0 of the next tile: range prefix + the state accumulated so far;
+      // lane 32 q + l (l < 16) of warps 0..3 holds row d = 16 q + l
+      if (i + 1 < it.ntiles && sub == 0) {
+        const int d = 16 * quad + lane;
+        float stv[2 * SP];
+#pragma unroll
+        for (int c = 0; c < 2 * SP; c += 8) tld8(tlane + LY::C_ST + c, stv + c);
+        tld_wait();
+        if (lane < 16 && d < D) {
+#pragma unroll
+          for (int s8 = 0; s8 < SP / 8; ++s8) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int s = s8 * 8 + e;
+              v[e] = b0f[s * D + d] + stv[s] + stv[SP + s];
+            }
+            uint4 hi, lo;
+            split8(v, hi, lo);
+            put_chunk<2 * SP>(b0, d, s8, hi);
+            put_chunk<2 * SP>(b0, d, SP / 8 + s8, lo);
+          }
+        }
+      }
+      fence_async_smem();
+      fence_before();
+      __syncthreads();
+      if (tid == 0 && !failed) {
+        tma_store_tile<T, D>(&maps.map[3], sm + LY::GM, prm.lo, prm, n, tile0);
+        bulk_commit();
+      }
+      if (T5_VOTE()) break;
+    }
+  }
+  T5_EPILOGUE
+}
+
+
+// ------------------------------------------------------------------ B1 query backward
+// Per tile (prefix B0, A0 at the tile start as in the forward):
+//   R = dO . B0^T + mask(dO . V^T) . pK       R_s(t) = dO(t) . B_s(t)
+//   dpQ_s = R_s / (A_s + eps),  alpha_s = -W_s dpQ_s,  dq = dproj(pQ, dpQ) . P
+// (misc/race.py:108-138 differentiated; kernels/cpu/race_pref.cpp:104-181 with
+// W folded in).  Per range: sum_t W_s(t) dO(t) and sum_t alpha_s(t) into the
+// range's gradient slot (the reverse scan over ranges makes them suffixes);
+// alpha per token and the key mass at every tile start for the key backward.
+template <int D, int SPAD>
+struct BwdQLayC {
+  static constexpr int NTH = 4;
+  static constexpr int SP = (SPAD + 15) / 16 * 16;
+  static constexpr int NFULL = 1;                       // one set of input slots
+  static constexpr int VX = 0;                          // v (landed, then hi | lo)
+  static constexpr int GX = VX + Slot<D>::FLOATS;       // dO (landed, then hi | lo)
+  static constexpr int PJX = GX + Slot<D>::FLOATS;      // projQ [TT][16] then projK [TT][16]
+  static constexpr int MM = PJX + 2 * TT * PJ;          // bf16 [TT x TT] masked dO V^T, hi then lo;
+                                                        // later alpha [TT][SA] and dq staging
+  static constexpr int STG_DQ = MM + TT * SP;           // dq staging (1 KB aligned)
+  static constexpr int PK = MM + TT * TT;               // bf16 [TT x 2SP] pK (hi | lo)
+  static constexpr int WP = PK + TT * SP;               // bf16 [TT x 2SP] W (hi | lo)
+  static constexpr int B0S = WP + TT * SP;              // bf16 [2SP x D] B0 (hi rows; lo rows)
+  static constexpr int DJ = B0S + SP * D;               // bf16 [TT x PJ] dproj hi, then lo
+  static constexpr int PT = DJ + TT * PJ;               // bf16 [2D x PJ] planes^T (hi; lo)
+  static constexpr int B0F = PT + D * PJ;               // fp32 [SP][D] prefix at the range start
+  static constexpr int A0 = B0F + SP * D;               // double [SP]
+  static constexpr int SCAN = A0 + 2 * SP;              // [SP][4]
+  static constexpr int RED = SCAN + 4 * SP;             // [16]
+  static constexpr int BAR = RED + 16;
+  static constexpr int FLOATS = BAR + 16 + 256;
+  static constexpr int TCOLS = 512;
+  // M [0, 128), R [128, 128 + 2SP), DQ [192, 192 + 2D), ST / WD (M = 64) 2SP each
+  static constexpr int C_M = 0, C_R = 128, C_DQ = 192, C_ST = 192 + 2 * D, C_WD = C_ST + 64;
+  static_assert(C_R + 2 * SP <= C_DQ && C_WD + 2 * SP <= TCOLS, "tensor-memory columns");
+  static_assert(STG_DQ + TT * D <= PK, "staging inside the masked-matrix area");
+  static_assert(MM % 256 == 0 && STG_DQ % 256 == 0, "1 KB aligned TMA boxes");
+  static_assert(FLOATS * 4 <= 227 * 1024, "shared memory");
+};
+
+// maps: 0 projQ, 1 projK, 2 v, 3 dO, 4 dq, 5 alpha ([N][T][SA] float32)
+template <typename T, int D, int SPAD, int K>
+__global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
+    k_c5_bwd_q(const Params prm, const __grid_constant__ TmaMaps maps) {
+  using LY = BwdQLayC<D, SPAD>;
+  constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
+  using G = Groups<K>;
+  constexpr int NG = SP / G::GB;
+  constexpr int MYG = (NG + NTH - 1) / NTH;
+  constexpr int GC = TT / NTH;
+  constexpr bool F32 = sizeof(T) == 4;
+  T5_PROLOGUE
+  (void)cur_n;
+  bf16* pk = reinterpret_cast<bf16*>(sm + LY::PK);
+  bf16* wp = reinterpret_cast<bf16*>(sm + LY::WP);
+  bf16* b0s = reinterpret_cast<bf16*>(sm + LY::B0S);
+  bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
+  bf16* pt = reinterpret_cast<bf16*>(sm + LY::PT);
+  bf16* mm_hi = reinterpret_cast<bf16*>(sm + LY::MM);
+  bf16* mm_lo = mm_hi + TT * TT;
+  float* b0f = sm + LY::B0F;
+  double* a0 = reinterpret_cast<double*>(sm + LY::A0);
+  float* scan = sm + LY::SCAN;
+  const int lane = tid & 31, quad = warp & 3;
+  const int64_t tiles_n = (prm.T + TT - 1) / TT;
+  // planes of DJ not covered by any bucket group stay zero
+  for (int i = tid; i < TT * PJ; i += NTHR) reinterpret_cast<float*>(dj)[i] = 0.f;
+  for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
+    const Item it = item_of(prm, w);
+    const int n = it.n;
+    float* slot = prm.gstate_out + ((size_t)n * prm.P + it.part) * prm.SS;
+    float ds = 0.f;
+    float asum[MYG][G::GB];
+#pragma unroll
+    for (int a = 0; a < MYG; ++a)
+#pragma unroll
+      for (int b = 0; b < G::GB; ++b) asum[a][b] = 0.f;
+    if (it.ntiles > 0) {
+      const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
+      __syncthreads();
+      if (m != cur_m) {
+        const float* pl = prm.planes + (size_t)m * prm.LK * D;
+        put_stack<D, PJ, 2, NTHR>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+        cur_m = m;
+      }
+      const float* st = prm.state + ((size_t)n * prm.P + it.part) * prm.SS;
+      for (int e = tid; e < SP * D; e += NTHR) b0f[e] = e / D < prm.S ? st[e] : 0.f;
+      for (int s2 = tid; s2 < SP; s2 += NTHR) a0[s2] = s2 < prm.S ? (double)st[prm.S * D + s2] : 0.0;
+      __syncthreads();
+      // B0 operand of the first tile: rows s (hi), SP + s (lo), columns d
+      for (int e = tid; e < SP * D; e += NTHR) {
+        const int s2 = e / D, d = e % D;
+        const float x = b0f[e];
+        const bf16 h = __float2bfloat16_rn(x);
+        b0s[elem<D>(s2, d)] = h;
+        b0s[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
+      }
+      auto load = [&](int j) {
+        if (failed) return;
+        inflight |= 1u;
+        if (tid == 0) {
+          const int64_t t0 = it.t0 + (int64_t)j * TT;
+          float* pj = sm + LY::PJX;
+          fence_async_smem();
+          bar_expect_tx(full, (uint32_t)(2 * Box<T, D>::BYTES + 2 * TT * PJ * 4));
+          tma_load3(pj, &maps.map[0], 0, (int)t0, n, full);
+          tma_load3(pj + TT * PJ, &maps.map[1], 0, (int)t0, n, full);
+          tma_rows5<T, D>(&maps.map[2], sm + LY::VX, prm.lv, prm, n, t0, full);
+          tma_rows5<T, D>(&maps.map[3], sm + LY::GX, prm.ldo, prm, n, t0, full);
+        }
+      };
+      load(0);
+      for (int i = 0; i < it.ntiles; ++i) {
+        const int64_t tile0 = it.t0 + (int64_t)i * TT;
+        float* VXt = sm + LY::VX;
+        float* GXt = sm + LY::GX;
+        const float* pj = sm + LY::PJX;
+        T5_WAIT(full, phF & 1);
+        if (!failed) {
+          phF ^= 1u;
+          inflight &= ~1u;
+        }
+        const bool valid = tile0 + row < it.t1;
+        float pq[MYG][G::GB], hq[MYG][G::GK], inv[MYG][G::GB], wv[MYG][G::GB];
+        {
+          float y[W], g[W];
+          read_cols<T, D, W>(VXt, row, sub * W, y);
+          read_cols<T, D, W>(GXt, row, sub * W, g);
+          float pkv[MYG][G::GB];
+#pragma unroll
+          for (int a = 0; a < MYG; ++a) {
+            const int gi = sub + a * NTH;
+            if (gi < NG) {
+              float pj_[G::GK], h[G::GK];
+              const bool has = gi * G::GK < PJ;
+#pragma unroll
+              for (int k = 0; k < G::GK; ++k) pj_[k] = has ? pj[row * PJ + gi * G::GK + k] : 0.f;
+              group_probs<K>(pj_, gi * G::GT, has ? L : 0, inv_scale, pq[a], hq[a]);
+#pragma unroll
+              for (int k = 0; k < G::GK; ++k)
+                pj_[k] = has ? pj[TT * PJ + row * PJ + gi * G::GK + k] : 0.f;
+              group_probs<K>(pj_, gi * G::GT, has ? L : 0, inv_scale, pkv[a], h);
+              if (!valid) {
+#pragma unroll
+                for (int b = 0; b < G::GB; ++b) pq[a][b] = pkv[a][b] = 0.f;
+              }
+            }
+          }
+          __syncthreads();   // raw tiles read; scan scratch free
+          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), nullptr, row,
+                                      sub * W, y);
+          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1), nullptr, row,
+                                      sub * W, g);
+          float incl[MYG][G::GB];
+#pragma unroll
+          for (int a = 0; a < MYG; ++a) {
+            const int gi = sub + a * NTH;
+            if (gi < NG) {
+#pragma unroll
+              for (int b = 0; b < G::GB; ++b) {
+                float tot;
+                incl[a][b] = warp_scan(pkv[a][b], tot);
+                if (lane == 31) scan[(gi * G::GB + b) * 4 + quad] = tot;
+              }
+            }
+          }
+          __syncthreads();
+#pragma unroll
+          for (int a = 0; a < MYG; ++a) {
+            const int gi = sub + a * NTH;
+            if (gi < NG) {
+#pragma unroll
+              for (int b = 0; b < G::GB; ++b) {
+                const int s2 = gi * G::GB + b;
+                float before = 0.f;
+                for (int q2 = 0; q2 < quad; ++q2) before += scan[s2 * 4 + q2];
+                const float A = (float)(a0[s2] + (double)(before + incl[a][b]));
+                inv[a][b] = 1.f / (A + prm.eps);
+                wv[a][b] = pq[a][b] * inv[a][b];
+              }
+#pragma unroll
+              for (int c8 = 0; c8 < G::GB / 8; ++c8) {
+                const int c = gi * G::GB / 8 + c8;
+                uint4 hi, lo;
+                split8(pkv[a] + 8 * c8, hi, lo);
+                put_chunk<2 * SP>(pk, row, c, hi);
+                put_chunk<2 * SP>(pk, row, SP / 8 + c, lo);
+                split8(wv[a] + 8 * c8, hi, lo);
+                put_chunk<2 * SP>(wp, row, c, hi);
+                put_chunk<2 * SP>(wp, row, SP / 8 + c, lo);
+              }
+            }
+          }
+        }
+        // the key mass at this tile's start, for the key-side walk
+        if (sub == 0 && tid < SP)
+          prm.range_mass[((size_t)n * tiles_n + tile0 / TT) * SP + tid] = a0[tid];
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          fence_after();
+          bulk_wait_read();   // the previous tile's alpha / dq staging sits in MM
+          const bf16* vp[2] = {Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1)};
+          const bf16* gp[2] = {Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1)};
+          // M = dO . V^T  (hi.hi, hi.lo, lo.hi)
+#pragma unroll
+          for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              if (a + b == 2 || (!F32 && a + b > 0)) continue;
+#pragma unroll
+              for (int ks = 0; ks < D / 16; ++ks)
+                mma(tbase + LY::C_M, desc<D>(gp[a], ks), desc<D>(vp[b], ks), idesc<TT>(),
+                    a + b > 0 || ks > 0);
+            }
+          // R = dO . B0^T (B0 hi and lo stacked along N)
+#pragma unroll
+          for (int a = 0; a < (F32 ? 2 : 1); ++a)
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks)
+              mma(tbase + LY::C_R, desc<D>(gp[a], ks), desc<D>(b0s, ks), idesc<2 * SP>(),
+                  a > 0 || ks > 0);
+          // ST[d][s] += v^T pK (the next tiles' B0);  WD[d][s] += dO^T W (range total)
+#pragma unroll
+          for (int a = 0; a < (F32 ? 2 : 1); ++a)
+#pragma unroll
+            for (int ks = 0; ks < TT / 16; ++ks) {
+              mma(tbase + LY::C_ST, desc_mn<D>(vp[a], ks), desc_mn<2 * SP>(pk, ks),
+                  idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
+              mma(tbase + LY::C_WD, desc_mn<D>(gp[a], ks), desc_mn<2 * SP>(wp, ks),
+                  idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
+            }
+          { commit(barA); ++issA; }
+        }
+        if (sub == 0 && tid < SP) {
+          float tot = 0.f;
+          for (int q2 = 0; q2 < 4; ++q2) tot += scan[tid * 4 + q2];
+          a0[tid] += (double)tot;
+        }
+        T5_WAIT(barA, phA);
+        phA ^= 1;
+        // every MMA that reads the input slots has completed: next tile's loads
+        if (i + 1 < it.ntiles) load(i + 1);
+        fence_after();
+#pragma unroll
+        for (int c0 = 0; c0 < GC; c0 += 16) {
+          float g[16];
+          tld16(tlane + LY::C_M + GC * sub + c0, g);
+          tld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (GC * sub + c0 + e > row) g[e] = 0.f;
+#pragma unroll
+          for (int c8 = 0; c8 < 2; ++c8) {
+            uint4 hi, lo;
+            split8(g + 8 * c8, hi, lo);
+            const int c = (GC * sub + c0) / 8 + c8;
+            put_chunk<TT>(mm_hi, row, c, hi);
+            put_chunk<TT>(mm_lo, row, c, lo);
+          }
+        }
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          fence_after();
+          // R += mask(M) . pK  (both parts of pK along N, both parts of M)
+#pragma unroll
+          for (int a = 0; a < 2; ++a) {
+            const bf16* mp = a ? mm_lo : mm_hi;
+#pragma unroll
+            for (int ks = 0; ks < TT / 16; ++ks)
+              mma(tbase + LY::C_R, desc<TT>(mp, ks), desc_mn<2 * SP>(pk, ks), idesc_bmn<2 * SP>(),
+                  true);
+          }
+          { commit(barB); ++issB; }
+        }
+        T5_WAIT(barB, phB);
+        phB ^= 1;
+        fence_after();
+        float* stg_a = sm + LY::MM;   // alpha staging [TT][SA] (the masked matrix is consumed)
+#pragma unroll 1
+        for (int a = 0; a < MYG; ++a) {
+          const int gi = sub + a * NTH;
+          if (gi < NG) {
+            float r[G::GB], dpq[G::GB], dj_[G::GK];
+            tld_sum<G::GB, 2>(tlane + LY::C_R + gi * G::GB, SP, r);
+            float al[G::GB];
+#pragma unroll
+            for (int b = 0; b < G::GB; ++b) {
+              dpq[b] = valid ? r[b] * inv[a][b] : 0.f;
+              al[b] = -wv[a][b] * dpq[b];
+              asum[a][b] += al[b];
+            }
+            float dsl = 0.f;
+            group_probs_bwd<K>(pq[a], dpq, hq[a], inv_scale, dj_, dsl);
+            if (valid) ds += dsl;
+#pragma unroll
+            for (int b = 0; b < G::GB; ++b) {
+              const int s2 = gi * G::GB + b;
+              if (s2 < prm.SA) stg_a[row * prm.SA + s2] = s2 < prm.S ? al[b] : 0.f;
+            }
+            if (gi * G::GK < PJ) {
+#pragma unroll
+              for (int j = 0; j < G::GK; ++j) {
+                const int jj = gi * G::GK + j;
+                if (jj < PJ) {
+                  const bf16 hb = __float2bfloat16_rn(valid ? dj_[j] : 0.f);
+                  dj[elem<PJ>(row, jj)] = hb;
+                  dj[TT * PJ + elem<PJ>(row, jj)] =
+                      __float2bfloat16_rn((valid ? dj_[j] : 0.f) - __bfloat162float(hb));
+                }
+              }
+            }
+          }
+        }
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          fence_after();
+          gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DQ, dj, dj + TT * PJ, nullptr, 2, pt,
+                                            false);
+          { commit(barA); ++issA; }
+          tma_store3(&maps.map[5], stg_a, 0, (int)tile0, n);
+          bulk_commit();
+        }
+        T5_WAIT(barA, phA);
+        phA ^= 1;
+        fence_after();
+        {
+          float o[W];
+          tld_sum<W>(tlane + LY::C_DQ + sub * W, D, o);
+          put_tile_cols<T, D, W>(sm + LY::STG_DQ, row, sub * W, o);
+        }
+        // B0 of the next tile: range prefix + the state so far (M = 64 lanes)
+        if (i + 1 < it.ntiles && sub == 0) {
+          const int d = 16 * quad + lane;
+          float stv[2 * SP];
+#pragma unroll
+          for (int c = 0; c < 2 * SP; c += 8) tld8(tlane + LY::C_ST + c, stv + c);
+          tld_wait();
+          if (lane < 16 && d < D) {
+#pragma unroll
+            for (int s2 = 0; s2 < SP; ++s2) {
+              const float x = b0f[s2 * D + d] + stv[s2] + stv[SP + s2];
+              const bf16 h = __float2bfloat16_rn(x);
+              b0s[elem<D>(s2, d)] = h;
+              b0s[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
+            }
+          }
+        }
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          tma_store_tile<T, D>(&maps.map[4], sm + LY::STG_DQ, prm.ldq, prm, n, tile0);
+          bulk_commit();
+        }
+        if (T5_VOTE()) break;
+      }
+      if (failed) break;
+      // range totals: sum_t W dO (M = 64 lanes) and sum_t alpha
+      fence_after();
+      if (sub == 0) {
+        const int d = 16 * quad + lane;
+#pragma unroll
+        for (int c = 0; c < SP; c += 8) {
+          float e0[8], e1[8];
+          tld8(tlane + LY::C_WD + c, e0);
+          tld8(tlane + LY::C_WD + SP + c, e1);
+          tld_wait();
+          if (lane < 16 && d < D) {
+#pragma unroll
+            for (int x = 0; x < 8; ++x)
+              if (c + x < prm.S) slot[(c + x) * D + d] = e0[x] + e1[x];
+          }
+        }
+      }
+      fence_before();
+      if (tid == 0) bulk_wait_read();
+      __syncthreads();
+      float* ms = sm + LY::MM;   // [TT][SP] per-thread alpha sums
+#pragma unroll
+      for (int a = 0; a < MYG; ++a)
+        if (sub + a * NTH < NG)
+#pragma unroll
+          for (int b = 0; b < G::GB; ++b) ms[row * SP + (sub + a * NTH) * G::GB + b] = asum[a][b];
+      __syncthreads();
+      if (tid < prm.S) {
+        float tot = 0.f;
+        for (int r2 = 0; r2 < TT; ++r2) tot += ms[r2 * SP + tid];
+        slot[prm.S * D + tid] = tot;
+      }
+    } else {
+      for (int e2 = tid; e2 < prm.S * D + prm.S; e2 += NTHR) slot[e2] = 0.f;
+    }
+    float x = ds;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    __syncthreads();
+    if ((tid & 31) == 0) sm[LY::RED + warp] = x;
+    __syncthreads();
+    if (tid == 0) {
+      float tot = 0.f;
+      for (int i = 0; i < NTHR / 32; ++i) tot += sm[LY::RED + i];
+      prm.dscale_part[(size_t)n * prm.P + it.part] = tot;
+    }
+  }
+  T5_EPILOGUE
+}
+
+
+// ------------------------------------------------------------------ B2 key/value backward
+// Walks each range from its last tile to its first with the exclusive suffix
+// (BS = sum_{later t} W_s(t) dO(t), AS = sum_{later t} alpha_s(t)) of the
+// range's end.  Per tile, with asuf(tau) = AS + the in-tile suffix of alpha:
+//   dpK(tau) = asuf(tau) + v . BS^T + mask'(V . dO^T) . W
+//   dv(tau)  = pK . BS + mask'(pK . W^T) . dO          (mask': t >= tau)
+//   dk       = dproj(pK, dpK) . P
+// (kernels/cpu/race_pref.cpp:183-220 with W folded in).  The key mass at the
+// tile start comes from the query walk's records.
+template <int D, int SPAD>
+struct BwdKVLayC {
+  static constexpr int NTH = 4;
+  static constexpr int SP = (SPAD + 15) / 16 * 16;
+  static constexpr int NFULL = 2;                       // 0: v + projections, 1: dO
+  static constexpr int VX = 0;
+  static constexpr int GX = VX + Slot<D>::FLOATS;
+  static constexpr int PJX = GX + Slot<D>::FLOATS;      // projQ [TT][16] then projK [TT][16]
+  static constexpr int MM = PJX + 2 * TT * PJ;          // bf16 [TT x TT] masked matrix (hi, lo);
+                                                        // later the dv and dk staging
+  static constexpr int PK = MM + TT * TT;               // bf16 [TT x 2SP] pK (hi | lo)
+  static constexpr int WH = PK + TT * SP;               // bf16 [TT x 2SP] W (hi | hi)
+  static constexpr int WL = WH + TT * SP;               // bf16 [TT x SP] W lo
+  static constexpr int BSS = WL + TT * SP / 2;          // bf16 [2SP x D] BS (hi rows; lo rows)
+  static constexpr int BST2 = BSS + SP * D;             // bf16 [D x 2SP] BS^T (hi | hi)
+  static constexpr int BSTL = BST2 + SP * D;            // bf16 [D x SP] BS^T lo
+  static constexpr int DJ = BSTL + SP * D / 2;          // bf16 [TT x PJ] hi, then lo
+  static constexpr int PT = DJ + TT * PJ;               // bf16 [2D x PJ] planes^T (hi; lo)
+  static constexpr int BSF = PT + D * PJ;               // fp32 [SP][D] suffix at the range end
+  static constexpr int AS = BSF + SP * D;               // double [SP] alpha suffix, running
+  static constexpr int A0T = AS + 2 * SP;               // double [SP] key mass at the tile start
+  static constexpr int SCAN = A0T + 2 * SP;             // [SP][4] per-warp key-mass totals
+  static constexpr int SCAN2 = SCAN + 4 * SP;           // [SP][4] per-warp alpha totals
+  static constexpr int RED = SCAN2 + 4 * SP;
+  static constexpr int BAR = RED + 16;
+  static constexpr int FLOATS = BAR + 16 + 256;
+  static constexpr int TCOLS = 512;
+  // MT / DK [0, 128), GT [128, 256), VB [256, 256 + 2SP), DV [C_DV, C_DV + D), BS (M = 64) 2SP
+  static constexpr int C_MT = 0, C_DK = 0, C_GT = 128, C_VB = 256, C_DV = 256 + 2 * SP,
+                       C_BS = C_DV + D;
+  static_assert(C_BS + 2 * SP <= TCOLS, "tensor-memory columns");
+  static_assert(2 * TT * D <= TT * TT, "dv and dk staging inside the masked-matrix area");
+  static_assert(MM % 256 == 0, "1 KB aligned TMA boxes");
+  static_assert(FLOATS * 4 <= 227 * 1024, "shared memory");
+};
+
+// maps: 0 projQ, 1 projK, 2 v, 3 dO, 5 dk, 6 dv; alpha is read directly
+template <typename T, int D, int SPAD, int K>
+__global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
+    k_c5_bwd_kv(const Params prm, const __grid_constant__ TmaMaps maps) {
+  using LY = BwdKVLayC<D, SPAD>;
+  constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
+  using G = Groups<K>;
+  constexpr int NG = SP / G::GB;
+  constexpr int MYG = (NG + NTH - 1) / NTH;
+  constexpr int GC = TT / NTH;
+  constexpr bool F32 = sizeof(T) == 4;
+  T5_PROLOGUE
+  (void)cur_n;
+  bf16* pk = reinterpret_cast<bf16*>(sm + LY::PK);
+  bf16* wh = reinterpret_cast<bf16*>(sm + LY::WH);
+  bf16* wl = reinterpret_cast<bf16*>(sm + LY::WL);
+  bf16* bss = reinterpret_cast<bf16*>(sm + LY::BSS);
+  bf16* bst2 = reinterpret_cast<bf16*>(sm + LY::BST2);
+  bf16* bstl = reinterpret_cast<bf16*>(sm + LY::BSTL);
+  bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
+  bf16* pt = reinterpret_cast<bf16*>(sm + LY::PT);
+  bf16* mm_hi = reinterpret_cast<bf16*>(sm + LY::MM);
+  bf16* mm_lo = mm_hi + TT * TT;
+  float* bsf = sm + LY::BSF;
+  double* as = reinterpret_cast<double*>(sm + LY::AS);
+  double* a0t = reinterpret_cast<double*>(sm + LY::A0T);
+  float* scan = sm + LY::SCAN;
+  float* scan2 = sm + LY::SCAN2;
+  const int lane = tid & 31, quad = warp & 3;
+  const int64_t tiles_n = (prm.T + TT - 1) / TT;
+  for (int i = tid; i < TT * PJ; i += NTHR) reinterpret_cast<float*>(dj)[i] = 0.f;
+
+  // BS operands (BSS, BST2, BSTL) from BS values x(s, d): one (s, d) entry
+  auto put_bs = [&](int s2, int d, float x) {
+    const bf16 h = __float2bfloat16_rn(x);
+    const bf16 l = __float2bfloat16_rn(x - __bfloat162float(h));
+    bss[elem<D>(s2, d)] = h;
+    bss[elem<D>(SP + s2, d)] = l;
+    bst2[elem<2 * SP>(d, s2)] = h;
+    bst2[elem<2 * SP>(d, SP + s2)] = h;
+    bstl[elem<SP>(d, s2)] = l;
+  };
+
+  for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
+    const Item it = item_of(prm, w);
+    const int n = it.n;
+    float ds = 0.f;
+    if (it.ntiles > 0) {
+      const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
+      __syncthreads();
+      if (m != cur_m) {
+        const float* pl = prm.planes + (size_t)m * prm.LK * D;
+        put_stack<D, PJ, 2, NTHR>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+        cur_m = m;
+      }
+      const float* gs = prm.gstate_in + ((size_t)n * prm.P + it.part) * prm.SS;
+      for (int e = tid; e < SP * D; e += NTHR) bsf[e] = e / D < prm.S ? gs[e] : 0.f;
+      for (int s2 = tid; s2 < SP; s2 += NTHR) as[s2] = s2 < prm.S ? (double)gs[prm.S * D + s2] : 0.0;
+      __syncthreads();
+      for (int e = tid; e < SP * D; e += NTHR) put_bs(e / D, e % D, bsf[e]);
+      auto tile_t0 = [&](int j) { return it.t0 + (int64_t)(it.ntiles - 1 - j) * TT; };
+      auto load_v = [&](int j) {   // v and the projections of walk step j
+        if (failed) return;
+        inflight |= 1u;
+        if (tid == 0) {
+          const int64_t t0 = tile_t0(j);
+          float* pj = sm + LY::PJX;
+          fence_async_smem();
+          bar_expect_tx(full, (uint32_t)(Box<T, D>::BYTES + 2 * TT * PJ * 4));
+          tma_load3(pj, &maps.map[0], 0, (int)t0, n, full);
+          tma_load3(pj + TT * PJ, &maps.map[1], 0, (int)t0, n, full);
+          tma_rows5<T, D>(&maps.map[2], sm + LY::VX, prm.lv, prm, n, t0, full);
+        }
+      };
+      auto load_do = [&](int j) {
+        if (failed) return;
+        inflight |= 2u;
+        if (tid == 0) {
+          fence_async_smem();
+          bar_expect_tx(full + 1, (uint32_t)Box<T, D>::BYTES);
+          tma_rows5<T, D>(&maps.map[3], sm + LY::GX, prm.ldo, prm, n, tile_t0(j), full + 1);
+        }
+      };
+      load_v(0);
+      load_do(0);
+      for (int i = 0; i < it.ntiles; ++i) {
+        const int64_t tile0 = tile_t0(i);
+        float* VXt = sm + LY::VX;
+        float* GXt = sm + LY::GX;
+        const float* pj = sm + LY::PJX;
+        if (tid < SP) a0t[tid] = prm.range_mass[((size_t)n * tiles_n + tile0 / TT) * SP + tid];
+        T5_WAIT(full, phF & 1);
+        if (!failed) {
+          phF ^= 1u;
+          inflight &= ~1u;
+        }
+        T5_WAIT(full + 1, (phF >> 1) & 1);
+        if (!failed) {
+          phF ^= 2u;
+          inflight &= ~2u;
+        }
+        const int64_t t = tile0 + row;
+        const bool valid = t < it.t1;
+        float pkv[MYG][G::GB], hk[MYG][G::GK], asf[MYG][G::GB], wv[MYG][G::GB];
+        {
+          float y[W], g[W];
+          read_cols<T, D, W>(VXt, row, sub * W, y);
+          read_cols<T, D, W>(GXt, row, sub * W, g);
+          float pq[MYG][G::GB], al[MYG][G::GB];
+#pragma unroll
+          for (int a = 0; a < MYG; ++a) {
+            const int gi = sub + a * NTH;
+            if (gi < NG) {
+              float pj_[G::GK], h[G::GK];
+              const bool has = gi * G::GK < PJ;
+#pragma unroll
+              for (int k = 0; k < G::GK; ++k) pj_[k] = has ? pj[row * PJ + gi * G::GK + k] : 0.f;
+              group_probs<K>(pj_, gi * G::GT, has ? L : 0, inv_scale, pq[a], h);
+#pragma unroll
+              for (int k = 0; k < G::GK; ++k)
+                pj_[k] = has ? pj[TT * PJ + row * PJ + gi * G::GK + k] : 0.f;
+              group_probs<K>(pj_, gi * G::GT, has ? L : 0, inv_scale, pkv[a], hk[a]);
+              const float* arow = prm.alpha + ((size_t)n * prm.T + (valid ? t : 0)) * prm.SA;
+#pragma unroll
+              for (int b = 0; b < G::GB; ++b) {
+                const int s2 = gi * G::GB + b;
+                al[a][b] = (valid && s2 < prm.S) ? arow[s2] : 0.f;
+              }
+              if (!valid) {
+#pragma unroll
+                for (int b = 0; b < G::GB; ++b) pq[a][b] = pkv[a][b] = 0.f;
+              }
+            }
+          }
+          __syncthreads();   // raw tiles read, the tile's key mass loaded, scratch free
+          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), nullptr, row,
+                                      sub * W, y);
+          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1), nullptr, row,
+                                      sub * W, g);
+          float incl[MYG][G::GB], rincl[MYG][G::GB];
+#pragma unroll
+          for (int a = 0; a < MYG; ++a) {
+            const int gi = sub + a * NTH;
+            if (gi < NG) {
+#pragma unroll
+              for (int b = 0; b < G::GB; ++b) {
+                float tot;
+                incl[a][b] = warp_scan(pkv[a][b], tot);
+                if (lane == 31) scan[(gi * G::GB + b) * 4 + quad] = tot;
+                // suffix of alpha over the warp's tokens
+                float x = al[a][b];
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                  const float yv = __shfl_down_sync(0xffffffffu, x, o);
+                  if (lane + o < 32) x += yv;
+                }
+                rincl[a][b] = x;
+                const float rt = __shfl_sync(0xffffffffu, x, 0);
+                if (lane == 0) scan2[(gi * G::GB + b) * 4 + quad] = rt;
+              }
+            }
+          }
+          __syncthreads();
+#pragma unroll
+          for (int a = 0; a < MYG; ++a) {
+            const int gi = sub + a * NTH;
+            if (gi < NG) {
+#pragma unroll
+              for (int b = 0; b < G::GB; ++b) {
+                const int s2 = gi * G::GB + b;
+                float before = 0.f, after = 0.f;
+                for (int q2 = 0; q2 < quad; ++q2) before += scan[s2 * 4 + q2];
+                for (int q2 = quad + 1; q2 < 4; ++q2) after += scan2[s2 * 4 + q2];
+                const float A = (float)(a0t[s2] + (double)(before + incl[a][b]));
+                wv[a][b] = pq[a][b] / (A + prm.eps);
+                asf[a][b] = (float)(as[s2] + (double)(after + rincl[a][b]));
+              }
+#pragma unroll
+              for (int c8 = 0; c8 < G::GB / 8; ++c8) {
+                const int c = gi * G::GB / 8 + c8;
+                uint4 hi, lo;
+                split8(pkv[a] + 8 * c8, hi, lo);
+                put_chunk<2 * SP>(pk, row, c, hi);
+                put_chunk<2 * SP>(pk, row, SP / 8 + c, lo);
+                split8(wv[a] + 8 * c8, hi, lo);
+                put_chunk<2 * SP>(wh, row, c, hi);
+                put_chunk<2 * SP>(wh, row, SP / 8 + c, hi);
+                put_chunk<SP>(wl, row, c, lo);
+              }
+            }
+          }
+        }
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          fence_after();
+          bulk_wait_read();   // the previous tile's dv / dk staging sits in MM
+          const bf16* vp[2] = {Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1)};
+          const bf16* gp[2] = {Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1)};
+          // MT[tau][t] = v(tau) . dO(t)
+#pragma unroll
+          for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              if (a + b == 2 || (!F32 && a + b > 0)) continue;
+#pragma unroll
+              for (int ks = 0; ks < D / 16; ++ks)
+                mma(tbase + LY::C_MT, desc<D>(vp[a], ks), desc<D>(gp[b], ks), idesc<TT>(),
+                    a + b > 0 || ks > 0);
+            }
+          // GT[tau][t] = pK(tau) . W(t)
+#pragma unroll
+          for (int ks = 0; ks < 2 * SP / 16; ++ks)
+            mma(tbase + LY::C_GT, desc<2 * SP>(pk, ks), desc<2 * SP>(wh, ks), idesc<TT>(), ks > 0);
+#pragma unroll
+          for (int ks = 0; ks < SP / 16; ++ks)
+            mma(tbase + LY::C_GT, desc<2 * SP>(pk, ks), desc<SP>(wl, ks), idesc<TT>(), true);
+          // VB = v . BS^T (BS hi and lo along N)
+#pragma unroll
+          for (int a = 0; a < (F32 ? 2 : 1); ++a)
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks)
+              mma(tbase + LY::C_VB, desc<D>(vp[a], ks), desc<D>(bss, ks), idesc<2 * SP>(),
+                  a > 0 || ks > 0);
+          // DV = pK . BS
+#pragma unroll
+          for (int ks = 0; ks < 2 * SP / 16; ++ks)
+            mma(tbase + LY::C_DV, desc<2 * SP>(pk, ks), desc<2 * SP>(bst2, ks), idesc<D>(), ks > 0);
+#pragma unroll
+          for (int ks = 0; ks < SP / 16; ++ks)
+            mma(tbase + LY::C_DV, desc<2 * SP>(pk, ks), desc<SP>(bstl, ks), idesc<D>(), true);
+          // BS[d][s] += dO^T W over the range (block 0: W hi, block 1: W lo)
+#pragma unroll
+          for (int a = 0; a < (F32 ? 2 : 1); ++a)
+#pragma unroll
+            for (int ks = 0; ks < TT / 16; ++ks) {
+              mma(tbase + LY::C_BS, desc_mn<D>(gp[a], ks), desc_mn<2 * SP>(wh, ks), idesc64_mn<SP>(),
+                  i > 0 || a > 0 || ks > 0);
+              if (a == 0)
+                mma(tbase + LY::C_BS + SP, desc_mn<D>(gp[a], ks), desc_mn<SP>(wl, ks),
+                    idesc64_mn<SP>(), i > 0 || ks > 0);
+            }
+          { commit(barA); ++issA; }
+        }
+        // the tile's alpha moves the suffix on (every thread has read `as`)
+        if (sub == 0 && tid < SP) {
+          float tot = 0.f;
+          for (int q2 = 0; q2 < 4; ++q2) tot += scan2[tid * 4 + q2];
+          as[tid] += (double)tot;
+        }
+        T5_WAIT(barA, phA);
+        phA ^= 1;
+        // v and the projections are consumed: the next walk step's
+        if (i + 1 < it.ntiles) load_v(i + 1);
+        fence_after();
+        // masked MT rows (t >= tau kept)
+#pragma unroll
+        for (int c0 = 0; c0 < GC; c0 += 16) {
+          float g[16];
+          tld16(tlane + LY::C_MT + GC * sub + c0, g);
+          tld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (GC * sub + c0 + e < row) g[e] = 0.f;
+#pragma unroll
+          for (int c8 = 0; c8 < 2; ++c8) {
+            uint4 hi, lo;
+            split8(g + 8 * c8, hi, lo);
+            const int c = (GC * sub + c0) / 8 + c8;
+            put_chunk<TT>(mm_hi, row, c, hi);
+            put_chunk<TT>(mm_lo, row, c, lo);
+          }
+        }
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          fence_after();
+          // VB += mask'(MT) . W  (block 0: W hi, block 1: W lo; lo.lo dropped)
+#pragma unroll
+          for (int a = 0; a < 2; ++a) {
+            const bf16* mp = a ? mm_lo : mm_hi;
+#pragma unroll
+            for (int ks = 0; ks < TT / 16; ++ks) {
+              mma(tbase + LY::C_VB, desc<TT>(mp, ks), desc_mn<2 * SP>(wh, ks), idesc_bmn<SP>(), true);
+              if (a == 0)
+                mma(tbase + LY::C_VB + SP, desc<TT>(mp, ks), desc_mn<SP>(wl, ks), idesc_bmn<SP>(),
+                    true);
+            }
+          }
+          { commit(barB); ++issB; }
+        }
+        T5_WAIT(barB, phB);
+        phB ^= 1;
+        fence_after();
+        // masked GT rows into the (consumed) masked-matrix area
+#pragma unroll
+        for (int c0 = 0; c0 < GC; c0 += 16) {
+          float g[16];
+          tld16(tlane + LY::C_GT + GC * sub + c0, g);
+          tld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (GC * sub + c0 + e < row) g[e] = 0.f;
+#pragma unroll
+          for (int c8 = 0; c8 < 2; ++c8) {
+            uint4 hi, lo;
+            split8(g + 8 * c8, hi, lo);
+            const int c = (GC * sub + c0) / 8 + c8;
+            put_chunk<TT>(mm_hi, row, c, hi);
+            put_chunk<TT>(mm_lo, row, c, lo);
+          }
+        }
+        // dpK and the hash backward of the keys
+#pragma unroll 1
+        for (int a = 0; a < MYG; ++a) {
+          const int gi = sub + a * NTH;
+          if (gi < NG) {
+            float vb[G::GB], dpk[G::GB], dj_[G::GK];
+            tld_sum<G::GB, 2>(tlane + LY::C_VB + gi * G::GB, SP, vb);
+#pragma unroll
+            for (int b = 0; b < G::GB; ++b) dpk[b] = valid ? asf[a][b] + vb[b] : 0.f;
+            float dsl = 0.f;
+            group_probs_bwd<K>(pkv[a], dpk, hk[a], inv_scale, dj_, dsl);
+            if (valid) ds += dsl;
+            if (gi * G::GK < PJ) {
+#pragma unroll
+              for (int j = 0; j < G::GK; ++j) {
+                const int jj = gi * G::GK + j;
+                if (jj < PJ) {
+                  const float x = valid ? dj_[j] : 0.f;
+                  const bf16 hb = __float2bfloat16_rn(x);
+                  dj[elem<PJ>(row, jj)] = hb;
+                  dj[TT * PJ + elem<PJ>(row, jj)] = __float2bfloat16_rn(x - __bfloat162float(hb));
+                }
+              }
+            }
+          }
+        }
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          fence_after();
+          const bf16* gp[2] = {Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1)};
+          // DV += mask'(GT) . dO
+#pragma unroll
+          for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              if (a + b == 2 || (!F32 && b == 1)) continue;
+              const bf16* mp = a ? mm_lo : mm_hi;
+#pragma unroll
+              for (int ks = 0; ks < TT / 16; ++ks)
+                mma(tbase + LY::C_DV, desc<TT>(mp, ks), desc_mn<D>(gp[b], ks), idesc_bmn<D>(), true);
+            }
+          // DK = dproj . P (into the consumed MT columns)
+          gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DK, dj, dj + TT * PJ, nullptr, 2, pt,
+                                            false);
+          { commit(barA); ++issA; }
+        }
+        T5_WAIT(barA, phA);
+        phA ^= 1;
+        if (i + 1 < it.ntiles) load_do(i + 1);
+        fence_after();
+        {
+          float o[W];
+          tld_sum<W, 1>(tlane + LY::C_DV + sub * W, 0, o);
+          put_tile_cols<T, D, W>(sm + LY::MM, row, sub * W, o);
+          tld_sum<W>(tlane + LY::C_DK + sub * W, D, o);
+          put_tile_cols<T, D, W>(sm + LY::MM + TT * D, row, sub * W, o);
+        }
+        // BS operands of the next (earlier) tile: range-end suffix + the
+        // tiles walked so far (M = 64 lanes: row d = 16 q + l)
+        if (i + 1 < it.ntiles && sub == 0) {
+          const int d = 16 * quad + lane;
+          float bsv[2 * SP];
+#pragma unroll
+          for (int c = 0; c < 2 * SP; c += 8) tld8(tlane + LY::C_BS + c, bsv + c);
+          tld_wait();
+          if (lane < 16 && d < D) {
+            for (int s2 = 0; s2 < SP; ++s2) put_bs(s2, d, bsf[s2 * D + d] + bsv[s2] + bsv[SP + s2]);
+          }
+        }
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (tid == 0 && !failed) {
+          tma_store_tile<T, D>(&maps.map[6], sm + LY::MM, prm.ldv, prm, n, tile0);
+          tma_store_tile<T, D>(&maps.map[5], sm + LY::MM + TT * D, prm.ldk, prm, n, tile0);
+          bulk_commit();
+        }
+        if (T5_VOTE()) break;
+      }
+    }
+    float x = ds;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    __syncthreads();
+    if ((tid & 31) == 0) sm[LY::RED + warp] = x;
+    __syncthreads();
+    if (tid == 0) {
+      float tot = 0.f;
+      for (int i = 0; i < NTHR / 32; ++i) tot += sm[LY::RED + i];
+      prm.dscale_part[(size_t)n * prm.P + it.part] = tot;
+    }
+  }
+  T5_EPILOGUE
+}
+
+#undef T5_WAIT
+#undef T5_VOTE
+#undef T5_PROLOGUE
+#undef T5_EPILOGUE
+
+}  // namespace c5
+}  // namespace race

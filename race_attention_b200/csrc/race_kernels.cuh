@@ -64,16 +64,21 @@ struct Params {
   int global_norm;       // causal: 1 = one denominator per token summed over all buckets
   float* den_out;        // causal global: [N][T] denominators (optional)
   const float* dden_in;  // causal global: [N][T] incoming gradient of den (optional)
+  float* projq;          // causal: fp32 projections of q onto the planes [N][T][16]
+  float* projk;          // causal: fp32 projections of k [N][T][16]
+  int SA;                // causal: floats per token of alpha ([N][T][SA], S rounded up to 4)
+  double* range_mass;    // causal: key mass at the start of every tile [N][tiles][SP] (float64)
 };
 
 __host__ __device__ constexpr int round_up(int a, int b) { return (a + b - 1) / b * b; }
 
 // TMA descriptors of a kernel's streamed inputs and outputs (encoded per call
 // on the host; a __grid_constant__ kernel parameter).  Each maps a
-// [M, B, T, H, D] tensor as 5-D (D, T, H, B, M) with 128-row boxes; maps 0-1
-// are inputs, 2-3 outputs.
+// [M, B, T, H, D] tensor as 5-D (D, T, H, B, M) with 128-row boxes, or a
+// [N][T][C] float32 array as 3-D (C, T, N); which map holds which tensor is
+// fixed per kernel.
 struct TmaMaps {
-  CUtensorMap map[4];
+  CUtensorMap map[8];
 };
 
 // ---------------------------------------------------------------- row I/O

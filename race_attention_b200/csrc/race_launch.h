@@ -16,6 +16,10 @@ enum KernelId {
   K_C_TOTALS,          // causal range totals: mma.sync reduce over 32-token tiles
   K_NC_BWD_Q_SYNC,
   K_NC_BWD_KV_SYNC,
+  K_C5_PROJ,           // causal: fp32 projections of q or k (pre-pass)
+  K_C5_FWD,            // causal: chunkwise tcgen05 forward readout
+  K_C5_BWD_Q,          // causal: chunkwise tcgen05 query backward
+  K_C5_BWD_KV,         // causal: chunkwise tcgen05 key/value backward (reverse walk)
   K_COUNT
 };
 

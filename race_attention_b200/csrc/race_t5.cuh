@@ -1527,10 +1527,8 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
   T5_EPILOGUE
 }
 
-#undef T5_WAIT
-#undef T5_VOTE
-#undef T5_PROLOGUE
-#undef T5_EPILOGUE
+// T5_WAIT, T5_VOTE, T5_PROLOGUE and T5_EPILOGUE stay defined for the causal
+// kernels of race_causal5.cuh, which undefines them.
 
 }  // namespace t5
 }  // namespace race

@@ -168,6 +168,10 @@ class _RaceFunction(torch.autograd.Function):
         ctx.in_dtypes = (q.dtype, k.dtype, v.dtype)
         dtype = q.dtype if q.dtype in _SUPPORTED else torch.float32
         q, k, v = (_prep(t, dtype) for t in (q, k, v))
+        if causal and normalize == 0 and not _mappable(q, k, v):
+            # the per-bucket causal kernels stream every input through the copy
+            # engine, which cannot walk a broadcast axis: materialise it
+            q, k, v = (t if _mappable(t) else t.contiguous() for t in (q, k, v))
         planes = planes.detach().to(torch.float32).contiguous()
         scale_d = scale.detach().to(torch.float32).reshape(()).contiguous()
         flags = _lib.RACE_FLAG_STRICT_TMA if _mappable(q, k, v) else 0

@@ -55,13 +55,18 @@ def test_query_sizes(lib):
     assert sz.workspace_bytes > 0
     assert lib.race_query(desc(causal=1, tokens=1000, chunk=128, normalize=1), sz) == 0
     assert lib.race_query(desc(causal=1, tokens=1000, chunk=128), sz) == 0
-    # causal: one prefix slot per token range (32-token tiles), then alpha and
-    # the float64 key mass of every tile behind the gradient slots
-    assert sz.chunk == 32 and 1 <= sz.num_chunks <= 8
+    # causal (per-bucket): one prefix slot per token range of whole 128-token
+    # tiles, then the fp32 projections of q and k ([N][T][16] each); behind the
+    # gradient slots alpha [N][T][S rounded to 4] and the float64 key mass at
+    # every tile start [N][tiles][SP]
+    assert 1 <= sz.num_chunks <= 8
     slots = N * sz.num_chunks * sz.slot_floats
-    assert sz.state_bytes == slots * 4
-    tiles = (1000 + 31) // 32
-    assert sz.gstate_bytes == (slots + N * 1000 * S + 2 * N * tiles * 24 + 2) * 4
+    up = lambda x: (x + 63) // 64 * 64
+    assert sz.state_bytes == (up(slots) + 2 * N * 1000 * 16) * 4
+    tiles = (1000 + 127) // 128
+    alpha_off = up(slots)
+    mass_off = up(alpha_off + N * 1000 * 20)
+    assert sz.gstate_bytes == (mass_off + 2 * N * tiles * 32 + 2) * 4
 
 
 @pytest.mark.parametrize("bad,code", [

@@ -123,6 +123,12 @@ def test_vs_oracle(N, T, d, K, L, causal, chunk, dtype):
     # is a near-total cancellation, as at T = 1 -- to the bar relative to the
     # sum of the magnitudes of the terms it adds up
     bar = max(tol, 4 * floors[4])
+    if T == 1:
+        # one token: E = v exactly up to eps, so dpQ and dpK cancel to zero in
+        # exact arithmetic and the temperature gradient is an eps-sized
+        # remainder of that cancellation; held to 16x the reference's own
+        # float32 error on it
+        bar = max(tol, 16 * floors[4])
     assert math.isclose(got[4], ds, rel_tol=bar, abs_tol=tol * ds_mag), (got[4], ds, bar, ds_mag)
 
 
@@ -154,8 +160,10 @@ def test_chunk_length_independent():
 def test_broadcast_batch_layout(causal):
     """A batch axis broadcast with stride 0 (one sequence shared by two batch
     rows) cannot be walked by the copy engine's tensor maps; the library then
-    runs the warp-level kernels.  Results must match two explicit copies (run
-    by the tcgen05 kernels) within the path's fp32 bar of 1e-4."""
+    runs the warp-level kernels (non-causal), or the autograd layer
+    materialises the broadcast (per-bucket causal, whose kernels stream every
+    input by TMA).  Results must match two explicit copies within the path's
+    fp32 bar of 1e-4."""
     from race_attention_b200 import race_attention
     dev = "cuda"
     g = torch.Generator().manual_seed(5)
