@@ -32,8 +32,10 @@
  *                all ranks after the caller's all-reduce);
  *               gstate = N slots of dE = sum_t pQ(t) dO(t).
  *   causal:     state  = N * num_chunks slots holding the EXCLUSIVE prefix at
- *                the start of every chunk; gstate = N * num_chunks gradient
- *                slots (exclusive suffix sums) followed by per-token alpha.
+ *                the start of every chunk (a range of whole 128-token tiles),
+ *                then the fp32 projections of q and k onto the planes;
+ *                gstate = N * num_chunks gradient slots (exclusive suffix
+ *                sums), then per-token alpha and per-tile key masses.
  *
  * Single GPU: race_forward() then race_backward().  Sequence-sharded multi-GPU
  * (each rank holds a contiguous token range of every stream): the split entry
@@ -105,7 +107,8 @@ typedef struct {
   int32_t batch;          /* B                                                   */
   int32_t heads;          /* H                                                   */
   int64_t tokens;         /* T held by this rank                                 */
-  int32_t chunk;          /* causal chunk length, 0 = chosen by the library      */
+  int32_t chunk;          /* accepted and ignored (the causal kernels use
+                             128-token tiles and choose the ranges)           */
   int32_t shared_planes;  /* 1: planes [1][L*K][d]; 0: planes [M][L*K][d]        */
   float eps;              /* added to the bucket mass (reference: 1e-6); GLOBAL:
                              the floor of the per-token denominator             */
@@ -122,7 +125,7 @@ typedef struct {
   size_t workspace_bytes;  /* scratch, contents not preserved between calls     */
   size_t total_bytes;      /* one [N] slot array (causal rank totals/offsets)   */
   int32_t slot_floats;     /* floats per state slot                             */
-  int32_t chunk;           /* causal chunk length in use                        */
+  int32_t chunk;           /* causal tile length (128)                          */
   int64_t num_chunks;      /* causal chunks per stream                          */
 } race_sizes_t;
 

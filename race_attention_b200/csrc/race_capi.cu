@@ -276,7 +276,7 @@ struct Plan {
   size_t alpha_off;    // c5: floats of the gradient state before alpha [N][T][SA]
   size_t mass_off;     // c5: floats of the gradient state before the tile key masses
   int SA;              // c5: floats per token of alpha
-  size_t state_floats, gstate_floats, part_floats, dscale_floats, tile_doubles;
+  size_t state_floats, gstate_floats, part_floats, dscale_floats;
   size_t norm_bytes;   // normalize_qk: one normalised [N][T][D] copy (q, then k)
 };
 
@@ -341,31 +341,21 @@ int make_plan(const race_desc_t* d, Plan* p) {
     p->state_floats = (size_t)p->N * p->SS;
     p->gstate_floats = (size_t)p->N * p->SS;
     p->part_floats = (size_t)p->N * p->P * p->SS;
-    p->tile_doubles = 0;
   } else {
-    // state: exclusive prefix slot of every range; gstate: exclusive suffix
-    // slot of every range, then alpha [N][T][S], then the float64 key mass at
-    // every 32-token tile start [N][tiles][S8]
-    p->CL = 32;
+    // state: the exclusive prefix slot of every range, then the fp32
+    // projections of q and k ([N][T][16] each); gstate: the exclusive suffix
+    // slot of every range, then alpha [N][T][SA] and the float64 key mass at
+    // every 128-token tile start [N][tiles][SP]
+    p->c5 = true;
+    p->CL = 128;
     p->NC = p->P;
     const size_t slots = (size_t)p->N * p->P;
-    const int64_t tiles = (T + 31) / 32;
-    p->state_floats = slots * p->SS;
-    // per-bucket mode: the forward also keeps the fp32 projections of q and k
-    // ([N][T][16] each) behind the prefix slots
-    p->c5 = d->normalize == RACE_NORM_BUCKET;
-    p->proj_off = (p->state_floats + 63) / 64 * 64;
-    if (p->c5) p->state_floats = p->proj_off + 2 * (size_t)p->N * T * PJW;
-    // per-bucket mode: gradient slots, then alpha [N][T][SA] and the float64
-    // key mass at every 128-token tile start [N][tiles][SP]
+    p->proj_off = (slots * p->SS + 63) / 64 * 64;
+    p->state_floats = p->proj_off + 2 * (size_t)p->N * T * PJW;
     p->SA = round_up(S, 4);
-    p->alpha_off = ((size_t)p->N * p->P * p->SS + 63) / 64 * 64;
+    p->alpha_off = (slots * p->SS + 63) / 64 * 64;
     p->mass_off = (p->alpha_off + (size_t)p->N * T * p->SA + 63) / 64 * 64;
-    p->tile_doubles = (size_t)p->N * tiles * round_up(S, 8);
-    p->gstate_floats = slots * p->SS + (size_t)p->N * T * S + 2 * p->tile_doubles + 2;
-    if (p->c5)
-      p->gstate_floats =
-          p->mass_off + 2 * (size_t)p->N * ((T + 127) / 128) * round_up(p->spad, 16) + 2;
+    p->gstate_floats = p->mass_off + 2 * (size_t)p->N * ((T + 127) / 128) * round_up(p->spad, 16) + 2;
     p->part_floats = 0;
   }
   return RACE_OK;
@@ -550,11 +540,8 @@ const char* kernel_name(KernelId id) {
     case K_NC_READOUT: return "t5_readout";
     case K_NC_BWD_Q: return "t5_bwd_q";
     case K_NC_BWD_KV: return "t5_bwd_kv";
-    case K_C_FWD: return "ctc_fwd";
-    case K_C_BWD_Q: return "ctc_bwd_q";
-    case K_C_BWD_KV: return "ctc_bwd_kv";
     case K_NC_READOUT_SYNC: return "tc_readout";
-    case K_C_TOTALS: return "tc_reduce";
+    case K_NC_REDUCE_SYNC: return "tc_reduce";
     case K_NC_BWD_Q_SYNC: return "tc_bwd_q";
     case K_NC_BWD_KV_SYNC: return "tc_bwd_kv";
     case K_C5_PROJ: return "c5_proj";
@@ -604,6 +591,9 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
     else if (id == K_NC_REDUCE)
       ok_map = encode_map(&maps.map[0], prm.k, prm.lk, d->dtype, prm, hd, "k", why, wl) &&
                encode_map(&maps.map[1], prm.v, prm.lv, d->dtype, prm, hd, "v", why, wl);
+    else if (id == K_C5_PROJ)
+      ok_map = encode_map(&maps.map[0], prm.q, prm.lq, d->dtype, prm, hd, "x", why, wl) &&
+               encode_map3(&maps.map[1], prm.projq, prm.N, prm.T, PJW, "proj", why, wl);
     else if (id == K_C5_BWD_Q)
       ok_map = encode_map3(&maps.map[0], prm.projq, prm.N, prm.T, PJW, "projq", why, wl) &&
                encode_map3(&maps.map[1], prm.projk, prm.N, prm.T, PJW, "projk", why, wl) &&
@@ -626,7 +616,7 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
     if (!ok_map) {   // layouts the copy engine cannot walk: warp-level kernels
       char note[220];
       std::snprintf(note, sizeof(note), "fallback: %s", why);
-      if (c.strict || c.plan.S > 32 || id == K_C5_FWD || id == K_C5_BWD_Q || id == K_C5_BWD_KV) {
+      if (c.strict || c.plan.S > 32 || id >= K_C5_PROJ) {
         log_kernel(kernel_name(id), note);
         std::snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", kernel_name(id), why);
         return RACE_ERR_UNSUPPORTED;
@@ -634,7 +624,7 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
       const KernelId alt = id == K_NC_READOUT  ? K_NC_READOUT_SYNC
                            : id == K_NC_BWD_KV ? K_NC_BWD_KV_SYNC
                            : id == K_NC_BWD_Q  ? K_NC_BWD_Q_SYNC
-                                               : K_C_TOTALS;
+                                               : K_NC_REDUCE_SYNC;
       return launch(d, c, alt, stream, note);
     }
   }
@@ -651,26 +641,12 @@ int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream
 }
 
 // causal pre-pass: fp32 projections of x (q or k) into proj [N][T][16]
-int launch_proj(const race_desc_t* d, const Call& c, const race_tensor_t& x, float* proj,
+int launch_proj(const race_desc_t* d, Call& c, const race_tensor_t& x, float* proj,
                 cudaStream_t stream) {
-  KernelInfo ki;
-  const int K = d->num_bits, sp = c.plan.spad;
-  bool ok;
-  if (d->dtype == RACE_F32)
-    ok = d->head_dim == 32 ? kernels_f32_d32(sp, K, K_C5_PROJ, &ki) : kernels_f32_d64(sp, K, K_C5_PROJ, &ki);
-  else
-    ok = d->head_dim == 32 ? kernels_bf16_d32(sp, K, K_C5_PROJ, &ki) : kernels_bf16_d64(sp, K, K_C5_PROJ, &ki);
-  if (!ok) return RACE_ERR_UNSUPPORTED;
-  Params prm = c.prm;
-  const void* xp = x.data;
-  Layout lx;
-  fill_layout(lx, x);
-  void* args[] = {&prm, &xp, &lx, &proj};
-  const dim3 grid((unsigned)((d->tokens + ki.threads - 1) / ki.threads), (unsigned)c.plan.N);
-  const cudaError_t e = cudaLaunchKernel(ki.fn, grid, dim3(ki.threads), args, 0, stream);
-  if (e != cudaSuccess) return cuda_fail(e);
-  log_kernel("c5_proj");
-  return RACE_OK;
+  c.prm.q = x.data;
+  fill_layout(c.prm.lq, x);
+  c.prm.projq = proj;
+  return launch(d, c, K_C5_PROJ, stream);
 }
 
 int post(cudaStream_t) {
@@ -709,14 +685,6 @@ void c5_pointers(Call& c, const float* state, const float* gstate, int64_t T) {
   c.prm.alpha = gs + c.plan.alpha_off;
   c.prm.range_mass = reinterpret_cast<double*>(gs + c.plan.mass_off);
   c.prm.SA = c.plan.SA;
-}
-
-// alpha and the per-tile key mass live behind the gradient slots
-void causal_scratch(Call& c, float* gstate) {
-  const size_t slot_floats = (size_t)c.plan.N * c.plan.P * c.plan.SS;
-  c.prm.alpha = gstate + slot_floats;
-  const size_t off = slot_floats + (size_t)c.plan.N * c.prm.T * c.prm.S;
-  c.prm.tilemass = reinterpret_cast<double*>(gstate + ((off + 1) & ~size_t(1)));
 }
 
 int zero_fill(void* p, size_t bytes, cudaStream_t stream) {
@@ -949,18 +917,13 @@ int race_forward_reduce(const race_desc_t* desc, race_tensor_t k, race_tensor_t 
                                             cudaMemcpyDeviceToDevice, stream);
       if (e != cudaSuccess) return cuda_fail(e);
     }
-  } else if (c.plan.c5) {
+  } else {
     // the key projections (kept for the readout and the backward), the range
     // totals straight into the state slots, then the exclusive scan
     float* projk = state + c.plan.proj_off + (size_t)c.plan.N * desc->tokens * PJW;
     RACE_TRY(launch_proj(desc, c, k, projk, stream));
     c.prm.part = state;
     RACE_TRY(launch(desc, c, K_NC_REDUCE, stream));
-    RACE_TRY(chunk_scan(c, state, 0, total, stream));
-  } else {
-    // range totals straight into the state slots, then the exclusive scan
-    c.prm.part = state;
-    RACE_TRY(launch(desc, c, K_C_TOTALS, stream));
     RACE_TRY(chunk_scan(c, state, 0, total, stream));
   }
   return RACE_OK;
@@ -995,15 +958,11 @@ int race_forward_readout_ex(const race_desc_t* desc, race_tensor_t q, race_tenso
     fill_layout(c.prm.lv, v);
     c.prm.k = k.data;
     c.prm.v = v.data;
-    if (c.plan.c5) {
-      float* projq = const_cast<float*>(state) + c.plan.proj_off;
-      RACE_TRY(launch_proj(desc, c, q, projq, stream));
-      c.prm.projq = projq;
-      c.prm.projk = projq + (size_t)c.plan.N * desc->tokens * PJW;
-      RACE_TRY(launch(desc, c, K_C5_FWD, stream));
-    } else {
-      RACE_TRY(launch(desc, c, K_C_FWD, stream));
-    }
+    float* projq = state + c.plan.proj_off;
+    RACE_TRY(launch_proj(desc, c, q, projq, stream));
+    c.prm.projq = projq;
+    c.prm.projk = projq + (size_t)c.plan.N * desc->tokens * PJW;
+    RACE_TRY(launch(desc, c, K_C5_FWD, stream));
   }
   return RACE_OK;
 }
@@ -1074,26 +1033,13 @@ int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k
       if (e != cudaSuccess) return cuda_fail(e);
     }
     RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 0, stream));
-  } else if (c.plan.c5) {
+  } else {
     RACE_TRY(check_tensor(desc, v));
     fill_layout(c.prm.lv, v);
     c.prm.v = v.data;
     c.prm.gstate_out = gstate;
     c5_pointers(c, state, gstate, desc->tokens);
     RACE_TRY(launch(desc, c, K_C5_BWD_Q, stream));
-    RACE_TRY(chunk_scan(c, gstate, 1, total, stream));
-    RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 0, stream));
-  } else {
-    RACE_TRY(check_tensor(desc, k));
-    RACE_TRY(check_tensor(desc, v));
-    if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &k, c.norm_k, stream));
-    fill_layout(c.prm.lk, k);
-    fill_layout(c.prm.lv, v);
-    c.prm.k = k.data;
-    c.prm.v = v.data;
-    c.prm.gstate_out = gstate;
-    causal_scratch(c, gstate);
-    RACE_TRY(launch(desc, c, K_C_BWD_Q, stream));
     RACE_TRY(chunk_scan(c, gstate, 1, total, stream));
     RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 0, stream));
   }
@@ -1138,23 +1084,12 @@ int race_backward_kv(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
   if (!desc->causal) {
     RACE_TRY(launch(desc, c, K_NC_BWD_KV, stream));
     RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 1, stream));
-  } else if (c.plan.c5) {
+  } else {
     RACE_TRY(check_tensor(desc, dout));
     fill_layout(c.prm.ldo, dout);
     c.prm.dout = dout.data;
     c5_pointers(c, state, gstate, desc->tokens);
     RACE_TRY(launch(desc, c, K_C5_BWD_KV, stream));
-    RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 1, stream));
-  } else {
-    RACE_TRY(check_tensor(desc, q));
-    RACE_TRY(check_tensor(desc, dout));
-    if (c.normalize_qk) RACE_TRY(normalize_into(desc, c, &q, c.norm_q, stream));
-    fill_layout(c.prm.lq, q);
-    fill_layout(c.prm.ldo, dout);
-    c.prm.q = q.data;
-    c.prm.dout = dout.data;
-    causal_scratch(c, const_cast<float*>(gstate));
-    RACE_TRY(launch(desc, c, K_C_BWD_KV, stream));
     RACE_TRY(dscale_final(c, c.plan.N * c.plan.P, dscale, 1, stream));
   }
   if (c.normalize_qk) RACE_TRY(normalize_backward(desc, c, k_in, dk, stream));

@@ -35,64 +35,6 @@ namespace c5 {
 
 using namespace t5;
 
-// ------------------------------------------------------------------ pre-pass
-// proj[n][t][j] = x[n][t] . planes[m][j] (j < L K; columns up to 16 are zero),
-// float32 FMAs, one thread per token, the stream's planes in shared memory.
-constexpr int kProjThreads = 128;
-
-template <typename T, int D>
-__global__ void __launch_bounds__(kProjThreads) k_c5_proj(const Params prm, const void* x,
-                                                         Layout lx, float* __restrict__ proj) {
-  __shared__ __align__(16) float pl[PJ * D];
-  const int n = blockIdx.y;
-  const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
-  const float* src = prm.planes + (size_t)m * prm.LK * D;
-  for (int i = threadIdx.x; i < PJ * D; i += kProjThreads) pl[i] = i < prm.LK * D ? src[i] : 0.f;
-  __syncthreads();
-  const int64_t t = (int64_t)blockIdx.x * kProjThreads + threadIdx.x;
-  if (t >= prm.T) return;
-  const T* row = static_cast<const T*>(x) + stream_offset(lx, n, prm.B, prm.H) + t * lx.st;
-  float xv[D];
-  if constexpr (sizeof(T) == 4) {
-#pragma unroll
-    for (int i = 0; i < D / 4; ++i) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(row) + i);
-      xv[4 * i] = v.x; xv[4 * i + 1] = v.y; xv[4 * i + 2] = v.z; xv[4 * i + 3] = v.w;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(row) + i);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        xv[8 * i + 2 * j] = f.x;
-        xv[8 * i + 2 * j + 1] = f.y;
-      }
-    }
-  }
-  float out[PJ];
-#pragma unroll
-  for (int j = 0; j < PJ; ++j) {
-    const float4* p4 = reinterpret_cast<const float4*>(pl + j * D);
-    float a = 0.f;
-#pragma unroll
-    for (int i = 0; i < D / 4; ++i) {
-      const float4 w = p4[i];
-      a = fmaf(xv[4 * i], w.x, a);
-      a = fmaf(xv[4 * i + 1], w.y, a);
-      a = fmaf(xv[4 * i + 2], w.z, a);
-      a = fmaf(xv[4 * i + 3], w.w, a);
-    }
-    out[j] = a;
-  }
-  float4* dst = reinterpret_cast<float4*>(proj + ((size_t)n * prm.T + t) * PJ);
-#pragma unroll
-  for (int i = 0; i < PJ / 4; ++i)
-    dst[i] = make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
-}
-
 // ------------------------------------------------------------------ TMA, 3-D
 // [N][T][C] float32 arrays (projections, alpha) are mapped as (C, T, N) with
 // 128-row boxes of whole rows (C * 4 bytes, a multiple of 16, no swizzle).
@@ -161,6 +103,126 @@ __device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
   split2(v[6], v[7], hi.w, lo.w);
 }
 
+// ------------------------------------------------------------------ projections
+// proj[n][t][j] = x[n][t] . planes[m][j] (j < L K; columns up to 16 are zero)
+// for one of q or k: the soft hash of every causal kernel reads these, so q and
+// k are read once.  128-token tiles land by TMA, are split into three bf16
+// parts (24 significant bits: fp32 accuracy, which the temperature gradient's
+// cancelling sum needs) and multiplied on the tensor core by the planes' three
+// parts (all nine cross products, N = 3 x 16); the fp32 rows leave by a TMA
+// store.  Persistent, two CTAs per SM, the next tile loading while this one
+// is converted.
+template <int D>
+struct ProjLay {
+  static constexpr int NTH = 1;
+  static constexpr int NFULL = 2;
+  static constexpr int XS = 0;                             // [2] slots: landed, then 3 parts
+  static constexpr int PS = XS + 2 * Slot<D, 3>::FLOATS;   // bf16 [3 PJ x D] planes (hi; mid; lo)
+  static constexpr int STG = PS + 3 * PJ * D / 2;          // fp32 [TT][PJ] staging of the store
+  static constexpr int BAR = STG + TT * PJ;
+  static constexpr int FLOATS = BAR + 16 + 256;
+  static constexpr int TCOLS = 64;                         // three PJ-column blocks
+  static_assert(FLOATS * 4 <= 113 * 1024, "two CTAs per SM");
+};
+
+// maps: 0 x (5-D), 1 proj ([N][T][16] float32)
+template <typename T, int D>
+__global__ void __launch_bounds__(TT, 2) k_c5_proj(const Params prm, const __grid_constant__ TmaMaps maps) {
+  using LY = ProjLay<D>;
+  constexpr bool F32 = sizeof(T) == 4;
+  T5_PROLOGUE
+  (void)cur_n;
+  (void)L;
+  (void)inv_scale;
+  (void)sub;
+  bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
+  float* stg = sm + LY::STG;
+  for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
+    const Item it = item_of(prm, w);
+    if (it.ntiles <= 0) continue;
+    const int n = it.n;
+    const int m = prm.Mp == 1 ? 0 : n / (prm.B * prm.H);
+    __syncthreads();
+    if (m != cur_m) {
+      const float* pl = prm.planes + (size_t)m * prm.LK * D;
+      put_stack<PJ, D, 3, TT>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+      cur_m = m;
+    }
+    auto load = [&](int j) {
+      if (failed) return;
+      const int f = j & 1;
+      inflight |= 1u << f;
+      if (tid == 0) {
+        fence_async_smem();
+        bar_expect_tx(full + f, (uint32_t)Box<T, D>::BYTES);
+        tma_rows5<T, D>(&maps.map[0], sm + LY::XS + f * Slot<D, 3>::FLOATS, prm.lq, prm, n,
+                        it.t0 + (int64_t)j * TT, full + f);
+      }
+    };
+    load(0);
+    for (int i = 0; i < it.ntiles; ++i) {
+      const int64_t tile0 = it.t0 + (int64_t)i * TT;
+      const int f = i & 1;
+      float* X = sm + LY::XS + f * Slot<D, 3>::FLOATS;
+      if (i + 1 < it.ntiles) load(i + 1);
+      T5_WAIT(full + f, (phF >> f) & 1);
+      if (!failed) {
+        phF ^= 1u << f;
+        inflight &= ~(1u << f);
+      }
+      {
+        float x[D];
+        read_cols<T, D, D>(X, row, 0, x);
+        __syncthreads();
+        put_cols<D, D, F32 ? 3 : 1>(Slot<D, 3>::part(X, 0), Slot<D, 3>::part(X, 1),
+                                    Slot<D, 3>::part(X, 2), row, 0, x);
+      }
+      fence_async_smem();
+      fence_before();
+      __syncthreads();
+      if (tid == 0 && !failed) {
+        fence_after();
+        bulk_wait_read();   // the previous tile's store has left the staging rows
+        gemm_parts<PJ, 3, D / 16, D, D>(tbase, Slot<D, 3>::part(X, 0), Slot<D, 3>::part(X, 1),
+                                        Slot<D, 3>::part(X, 2), F32 ? 3 : 1, ps, false);
+        { commit(barA); ++issA; }
+      }
+      T5_WAIT(barA, phA);
+      phA ^= 1;
+      fence_after();
+      {
+        float pr[PJ];
+        tld_sum<PJ, 3>(tlane, PJ, pr);
+        float4* dst = reinterpret_cast<float4*>(stg + row * PJ);
+#pragma unroll
+        for (int q4 = 0; q4 < PJ / 4; ++q4)
+          dst[q4] = make_float4(pr[4 * q4], pr[4 * q4 + 1], pr[4 * q4 + 2], pr[4 * q4 + 3]);
+      }
+      fence_async_smem();
+      fence_before();
+      __syncthreads();
+      if (tid == 0 && !failed) {
+        tma_store3(&maps.map[1], stg, 0, (int)tile0, n);
+        bulk_commit();
+      }
+      if (T5_VOTE()) break;
+    }
+  }
+  T5_EPILOGUE
+}
+
+// Sum of one value over the NTH threads (row, sub) of each token, in a fixed
+// order, through shared memory (the threads of a token sit in different warps).
+template <int NTH>
+__device__ __forceinline__ float token_sum(float x, float* xs, int row, int sub) {
+  xs[sub * TT + row] = x;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int k = 0; k < NTH; ++k) t += xs[k * TT + row];
+  return t;
+}
+
 // ------------------------------------------------------------------ F2 forward
 template <int D, int SPAD>
 struct FwdLay {
@@ -179,7 +241,8 @@ struct FwdLay {
   static constexpr int B0F = B0 + D * SP;               // fp32 [SP][D] prefix at the range start
   static constexpr int A0 = B0F + SP * D;               // double [SP] key mass at the tile start
   static constexpr int SCAN = A0 + 2 * SP;              // [SP][4] per-warp token totals
-  static constexpr int BAR = SCAN + 4 * SP;
+  static constexpr int DENX = SCAN + 4 * SP;            // [NTH][TT] global mode: den parts
+  static constexpr int BAR = DENX + NTH * TT;
   static constexpr int FLOATS = BAR + 16 + 256;         // + slack for 1 KB alignment
   static constexpr int TCOLS = 256;                     // G [0, 128), OUT [128, 128 + D), ST
   static constexpr int C_G = 0, C_OUT = 128, C_ST = 128 + D;   // ST: M = 64, 2 SP columns
@@ -308,19 +371,36 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
           }
         }
         __syncthreads();
+        // key mass A_s(t); global mode: den(t) = sum_s pQ_s A_s over the token's threads
+        float av[MYG][G::GB], dpart = 0.f;
+#pragma unroll
+        for (int a = 0; a < MYG; ++a) {
+          const int gi = sub + a * NTH;
+          if (gi < NG) {
+#pragma unroll
+            for (int b = 0; b < G::GB; ++b) {
+              const int s = gi * G::GB + b;
+              float before = 0.f;
+              for (int q2 = 0; q2 < quad; ++q2) before += scan[s * 4 + q2];
+              av[a][b] = (float)(a0[s] + (double)(before + incl[a][b]));
+              dpart = fmaf(pq[a][b], av[a][b], dpart);
+            }
+          }
+        }
+        float rden = 0.f;   // global mode: 1 / max(den, eps)
+        if (prm.global_norm) {
+          const float den = token_sum<NTH>(dpart, sm + LY::DENX, row, sub);
+          rden = 1.f / fmaxf(den, prm.eps);
+          if (prm.den_out != nullptr && sub == 0 && valid) prm.den_out[(size_t)n * prm.T + tile0 + row] = den;
+        }
 #pragma unroll
         for (int a = 0; a < MYG; ++a) {
           const int gi = sub + a * NTH;
           if (gi < NG) {
             float wv[G::GB];
 #pragma unroll
-            for (int b = 0; b < G::GB; ++b) {
-              const int s = gi * G::GB + b;
-              float before = 0.f;
-              for (int q2 = 0; q2 < quad; ++q2) before += scan[s * 4 + q2];
-              const float A = (float)(a0[s] + (double)(before + incl[a][b]));
-              wv[b] = pq[a][b] / (A + prm.eps);
-            }
+            for (int b = 0; b < G::GB; ++b)
+              wv[b] = prm.global_norm ? pq[a][b] * rden : pq[a][b] / (av[a][b] + prm.eps);
             // pK (hi | lo), W (hi | hi) and W lo, 8 buckets per chunk
 #pragma unroll
             for (int c8 = 0; c8 < G::GB / 8; ++c8) {
@@ -493,7 +573,8 @@ struct BwdQLayC {
   static constexpr int B0F = PT + D * PJ;               // fp32 [SP][D] prefix at the range start
   static constexpr int A0 = B0F + SP * D;               // double [SP]
   static constexpr int SCAN = A0 + 2 * SP;              // [SP][4]
-  static constexpr int RED = SCAN + 4 * SP;             // [16]
+  static constexpr int DENX = SCAN + 4 * SP;            // [NTH][TT] global mode: row-sum parts
+  static constexpr int RED = DENX + NTH * TT;           // [16]
   static constexpr int BAR = RED + 16;
   static constexpr int FLOATS = BAR + 16 + 256;
   static constexpr int TCOLS = 512;
@@ -588,7 +669,8 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
           inflight &= ~1u;
         }
         const bool valid = tile0 + row < it.t1;
-        float pq[MYG][G::GB], hq[MYG][G::GK], inv[MYG][G::GB], wv[MYG][G::GB];
+        float pq[MYG][G::GB], hq[MYG][G::GK], am[MYG][G::GB], wv[MYG][G::GB];
+        float den = 0.f, rden = 0.f;   // global mode
         {
           float y[W], g[W];
           read_cols<T, D, W>(VXt, row, sub * W, y);
@@ -632,6 +714,7 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
             }
           }
           __syncthreads();
+          float dpart = 0.f;
 #pragma unroll
           for (int a = 0; a < MYG; ++a) {
             const int gi = sub + a * NTH;
@@ -641,10 +724,22 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
                 const int s2 = gi * G::GB + b;
                 float before = 0.f;
                 for (int q2 = 0; q2 < quad; ++q2) before += scan[s2 * 4 + q2];
-                const float A = (float)(a0[s2] + (double)(before + incl[a][b]));
-                inv[a][b] = 1.f / (A + prm.eps);
-                wv[a][b] = pq[a][b] * inv[a][b];
+                am[a][b] = (float)(a0[s2] + (double)(before + incl[a][b]));
+                dpart = fmaf(pq[a][b], am[a][b], dpart);
               }
+            }
+          }
+          if (prm.global_norm) {
+            den = token_sum<NTH>(dpart, sm + LY::DENX, row, sub);
+            rden = 1.f / fmaxf(den, prm.eps);
+          }
+#pragma unroll
+          for (int a = 0; a < MYG; ++a) {
+            const int gi = sub + a * NTH;
+            if (gi < NG) {
+#pragma unroll
+              for (int b = 0; b < G::GB; ++b)
+                wv[a][b] = prm.global_norm ? pq[a][b] * rden : pq[a][b] / (am[a][b] + prm.eps);
 #pragma unroll
               for (int c8 = 0; c8 < G::GB / 8; ++c8) {
                 const int c = gi * G::GB / 8 + c8;
@@ -747,17 +842,40 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
         phB ^= 1;
         fence_after();
         float* stg_a = sm + LY::MM;   // alpha staging [TT][SA] (the masked matrix is consumed)
-#pragma unroll 1
+        // R_s(t) = dO(t) . B_s(t); global mode: dO . out = sum_s W_s R_s over the token
+        float rr[MYG][G::GB], wr = 0.f;
+#pragma unroll
         for (int a = 0; a < MYG; ++a) {
           const int gi = sub + a * NTH;
           if (gi < NG) {
-            float r[G::GB], dpq[G::GB], dj_[G::GK];
-            tld_sum<G::GB, 2>(tlane + LY::C_R + gi * G::GB, SP, r);
-            float al[G::GB];
+            tld_sum<G::GB, 2>(tlane + LY::C_R + gi * G::GB, SP, rr[a]);
+#pragma unroll
+            for (int b = 0; b < G::GB; ++b) wr = fmaf(wv[a][b], rr[a][b], wr);
+          }
+        }
+        // global mode (out = num / max(den, eps), den = sum_s pQ_s A_s):
+        //   gden = -(dO . out) / max(den, eps) (0 where the clamp holds) + d(den) given,
+        //   dpQ_s = R_s / max(den, eps) + A_s gden,  alpha_s = pQ_s gden
+        float gden = 0.f;
+        if (prm.global_norm) {
+          const float dotw = token_sum<NTH>(wr, sm + LY::DENX, row, sub);
+          gden = den >= prm.eps ? -dotw * rden : 0.f;
+          if (prm.dden_in != nullptr && valid) gden += prm.dden_in[(size_t)n * prm.T + tile0 + row];
+        }
+#pragma unroll
+        for (int a = 0; a < MYG; ++a) {
+          const int gi = sub + a * NTH;
+          if (gi < NG) {
+            float dpq[G::GB], dj_[G::GK], al[G::GB];
 #pragma unroll
             for (int b = 0; b < G::GB; ++b) {
-              dpq[b] = valid ? r[b] * inv[a][b] : 0.f;
-              al[b] = -wv[a][b] * dpq[b];
+              if (prm.global_norm) {
+                dpq[b] = valid ? rr[a][b] * rden + am[a][b] * gden : 0.f;
+                al[b] = valid ? pq[a][b] * gden : 0.f;
+              } else {
+                dpq[b] = valid ? rr[a][b] / (am[a][b] + prm.eps) : 0.f;
+                al[b] = -wv[a][b] * dpq[b];
+              }
               asum[a][b] += al[b];
             }
             float dsl = 0.f;
@@ -911,6 +1029,9 @@ struct BwdKVLayC {
   static constexpr int A0T = AS + 2 * SP;               // double [SP] key mass at the tile start
   static constexpr int SCAN = A0T + 2 * SP;             // [SP][4] per-warp key-mass totals
   static constexpr int SCAN2 = SCAN + 4 * SP;           // [SP][4] per-warp alpha totals
+  // [NTH][TT] global mode: den parts, in the projection slot (read before the
+  // scan barrier, reloaded after the first MMA batch)
+  static constexpr int DENX = PJX;
   static constexpr int RED = SCAN2 + 4 * SP;
   static constexpr int BAR = RED + 16;
   static constexpr int FLOATS = BAR + 16 + 256;
@@ -1087,6 +1208,7 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
             }
           }
           __syncthreads();
+          float am[MYG][G::GB], dpart = 0.f;
 #pragma unroll
           for (int a = 0; a < MYG; ++a) {
             const int gi = sub + a * NTH;
@@ -1097,10 +1219,22 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
                 float before = 0.f, after = 0.f;
                 for (int q2 = 0; q2 < quad; ++q2) before += scan[s2 * 4 + q2];
                 for (int q2 = quad + 1; q2 < 4; ++q2) after += scan2[s2 * 4 + q2];
-                const float A = (float)(a0t[s2] + (double)(before + incl[a][b]));
-                wv[a][b] = pq[a][b] / (A + prm.eps);
+                am[a][b] = (float)(a0t[s2] + (double)(before + incl[a][b]));
+                dpart = fmaf(pq[a][b], am[a][b], dpart);
                 asf[a][b] = (float)(as[s2] + (double)(after + rincl[a][b]));
               }
+            }
+          }
+          float rden = 0.f;   // global mode: W_s = pQ_s / max(den, eps)
+          if (prm.global_norm)
+            rden = 1.f / fmaxf(token_sum<NTH>(dpart, sm + LY::DENX, row, sub), prm.eps);
+#pragma unroll
+          for (int a = 0; a < MYG; ++a) {
+            const int gi = sub + a * NTH;
+            if (gi < NG) {
+#pragma unroll
+              for (int b = 0; b < G::GB; ++b)
+                wv[a][b] = prm.global_norm ? pq[a][b] * rden : pq[a][b] / (am[a][b] + prm.eps);
 #pragma unroll
               for (int c8 = 0; c8 < G::GB / 8; ++c8) {
                 const int c = gi * G::GB / 8 + c8;

@@ -1,9 +1,9 @@
 // race_kernels.cuh -- shared definitions of the RACE attention kernels:
 // launch parameters, row I/O helpers and small reductions.  The kernels
 // themselves live in race_t5.cuh (non-causal, tcgen05 + TMA), race_mma.cuh
-// (mma.sync generation: causal range totals and the fallback for layouts the
-// copy engine cannot map) and race_causal_tc.cuh (causal walks);
-// race_tiles.cuh has the shared-memory tile staging they build on.
+// (mma.sync generation: the fallback of the non-causal kernels for layouts the
+// copy engine cannot map) and race_causal5.cuh (causal, tcgen05 + TMA);
+// race_tiles.cuh has the shared-memory tile staging the mma.sync kernels use.
 //
 // Soft hash.  softmax over the 2^K corners of sum_k c_rk u_k factorises:
 //   p_r = prod_k sigmoid(2 c_rk u_k),  u_k = tanh(x . P_k) / scale,
@@ -60,7 +60,6 @@ struct Params {
   int SS;                // floats per slot
   unsigned* err;         // device status word (last 64 bytes of the workspace), 0 = ok
   int wait_polls;        // polls of each bounded wait in the kernels' main loops
-  double* tilemass;      // causal: key mass at every 32-token tile start [N][tiles][S8]
   int global_norm;       // causal: 1 = one denominator per token summed over all buckets
   float* den_out;        // causal global: [N][T] denominators (optional)
   const float* dden_in;  // causal global: [N][T] incoming gradient of den (optional)

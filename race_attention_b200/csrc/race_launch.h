@@ -9,11 +9,8 @@ enum KernelId {
   K_NC_READOUT,
   K_NC_BWD_Q,
   K_NC_BWD_KV,
-  K_C_FWD,
-  K_C_BWD_Q,
-  K_C_BWD_KV,
   K_NC_READOUT_SYNC,   // warp-level mma.sync generation (comparison)
-  K_C_TOTALS,          // causal range totals: mma.sync reduce over 32-token tiles
+  K_NC_REDUCE_SYNC,    // warp-level range totals (fallback of the tcgen05 reduce)
   K_NC_BWD_Q_SYNC,
   K_NC_BWD_KV_SYNC,
   K_C5_PROJ,           // causal: fp32 projections of q or k (pre-pass)

@@ -168,9 +168,9 @@ class _RaceFunction(torch.autograd.Function):
         ctx.in_dtypes = (q.dtype, k.dtype, v.dtype)
         dtype = q.dtype if q.dtype in _SUPPORTED else torch.float32
         q, k, v = (_prep(t, dtype) for t in (q, k, v))
-        if causal and normalize == 0 and not _mappable(q, k, v):
-            # the per-bucket causal kernels stream every input through the copy
-            # engine, which cannot walk a broadcast axis: materialise it
+        if causal and not _mappable(q, k, v):
+            # the causal kernels stream every input through the copy engine,
+            # which cannot walk a broadcast axis: materialise it
             q, k, v = (t if _mappable(t) else t.contiguous() for t in (q, k, v))
         planes = planes.detach().to(torch.float32).contiguous()
         scale_d = scale.detach().to(torch.float32).reshape(()).contiguous()
@@ -267,8 +267,8 @@ def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: to
       causal: per-bucket prefix mean (misc/race.py:108-138) instead of the
         full-sequence bucket mean (misc/vit.py:967-975).
       eps: added to the bucket mass.
-      chunk: causal work-chunk length (0 = chosen by the library); results do
-        not depend on it beyond float rounding.
+      chunk: accepted for the reference's signature and ignored (the causal
+        kernels work on 128-token tiles; results do not depend on a chunk).
       group: torch.distributed process group across which the token axis is
         sharded (contiguous ranges in rank order), or None.
       normalize: causal only.  "bucket" (default): every bucket normalised by
