@@ -251,6 +251,24 @@ int race_backward_q_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k
                        void* workspace, size_t workspace_bytes,
                        cudaStream_t stream);
 
+/* ---- multi-GPU hook -------------------------------------------------------
+ * With a communicator set, race_forward / race_forward_ex and race_backward /
+ * race_backward_ex run a sequence-sharded call: every rank passes its own
+ * contiguous token range of every stream (ranks in token order) and the
+ * library runs the exchange between the split phases on `stream` -- an NCCL
+ * all-reduce of the bucket sums and of dE (non-causal), or an all-gather of
+ * the range totals whose lower- (forward) or higher- (backward) rank sum is
+ * added to the local prefixes (causal).  The temperature gradient stays
+ * rank-local.  Replaces the reference's missing multi-GPU path (it runs one
+ * sequence per GPU); NCCL is opened at run time (libnccl.so.2).  Set the
+ * communicator before race_query: the workspace then includes the exchange
+ * buffers.  The setting is process-wide; NULL returns to single-GPU calls. */
+int race_comm_unique_id(void* id128);   /* NCCL unique id, 128 bytes, on one rank */
+int race_comm_init(void** comm, int nranks, const void* id128, int rank);
+int race_comm_destroy(void* comm);
+int race_set_comm(void* comm);
+const char* race_comm_error(void);      /* text of the last NCCL failure on this thread */
+
 /* Causal only: adds offset (N slots) to every chunk slot of `slots`
  * (state or gstate).  Gradient slots also carry the per-chunk key mass,
  * which the offset does not touch. */

@@ -31,6 +31,8 @@ SYMBOLS = (
     "race_probs", "race_probs_workspace", "race_probs_backward",
     "race_forward_ex", "race_forward_readout_ex", "race_backward_ex", "race_backward_q_ex",
     "race_last_kernels", "race_status_clear", "race_device_status",
+    "race_comm_unique_id", "race_comm_init", "race_comm_destroy", "race_set_comm",
+    "race_comm_error",
 )
 
 
@@ -74,6 +76,12 @@ _SIGS = {
     "race_last_kernels": ([], ctypes.c_char_p),
     "race_status_clear": ([_P, ctypes.c_size_t, _P], ctypes.c_int),
     "race_device_status": ([_P, ctypes.c_size_t, _P, _P], ctypes.c_int),
+    "race_comm_unique_id": ([_P], ctypes.c_int),
+    "race_comm_init": ([ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _P, ctypes.c_int],
+                       ctypes.c_int),
+    "race_comm_destroy": ([_P], ctypes.c_int),
+    "race_set_comm": ([_P], ctypes.c_int),
+    "race_comm_error": ([], ctypes.c_char_p),
     "race_query": ([ctypes.POINTER(RaceDesc), ctypes.POINTER(RaceSizes)], ctypes.c_int),
     "race_forward": ([ctypes.POINTER(RaceDesc), _T, _T, _T, _P, _P, _T, _P, _P, ctypes.c_size_t, _P],
                      ctypes.c_int),

@@ -18,7 +18,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "librace_b200.so")
 SOURCES = ["race_capi.cu", "race_f32_d32.cu", "race_f32_d64.cu", "race_bf16_d32.cu",
-           "race_bf16_d64.cu", "race_probs.cu"]
+           "race_bf16_d64.cu", "race_probs.cu", "race_comm.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
@@ -71,7 +71,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         list(ex.map(compile_one, todo))
     objs = [os.path.join(objdir, s.replace(".cu", ".o")) for s in SOURCES]
     tmp = OUT + ".tmp"
-    cmd = [cc, *ARCH, "-shared", "-o", tmp, *objs]   # cudart linked statically
+    cmd = [cc, *ARCH, "-shared", "-o", tmp, *objs, "-ldl"]   # cudart linked statically
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")

@@ -278,6 +278,9 @@ struct Plan {
   int SA;              // c5: floats per token of alpha
   size_t state_floats, gstate_floats, part_floats, dscale_floats;
   size_t norm_bytes;   // normalize_qk: one normalised [N][T][D] copy (q, then k)
+  void* comm;          // race_set_comm's communicator (nullptr: single GPU)
+  int rank, world;
+  size_t comm_floats;  // world > 1: gathered totals [world][N][SS], total, offset
 };
 
 bool tensor_ok(const race_tensor_t& t, int elem_bytes) {
@@ -332,6 +335,11 @@ int make_plan(const race_desc_t* d, Plan* p) {
   if (P < 1) P = 1;
   p->P = (int)P;
   p->dscale_floats = (size_t)p->N * p->P;
+  {
+    const int rc = comm_rank_size(&p->comm, &p->rank, &p->world);
+    if (rc != RACE_OK) return rc;
+    p->comm_floats = p->world > 1 ? (size_t)(p->world + 2) * p->N * p->SS : 0;
+  }
   const size_t es = d->dtype == RACE_F32 ? 4 : 2;
   p->norm_bytes = (d->flags & RACE_FLAG_NORMALIZE_QK)
                       ? ((size_t)p->N * (size_t)T * D * es + 255) / 256 * 256 : 0;
@@ -362,7 +370,8 @@ int make_plan(const race_desc_t* d, Plan* p) {
 }
 
 size_t ws_bytes(const Plan& p) {
-  return 2 * p.norm_bytes + (p.part_floats + (p.dscale_floats + 3) / 4 * 4 + 64) * sizeof(float);
+  return 2 * p.norm_bytes +
+         (p.comm_floats + p.part_floats + (p.dscale_floats + 3) / 4 * 4 + 64) * sizeof(float);
 }
 
 // The device status word: the last 64 bytes of the workspace the caller
@@ -378,6 +387,7 @@ struct Call {
   bool normalize_qk = false;
   char* norm_q = nullptr;   // normalised copies in the workspace (normalize_qk)
   char* norm_k = nullptr;
+  float* comm_ws = nullptr;  // world > 1: gathered totals, total, offset
   Plan plan;
   Params prm;
   float* part = nullptr;
@@ -403,7 +413,8 @@ int prepare(const race_desc_t* d, const float* planes, const float* scale, void*
   c->normalize_qk = (d->flags & RACE_FLAG_NORMALIZE_QK) != 0;
   c->norm_q = static_cast<char*>(ws);
   c->norm_k = c->norm_q + c->plan.norm_bytes;
-  c->part = reinterpret_cast<float*>(c->norm_k + c->plan.norm_bytes);
+  c->comm_ws = reinterpret_cast<float*>(c->norm_k + c->plan.norm_bytes);
+  c->part = c->comm_ws + c->plan.comm_floats;
   c->dscale_part = c->part + c->plan.part_floats;
   Params& p = c->prm;
   std::memset(&p, 0, sizeof(p));
@@ -981,6 +992,28 @@ int race_forward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, r
                     float* state, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   ApiScope scope_;
   RACE_TRY(race_status_clear(workspace, workspace_bytes, stream));
+  Call c;
+  RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
+  const Plan& pl = c.plan;
+  if (pl.world > 1 && desc->tokens > 0) {
+    // sequence-sharded over the communicator's ranks (this rank holds a
+    // contiguous token range): bucket sums all-reduced, or the causal range
+    // prefixes offset by the totals of the lower ranks
+    const size_t cnt = (size_t)pl.N * pl.SS;
+    float* gathered = c.comm_ws;
+    float* tot = gathered + (size_t)pl.world * cnt;
+    float* off = tot + cnt;
+    RACE_TRY(race_forward_reduce(desc, k, v, planes, scale, state, desc->causal ? tot : nullptr,
+                                 workspace, workspace_bytes, stream));
+    if (!desc->causal) {
+      RACE_TRY(comm_all_reduce(pl.comm, state, cnt, stream));
+    } else {
+      RACE_TRY(comm_gather_sum(pl.comm, tot, gathered, cnt, 0, pl.rank, off, stream));
+      if (pl.rank > 0) RACE_TRY(race_add_offset(desc, state, off, 0, stream));
+    }
+    return race_forward_readout_ex(desc, q, k, v, planes, scale, state, out, den, workspace,
+                                   workspace_bytes, stream);
+  }
   RACE_TRY(race_forward_reduce(desc, k, v, planes, scale, state, nullptr, workspace,
                                workspace_bytes, stream));
   return race_forward_readout_ex(desc, q, k, v, planes, scale, state, out, den, workspace,
@@ -1112,6 +1145,27 @@ int race_backward_ex(const race_desc_t* desc, race_tensor_t q, race_tensor_t k, 
                      size_t workspace_bytes, cudaStream_t stream) {
   ApiScope scope_;
   RACE_TRY(race_status_clear(workspace, workspace_bytes, stream));
+  Call c;
+  RACE_TRY(prepare(desc, planes, scale, workspace, workspace_bytes, &c));
+  const Plan& pl = c.plan;
+  if (pl.world > 1 && desc->tokens > 0) {
+    // dE all-reduced, or the causal gradient suffixes offset by the totals of
+    // the higher ranks; *dscale covers this rank's tokens
+    const size_t cnt = (size_t)pl.N * pl.SS;
+    float* gathered = c.comm_ws;
+    float* tot = gathered + (size_t)pl.world * cnt;
+    float* off = tot + cnt;
+    RACE_TRY(race_backward_q_ex(desc, q, k, v, planes, scale, state, dout, dden, dq, dscale, gstate,
+                                desc->causal ? tot : nullptr, workspace, workspace_bytes, stream));
+    if (!desc->causal) {
+      RACE_TRY(comm_all_reduce(pl.comm, gstate, cnt, stream));
+    } else {
+      RACE_TRY(comm_gather_sum(pl.comm, tot, gathered, cnt, pl.rank + 1, pl.world, off, stream));
+      if (pl.rank + 1 < pl.world) RACE_TRY(race_add_offset(desc, gstate, off, 1, stream));
+    }
+    return race_backward_kv(desc, q, k, v, planes, scale, state, gstate, dout, dk, dv, dscale,
+                            workspace, workspace_bytes, stream);
+  }
   RACE_TRY(race_backward_q_ex(desc, q, k, v, planes, scale, state, dout, dden, dq, dscale, gstate,
                               nullptr, workspace, workspace_bytes, stream));
   return race_backward_kv(desc, q, k, v, planes, scale, state, gstate, dout, dk, dv, dscale,

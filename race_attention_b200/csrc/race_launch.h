@@ -52,4 +52,11 @@ cudaError_t launch_probs(bool bwd, bool bf16, int D, const Params& prm, float* o
                          float* part, cudaStream_t s);
 int64_t probs_blocks(int64_t T);
 
+// race_comm.cu: the communicator set by race_set_comm (none: world 1, rank 0)
+// and the two exchanges of a sequence-sharded call, on the caller's stream.
+int comm_rank_size(void** comm, int* rank, int* world);
+int comm_all_reduce(void* comm, float* buf, size_t count, cudaStream_t stream);
+int comm_gather_sum(void* comm, const float* total, float* gathered, size_t count, int r0, int r1,
+                    float* offset, cudaStream_t stream);
+
 }  // namespace race

@@ -92,3 +92,90 @@ def test_two_gpu_sharded_matches_oracle():
                 assert err < 1e-4, (causal, name, err)
             for p in parts:
                 assert math.isclose(float(p["ds"]), ref[4], rel_tol=1e-3), (float(p["ds"]), ref[4])
+
+
+def _worker_capi(rank, world, port, outdir):
+    """The library's own hook: race_set_comm with an NCCL communicator made by
+    race_comm_init, then plain race_forward / race_backward calls through the
+    C ABI on this rank's shard; the library runs the exchange itself."""
+    import ctypes
+    import torch.distributed as dist
+    from race_attention_b200 import _lib
+    from race_attention_b200.functional import Buffers, _ptr, _rt, _stream, make_desc, query
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    lib = _lib.load()
+    comm = ctypes.c_void_p()
+    try:
+        dev = torch.device("cuda", rank)
+        uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            host = torch.zeros(128, dtype=torch.uint8)
+            _lib.check(lib.race_comm_unique_id(_ptr(host)))
+            uid.copy_(host)
+        dist.broadcast(uid, 0)
+        uid_h = uid.cpu().contiguous()
+        _lib.check(lib.race_comm_init(ctypes.byref(comm), world, _ptr(uid_h), rank))
+        _lib.check(lib.race_set_comm(comm))
+        q, k, v, dout, planes = _data()
+        lo, hi = T * rank // world, T * (rank + 1) // world
+        Pd = torch.tensor(planes, device=dev)
+        for causal in (False, True):
+            scale = torch.tensor(8.0 if causal else 1.3, device=dev)
+            t = lambda a: torch.tensor(a[:, lo:hi], device=dev).unsqueeze(0).unsqueeze(3).contiguous()
+            qt, kt, vt, dot = (t(a) for a in (q, k, v, dout))
+            shape = tuple(qt.shape)
+            desc = make_desc(shape, torch.float32, K, L, causal, 1e-6, 0, True, 0,
+                             _lib.RACE_FLAG_STRICT_TMA)
+            sizes = query(desc)
+            buf = Buffers(sizes, dev)
+            state, gstate, ws = (buf.floats(sizes.state_bytes), buf.floats(sizes.gstate_bytes),
+                                 buf.workspace())
+            out, dq, dk, dv = (torch.empty(shape, device=dev) for _ in range(4))
+            ds = torch.zeros((), device=dev)
+            _lib.check(lib.race_forward(desc, _rt(qt), _rt(kt), _rt(vt), _ptr(Pd), _ptr(scale),
+                                        _rt(out), _ptr(state), _ptr(ws), ws.numel(), _stream()))
+            _lib.check(lib.race_backward(desc, _rt(qt), _rt(kt), _rt(vt), _ptr(Pd), _ptr(scale),
+                                         _ptr(state), _rt(dot), _rt(dq), _rt(dk), _rt(dv),
+                                         _ptr(ds), _ptr(gstate), _ptr(ws), ws.numel(),
+                                         _stream()))
+            dist.all_reduce(ds)   # rank-local through the C ABI: sum as a parameter gradient
+            torch.cuda.synchronize()
+            f = lambda x: x.detach().squeeze(3).squeeze(0).double().cpu().numpy()
+            np.savez(os.path.join(outdir, f"r{rank}_capi{int(causal)}.npz"), out=f(out),
+                     dq=f(dq), dk=f(dk), dv=f(dv), ds=float(ds))
+    finally:
+        lib.race_set_comm(None)
+        if comm.value:
+            lib.race_comm_destroy(comm)
+        dist.destroy_process_group()
+
+
+def test_two_gpu_library_hook_matches_oracle():
+    """race_set_comm: the sharded exchange run by the library itself (C ABI)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    q, k, v, dout, planes = _data()
+    with tempfile.TemporaryDirectory() as td:
+        mp.spawn(_worker_capi, args=(2, port, td), nprocs=2, join=True)
+        for causal in (False, True):
+            scale = 8.0 if causal else 1.3
+            parts = [np.load(os.path.join(td, f"r{r}_capi{int(causal)}.npz")) for r in range(2)]
+            cat = lambda key: np.concatenate([p[key] for p in parts], axis=1)
+            P = np.broadcast_to(planes, (N,) + planes.shape[1:])
+            if causal:
+                ref = O.causal_streamed(q, k, v, P, K, L, scale, dout)
+            else:
+                ref = (O.forward(q, k, v, P, K, L, scale, False),) + \
+                    O.backward(q, k, v, P, K, L, scale, False, dout)
+            for name, b in zip(("out", "dq", "dk", "dv"), ref[:4]):
+                err = O.rel_l2(cat(name), b)
+                assert err < 1e-4, (causal, name, err)
+            for p in parts:
+                assert math.isclose(float(p["ds"]), ref[4], rel_tol=1e-3), (float(p["ds"]), ref[4])
