@@ -128,19 +128,22 @@ def dist_env():
 class Layer:
     """Preallocated buffers + the C-ABI calls of one fwd+bwd step."""
 
-    def __init__(self, causal, dtype, tokens, group, device, seed, normalize=0):
+    def __init__(self, causal, dtype, tokens, group, device, seed, normalize=0, batch=1, heads=1,
+                 bits=K, tables=L):
         from race_attention_b200 import _lib
         from race_attention_b200.functional import Buffers, make_desc, query
         self.lib = _lib.load()
         self.causal, self.dtype, self.group = causal, dtype, group
         g = torch.Generator(device=device).manual_seed(seed)
-        shape = (1, 1, tokens, 1, D)
+        # [M=1, B, T, H, d] as the modules lay the Linear outputs out
+        shape = (1, batch, tokens, heads, D)
         rnd = lambda: torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(dtype)
         self.q, self.k, self.v, self.dout = rnd(), rnd(), rnd(), rnd()
         g0 = torch.Generator(device=device).manual_seed(0)   # identical planes on every rank
-        self.planes = torch.randn((1, K * L, D), generator=g0, device=device)
+        self.planes = torch.randn((1, bits * tables, D), generator=g0, device=device)
         self.scale = torch.tensor(1.0, device=device)
-        self.desc = make_desc(shape, dtype, K, L, causal, 1e-6, 0, True, normalize)
+        self.desc = make_desc(shape, dtype, bits, tables, causal, 1e-6, 0, True, normalize,
+                              _lib.RACE_FLAG_STRICT_TMA)
         self.sizes = query(self.desc)
         self.buf = Buffers(self.sizes, device)
         self.out = torch.empty(shape, dtype=dtype, device=device)
@@ -406,6 +409,7 @@ def run_ours(args):
         torch.cuda.empty_cache()
 
     strong = None if args.no_strong else strong_scaling(args, world, group, device)
+    shapes = baseline_shapes(args, device) if (world == 1 and not args.no_shapes) else None
     parity = sharded_parity(group, device) if world > 1 else None
 
     layer, rec = head
@@ -428,6 +432,8 @@ def run_ours(args):
     }
     if strong is not None:
         line["strong_64M"] = strong
+    if shapes is not None:
+        line["baseline_shapes"] = shapes
     if parity is not None:
         line["sharded_parity"] = parity
     if world == 1:
@@ -471,6 +477,29 @@ def strong_scaling(args, world, group, device):
     return {"tokens_total": STRONG_TOKENS, "tokens_per_gpu": tokens, "steps": steps,
             "ms_per_step": ms, "value": STRONG_TOKENS / (ms / 1e3), "unit": "tokens/s",
             "scaling": "strong"}
+
+
+def baseline_shapes(args, device):
+    """The BASELINE configs' own layer shapes on one GPU (many independent
+    (b, h) streams: the replica case, no collective): C3 ViT (B 256, H 6,
+    785 tokens, K4 L4 = 64 buckets, fp32, non-causal), C2 (B 4, H 12, 16384
+    tokens, bf16, causal), C4 (B 1, H 12, 65536 tokens, bf16, causal).
+    tokens/s counts B * T per layer call; head-tokens/s counts B * H * T."""
+    res = []
+    for name, b, t, h, bits, tables, causal, dtype in (
+            ("C3_vit", 256, 785, 6, 4, 4, False, torch.float32),
+            ("C2_causal", 4, 16384, 12, 2, 5, True, torch.bfloat16),
+            ("C4_long_causal", 1, 65536, 12, 2, 5, True, torch.bfloat16)):
+        layer = Layer(causal, dtype, t, None, device, seed=3000, batch=b, heads=h, bits=bits,
+                      tables=tables)
+        ms = timed(layer.step, 20, 3, None, device)
+        res.append({"config": name, "batch": b, "heads": h, "tokens": t, "K": bits, "L": tables,
+                    "causal": causal, "dtype": "f32" if dtype == torch.float32 else "bf16",
+                    "ms_per_step": ms, "tokens_per_s": b * t / (ms / 1e3),
+                    "head_tokens_per_s": b * h * t / (ms / 1e3)})
+        del layer
+        torch.cuda.empty_cache()
+    return res
 
 
 def sharded_parity(group, device):
@@ -565,6 +594,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-strong", action="store_true")
+    ap.add_argument("--no-shapes", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

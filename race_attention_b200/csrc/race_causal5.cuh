@@ -737,9 +737,12 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
           for (int a = 0; a < MYG; ++a) {
             const int gi = sub + a * NTH;
             if (gi < NG) {
+              // per-bucket mode keeps 1 / (A + eps) in am, global mode keeps A
 #pragma unroll
-              for (int b = 0; b < G::GB; ++b)
-                wv[a][b] = prm.global_norm ? pq[a][b] * rden : pq[a][b] / (am[a][b] + prm.eps);
+              for (int b = 0; b < G::GB; ++b) {
+                if (!prm.global_norm) am[a][b] = 1.f / (am[a][b] + prm.eps);
+                wv[a][b] = pq[a][b] * (prm.global_norm ? rden : am[a][b]);
+              }
 #pragma unroll
               for (int c8 = 0; c8 < G::GB / 8; ++c8) {
                 const int c = gi * G::GB / 8 + c8;
@@ -873,7 +876,7 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
                 dpq[b] = valid ? rr[a][b] * rden + am[a][b] * gden : 0.f;
                 al[b] = valid ? pq[a][b] * gden : 0.f;
               } else {
-                dpq[b] = valid ? rr[a][b] / (am[a][b] + prm.eps) : 0.f;
+                dpq[b] = valid ? rr[a][b] * am[a][b] : 0.f;
                 al[b] = -wv[a][b] * dpq[b];
               }
               asum[a][b] += al[b];

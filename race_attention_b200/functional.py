@@ -320,6 +320,24 @@ def race_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, planes: to
     return (out, den) if return_den else out
 
 
+def fused_qkv(x: torch.Tensor, q_lin, k_lin, v_lin, heads: int, head_dim: int):
+    """q, k, v projections of x [B, T, d_in] as ONE GEMM over the three Linear
+    layers' concatenated weights (the reference runs three, misc/vit.py:1012-1014,
+    misc/race.py:160-162), returned as [B, T, H, d_k] strided views of the
+    [B, T, 3, H, d_k] result: the kernels read them in place (token stride
+    3 H d_k), so no copy or permute follows.  Gradients flow back to the three
+    layers' weights and biases through the concatenation."""
+    B, T, _ = x.shape
+    w = torch.cat([q_lin.weight, k_lin.weight, v_lin.weight], dim=0)
+    if q_lin.bias is not None:
+        b = torch.cat([q_lin.bias, k_lin.bias, v_lin.bias], dim=0)
+        y = torch.nn.functional.linear(x, w, b)
+    else:
+        y = torch.nn.functional.linear(x, w)
+    y = y.view(B, T, 3, heads, head_dim)
+    return y[:, :, 0], y[:, :, 1], y[:, :, 2]
+
+
 def default_causal_scale(head_dim: int) -> float:
     """Fixed divisor of the causal module (misc/race.py:67)."""
     return math.sqrt(head_dim)

@@ -12,7 +12,7 @@ import math
 import torch
 from torch import nn
 
-from .functional import race_attention
+from .functional import fused_qkv, race_attention
 
 
 class BatchedACE(nn.Module):
@@ -59,11 +59,12 @@ class RACEAttention(nn.Module):
     """
 
     def __init__(self, d, h, K, L, M, drop=0.1, qkv_bias=False, device="cpu",
-                 merge_heads: str = "reference"):
+                 merge_heads: str = "reference", fuse_qkv: bool = True):
         super().__init__()
         if merge_heads not in ("reference", "concat"):
             raise ValueError("merge_heads must be 'reference' or 'concat'")
         self.merge_heads = merge_heads
+        self.fuse_qkv = fuse_qkv   # one GEMM for q, k, v (same parameters as three)
         assert d % h == 0
         self.h, self.d_k, self.M = h, d // h, M
         self.q = nn.Linear(d, d, bias=qkv_bias)
@@ -75,9 +76,12 @@ class RACEAttention(nn.Module):
 
     def forward(self, x):
         B, T, _ = x.shape
-        Q = self.q(x).view(B, T, self.h, self.d_k)
-        K = self.k(x).view(B, T, self.h, self.d_k)
-        V = self.v(x).view(B, T, self.h, self.d_k)
+        if self.fuse_qkv:
+            Q, K, V = fused_qkv(x, self.q, self.k, self.v, self.h, self.d_k)
+        else:
+            Q = self.q(x).view(B, T, self.h, self.d_k)
+            K = self.k(x).view(B, T, self.h, self.d_k)
+            V = self.v(x).view(B, T, self.h, self.d_k)
         pack = lambda z: z.unsqueeze(0).expand(self.M, -1, -1, -1, -1)
         ref = self.merge_heads == "reference"
         out_h = self.ace(pack(K), pack(V), pack(Q), head_major_out=ref)

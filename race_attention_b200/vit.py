@@ -12,7 +12,7 @@ import itertools
 import torch
 from torch import nn
 
-from .functional import race_attention
+from .functional import fused_qkv, race_attention
 
 
 class BatchedACE(nn.Module):
@@ -68,11 +68,12 @@ class RACEAttention(nn.Module):
     """
 
     def __init__(self, d_in, d_out, dropout, num_heads, L, K, N_M, qkv_bias=False, device="cpu",
-                 merge_heads: str = "reference"):
+                 merge_heads: str = "reference", fuse_qkv: bool = True):
         super().__init__()
         if merge_heads not in ("reference", "concat"):
             raise ValueError("merge_heads must be 'reference' or 'concat'")
         self.merge_heads = merge_heads
+        self.fuse_qkv = fuse_qkv   # one GEMM for q, k, v (same parameters as three)
         assert d_in % num_heads == 0
         self.H = num_heads
         self.d_k = d_in // num_heads
@@ -89,9 +90,12 @@ class RACEAttention(nn.Module):
     def forward(self, x):
         B, T, _ = x.shape
         H, d_k, M = self.H, self.d_k, self.M
-        Q = self.q_proj(x).view(B, T, H, d_k)
-        K = self.k_proj(x).view(B, T, H, d_k)
-        V = self.v_proj(x).view(B, T, H, d_k)
+        if self.fuse_qkv:
+            Q, K, V = fused_qkv(x, self.q_proj, self.k_proj, self.v_proj, H, d_k)
+        else:
+            Q = self.q_proj(x).view(B, T, H, d_k)
+            K = self.k_proj(x).view(B, T, H, d_k)
+            V = self.v_proj(x).view(B, T, H, d_k)
         pack = lambda Z: Z.unsqueeze(0).expand(M, -1, -1, -1, -1)
         ref = self.merge_heads == "reference"
         # reference merge: the output is written head-major, so the merge is a view for M = 1

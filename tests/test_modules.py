@@ -89,15 +89,36 @@ def test_numpy_restatement_matches_reference_module(path):
     assert O.rel_l2(out, z["out"].astype(np.float64)) < 1e-6
 
 
+def test_fused_qkv_matches_three_linears():
+    """The one-GEMM q/k/v projection gives the three Linear layers' outputs and
+    gradients (CPU, float64)."""
+    from race_attention_b200.functional import fused_qkv
+    torch.manual_seed(0)
+    lins = [torch.nn.Linear(48, 48, bias=True).double() for _ in range(3)]
+    x = torch.randn(2, 7, 48, dtype=torch.float64, requires_grad=True)
+    q, k, v = fused_qkv(x, *lins, heads=3, head_dim=16)
+    ref = [lin(x).view(2, 7, 3, 16) for lin in lins]
+    for a, b in zip((q, k, v), ref):
+        assert torch.allclose(a, b, rtol=1e-12, atol=1e-12)
+    g = [torch.randn_like(a) for a in (q, k, v)]
+    gx, *gw = torch.autograd.grad([q, k, v], [x] + [lin.weight for lin in lins], g)
+    rx, *rw = torch.autograd.grad(ref, [x] + [lin.weight for lin in lins], g)
+    assert torch.allclose(gx, rx, rtol=1e-12, atol=1e-12)
+    for a, b in zip(gw, rw):
+        assert torch.allclose(a, b, rtol=1e-12, atol=1e-12)
+
+
 @pytest.mark.gpu
+@pytest.mark.parametrize("fuse", [True, False], ids=["fused_qkv", "three_gemms"])
 @pytest.mark.parametrize("path", FILES, ids=IDS)
-def test_module_forward_backward_on_gpu(path):
+def test_module_forward_backward_on_gpu(path, fuse):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     meta, sd, z = G.load_module(path)
     mod = G.build_module(meta, device="cuda")
     mod.load_state_dict(sd, strict=True)
     mod = mod.cuda().eval()
+    (mod.att if meta["kind"] == "block" else mod).fuse_qkv = fuse
     x = torch.tensor(z["x"], device="cuda", requires_grad=True)
     out = mod(x)
     out.backward(torch.tensor(z["dout"], device="cuda"))
