@@ -14,8 +14,9 @@
 //   out = W . B0^T + mask(W . pK^T) . V         (mask: tau <= t)
 //
 // with B0 the prefix at the tile start: the 128 x 128 intra-tile matrix
-// G = W pK^T, masked and split into bf16 parts in shared memory, is the A
-// operand of the second product.  The state B0 is carried from tile to tile
+// G = W pK^T, masked and split into bf16 parts (in place in tensor memory,
+// or in shared memory for the query backward), is the A operand of the
+// second product.  The state B0 is carried from tile to tile
 // by the tensor core (B0 += V^T pK accumulates in tensor memory over the
 // range); A(t) is a warp scan of pK over the tile's tokens.
 //
@@ -224,43 +225,64 @@ __device__ __forceinline__ float token_sum(float x, float* xs, int row, int sub)
 }
 
 // ------------------------------------------------------------------ F2 forward
+// Per tile of a range, with the prefix B0, A0 at the tile start: the hash from
+// the projections, A by a warp scan, W, then on the tensor core G = W pK^T,
+// out = W B0^T + mask(G) V and the state B0 += V^T pK.  The masked intra-tile
+// matrix is kept in tensor memory:
+// the G accumulator's 128 columns are read by the threads, masked, split into
+// bf16 hi / lo and written back in place (packed, 64 columns each) as the A
+// operand of mask(G) . V, so the shared memory holds only one set of input
+// slots and the operands (about 110 KB) and two CTAs of 256 threads share an
+// SM: one CTA's thread phases run while the other's MMAs and loads are in
+// flight.  The out tile leaves through the consumed v slot.
 template <int D, int SPAD>
 struct FwdLay {
-  static constexpr int NTH = 4;                         // threads per token
-  static constexpr int SP = (SPAD + 15) / 16 * 16;      // bucket columns
-  static constexpr int NFULL = 2;                       // input slots (projections + v)
-  static constexpr int VX = 0;                          // [2] v slots (landed, then hi | lo)
-  static constexpr int PJX = VX + 2 * Slot<D>::FLOATS;  // [2] projQ [TT][16] then projK [TT][16]
-  static constexpr int PJF = 2 * TT * PJ;               // floats per projection slot
-  static constexpr int GM = PJX + 2 * PJF;              // bf16 [TT x TT] masked G, hi then lo;
-                                                        // later the out tile's staging
-  static constexpr int PK = GM + TT * TT;               // bf16 [TT x 2SP] pK (hi | lo)
+  static constexpr int NTH = 2;
+  static constexpr int SP = (SPAD + 15) / 16 * 16;
+  static constexpr int NFULL = 2;                       // 0: projections, 1: v
+  static constexpr int VX = 0;                          // v (landed, hi | lo), then out staging
+  static constexpr int PJX = VX + Slot<D>::FLOATS;      // projQ [TT][16] then projK [TT][16]
+  static constexpr int PK = PJX + 2 * TT * PJ;          // bf16 [TT x 2SP] pK (hi | lo)
   static constexpr int WH = PK + TT * SP;               // bf16 [TT x 2SP] W (hi | hi)
   static constexpr int WL = WH + TT * SP;               // bf16 [TT x SP] W lo
   static constexpr int B0 = WL + TT * SP / 2;           // bf16 [D x 2SP] B0^T (hi | lo)
-  static constexpr int B0F = B0 + D * SP;               // fp32 [SP][D] prefix at the range start
-  static constexpr int A0 = B0F + SP * D;               // double [SP] key mass at the tile start
-  static constexpr int SCAN = A0 + 2 * SP;              // [SP][4] per-warp token totals
-  static constexpr int DENX = SCAN + 4 * SP;            // [NTH][TT] global mode: den parts
+  static constexpr int B0F = B0 + D * SP;               // fp32 [SP][D]
+  static constexpr int A0 = B0F + SP * D;               // double [SP]
+  static constexpr int SCAN = A0 + 2 * SP;              // [SP][4]
+  static constexpr int DENX = SCAN + 4 * SP;            // [NTH][TT]
   static constexpr int BAR = DENX + NTH * TT;
-  static constexpr int FLOATS = BAR + 16 + 256;         // + slack for 1 KB alignment
-  static constexpr int TCOLS = 256;                     // G [0, 128), OUT [128, 128 + D), ST
-  static constexpr int C_G = 0, C_OUT = 128, C_ST = 128 + D;   // ST: M = 64, 2 SP columns
+  static constexpr int FLOATS = BAR + 16 + 256;
+  static constexpr int TCOLS = 256;
+  // G [0, 128) (then mask(G) hi [0, 64), lo [64, 128) as packed bf16), OUT, ST (M = 64)
+  static constexpr int C_G = 0, C_OUT = 128, C_ST = 128 + D;
   static_assert(C_ST + 2 * SP <= TCOLS, "tensor-memory columns");
-  static_assert(GM % 256 == 0 && VX % 256 == 0, "1 KB aligned TMA boxes");
-  static_assert(FLOATS * 4 <= 227 * 1024, "shared memory");
+  static_assert(FLOATS * 4 <= 113 * 1024, "two CTAs per SM");
 };
 
-// Forward readout of one causal range per work item (maps: 0 projQ, 1 projK,
-// 2 v, 3 out).
+__device__ __forceinline__ void mma_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t id,
+                                       bool acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(id), "r"((uint32_t)acc));
+}
+// 8 consecutive 32-bit columns of this thread's lane
+__device__ __forceinline__ void tst8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+      : "memory");
+}
+__device__ __forceinline__ void tst_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 template <typename T, int D, int SPAD, int K>
-__global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
+__global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
     k_c5_fwd(const Params prm, const __grid_constant__ TmaMaps maps) {
   using LY = FwdLay<D, SPAD>;
   constexpr int SP = LY::SP, NTH = LY::NTH, W = D / NTH;
   using G = Groups<K>;
-  constexpr int NG = SP / G::GB;                       // bucket groups
-  constexpr int MYG = (NG + NTH - 1) / NTH;            // groups per thread (at most)
+  constexpr int NG = SP / G::GB;
+  constexpr int MYG = (NG + NTH - 1) / NTH;
   constexpr int GC = TT / NTH;                         // G columns per thread
   T5_PROLOGUE
   (void)cur_m;
@@ -269,8 +291,6 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
   bf16* wh = reinterpret_cast<bf16*>(sm + LY::WH);
   bf16* wl = reinterpret_cast<bf16*>(sm + LY::WL);
   bf16* b0 = reinterpret_cast<bf16*>(sm + LY::B0);
-  bf16* gm_hi = reinterpret_cast<bf16*>(sm + LY::GM);
-  bf16* gm_lo = gm_hi + TT * TT;
   float* b0f = sm + LY::B0F;
   double* a0 = reinterpret_cast<double*>(sm + LY::A0);
   float* scan = sm + LY::SCAN;
@@ -279,18 +299,13 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
     const Item it = item_of(prm, w);
     if (it.ntiles <= 0) continue;
     const int n = it.n;
-    __syncthreads();   // the previous item's MMAs and stores are done with shared memory
+    __syncthreads();
     {
-      // the range's exclusive prefix: B0 [S][D] (fp32) and A0 [S] (float64)
       const float* st = prm.state + ((size_t)n * prm.P + it.part) * prm.SS;
-      for (int e = tid; e < SP * D; e += TT * NTH) {
-        const int s = e / D;
-        b0f[e] = s < prm.S ? st[e] : 0.f;
-      }
+      for (int e = tid; e < SP * D; e += TT * NTH) b0f[e] = e / D < prm.S ? st[e] : 0.f;
       for (int s = tid; s < SP; s += TT * NTH) a0[s] = s < prm.S ? (double)st[prm.S * D + s] : 0.0;
     }
     __syncthreads();
-    // B0 operand of the first tile: the range prefix
     if (tid < D) {
       for (int s8 = 0; s8 < SP / 8; ++s8) {
         float v[8];
@@ -302,38 +317,49 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
         put_chunk<2 * SP>(b0, tid, SP / 8 + s8, lo);
       }
     }
-    auto load = [&](int j) {
+    auto load_p = [&](int j) {
       if (failed) return;
-      const int f = j & 1;
-      inflight |= 1u << f;
+      inflight |= 1u;
       if (tid == 0) {
         const int64_t t0 = it.t0 + (int64_t)j * TT;
-        float* pj = sm + LY::PJX + f * LY::PJF;
+        float* pj = sm + LY::PJX;
         fence_async_smem();
-        bar_expect_tx(full + f, (uint32_t)(Box<T, D>::BYTES + 2 * TT * PJ * 4));
-        tma_load3(pj, &maps.map[0], 0, (int)t0, n, full + f);
-        tma_load3(pj + TT * PJ, &maps.map[1], 0, (int)t0, n, full + f);
-        tma_rows5<T, D>(&maps.map[2], sm + LY::VX + f * Slot<D>::FLOATS, prm.lv, prm, n, t0,
-                        full + f);
+        bar_expect_tx(full, (uint32_t)(2 * TT * PJ * 4));
+        tma_load3(pj, &maps.map[0], 0, (int)t0, n, full);
+        tma_load3(pj + TT * PJ, &maps.map[1], 0, (int)t0, n, full);
       }
     };
-    load(0);
+    auto load_v = [&](int j) {   // thread 0 only after the out store has read the slot
+      if (failed) return;
+      inflight |= 2u;
+      if (tid == 0) {
+        bulk_wait_read();
+        fence_async_smem();
+        bar_expect_tx(full + 1, (uint32_t)Box<T, D>::BYTES);
+        tma_rows5<T, D>(&maps.map[2], sm + LY::VX, prm.lv, prm, n, it.t0 + (int64_t)j * TT,
+                        full + 1);
+      }
+    };
+    load_p(0);
+    load_v(0);
     for (int i = 0; i < it.ntiles; ++i) {
       const int64_t tile0 = it.t0 + (int64_t)i * TT;
-      const int f = i & 1;
-      float* VXt = sm + LY::VX + f * Slot<D>::FLOATS;
-      const float* pj = sm + LY::PJX + f * LY::PJF;
-      if (i + 1 < it.ntiles) load(i + 1);
-      T5_WAIT(full + f, (phF >> f) & 1);
+      float* VXt = sm + LY::VX;
+      const float* pj = sm + LY::PJX;
+      T5_WAIT(full, phF & 1);
       if (!failed) {
-        phF ^= 1u << f;
-        inflight &= ~(1u << f);
+        phF ^= 1u;
+        inflight &= ~1u;
+      }
+      T5_WAIT(full + 1, (phF >> 1) & 1);
+      if (!failed) {
+        phF ^= 2u;
+        inflight &= ~2u;
       }
       const bool valid = tile0 + row < it.t1;
       {
         float y[W];
         read_cols<T, D, W>(VXt, row, sub * W, y);
-        // hash of this thread's bucket groups, then the key-mass scan
         float pq[MYG][G::GB], pkv[MYG][G::GB];
 #pragma unroll
         for (int a = 0; a < MYG; ++a) {
@@ -354,7 +380,8 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
             }
           }
         }
-        __syncthreads();   // v slot read; scan scratch free
+        __syncthreads();   // v and the projections read
+        if (i + 1 < it.ntiles) load_p(i + 1);
         put_cols<D, W, sizeof(T) == 4 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1),
                                                nullptr, row, sub * W, y);
         float incl[MYG][G::GB];
@@ -371,7 +398,6 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
           }
         }
         __syncthreads();
-        // key mass A_s(t); global mode: den(t) = sum_s pQ_s A_s over the token's threads
         float av[MYG][G::GB], dpart = 0.f;
 #pragma unroll
         for (int a = 0; a < MYG; ++a) {
@@ -387,7 +413,7 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
             }
           }
         }
-        float rden = 0.f;   // global mode: 1 / max(den, eps)
+        float rden = 0.f;
         if (prm.global_norm) {
           const float den = token_sum<NTH>(dpart, sm + LY::DENX, row, sub);
           rden = 1.f / fmaxf(den, prm.eps);
@@ -401,7 +427,6 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
 #pragma unroll
             for (int b = 0; b < G::GB; ++b)
               wv[b] = prm.global_norm ? pq[a][b] * rden : pq[a][b] / (av[a][b] + prm.eps);
-            // pK (hi | lo), W (hi | hi) and W lo, 8 buckets per chunk
 #pragma unroll
             for (int c8 = 0; c8 < G::GB / 8; ++c8) {
               const int c = gi * G::GB / 8 + c8;
@@ -417,24 +442,17 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
           }
         }
       }
-      // padding buckets (>= the groups' columns) of pK / W stay zero: every
-      // group column below SP is written above
       fence_async_smem();
       fence_before();
       __syncthreads();
       if (tid == 0 && !failed) {
         fence_after();
-        // the previous tile's out store has left the staging area (the masked
-        // G written after this barrier): no thread passes barA before this
-        bulk_wait_read();
-        // G = W . pK^T (hi.hi + hi.lo through the duplicated W hi, lo.hi)
 #pragma unroll
         for (int ks = 0; ks < 2 * SP / 16; ++ks)
           mma(tbase + LY::C_G, desc<2 * SP>(wh, ks), desc<2 * SP>(pk, ks), idesc<TT>(), ks > 0);
 #pragma unroll
         for (int ks = 0; ks < SP / 16; ++ks)
           mma(tbase + LY::C_G, desc<SP>(wl, ks), desc<2 * SP>(pk, ks), idesc<TT>(), true);
-        // OUT = W . B0^T
 #pragma unroll
         for (int ks = 0; ks < 2 * SP / 16; ++ks)
           mma(tbase + LY::C_OUT, desc<2 * SP>(wh, ks), desc<2 * SP>(b0, ks), idesc<D>(), ks > 0);
@@ -443,7 +461,6 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
           mma(tbase + LY::C_OUT, desc<SP>(wl, ks), desc<2 * SP>(b0, ks), idesc<D>(), true);
         { commit(barA); ++issA; }
       }
-      // the tile's key mass moves the prefix on (every thread has read a0)
       if (sub == 0 && tid < SP) {
         float tot = 0.f;
         for (int q2 = 0; q2 < 4; ++q2) tot += scan[tid * 4 + q2];
@@ -453,7 +470,8 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
       phA ^= 1;
       fence_after();
       {
-        // masked G row: columns [GC sub, GC sub + GC) of token `row`
+        // masked G row (columns [GC sub, GC sub + GC)), split to packed bf16 pairs
+        uint32_t hw[GC / 2], lw[GC / 2];
 #pragma unroll
         for (int c0 = 0; c0 < GC; c0 += 16) {
           float g[16];
@@ -463,23 +481,29 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
           for (int e = 0; e < 16; ++e)
             if (GC * sub + c0 + e > row) g[e] = 0.f;
 #pragma unroll
-          for (int c8 = 0; c8 < 2; ++c8) {
-            uint4 hi, lo;
-            split8(g + 8 * c8, hi, lo);
-            const int c = (GC * sub + c0) / 8 + c8;
-            put_chunk<TT>(gm_hi, row, c, hi);
-            put_chunk<TT>(gm_lo, row, c, lo);
-          }
+          for (int e = 0; e < 16; e += 2) split2(g[e], g[e + 1], hw[(c0 + e) / 2], lw[(c0 + e) / 2]);
         }
+        fence_before();
+        __syncthreads();   // every G column has been read before any is overwritten
+        fence_after();
+#pragma unroll
+        for (int c = 0; c < GC / 2; c += 8) {
+          uint32_t h8[8], l8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            h8[e] = hw[c + e];
+            l8[e] = lw[c + e];
+          }
+          tst8(tlane + LY::C_G + GC / 2 * sub + c, h8);
+          tst8(tlane + LY::C_G + 64 + GC / 2 * sub + c, l8);
+        }
+        tst_wait();
       }
-      fence_async_smem();
       fence_before();
       __syncthreads();
       if (tid == 0 && !failed) {
         fence_after();
         const bf16* vp[2] = {Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1)};
-        const bf16* gp[2] = {gm_hi, gm_lo};
-        // OUT += mask(G) . V  (hi.hi, hi.lo, lo.hi; bf16 v is exact in its first part)
 #pragma unroll
         for (int a = 0; a < 2; ++a)
 #pragma unroll
@@ -487,10 +511,9 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
             if (a + b == 2 || (sizeof(T) == 2 && b == 1)) continue;
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks)
-              mma(tbase + LY::C_OUT, desc<TT>(gp[a], ks), desc_mn<D>(vp[b], ks), idesc_bmn<D>(),
-                  true);
+              mma_ta(tbase + LY::C_OUT, tbase + LY::C_G + 64 * a + 8 * ks, desc_mn<D>(vp[b], ks),
+                     idesc_bmn<D>(), true);
           }
-        // ST[d][s] += sum_t v[t][d] pK[t][s] over the range (both parts of pK along N)
 #pragma unroll
         for (int a = 0; a < (sizeof(T) == 4 ? 2 : 1); ++a)
 #pragma unroll
@@ -505,11 +528,8 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
       {
         float o[W];
         tld_sum<W, 1>(tlane + LY::C_OUT + sub * W, 0, o);
-        // staging of the out tile in the (consumed) masked-G area
-        put_tile_cols<T, D, W>(sm + LY::GM, row, sub * W, o);
+        put_tile_cols<T, D, W>(sm + LY::VX, row, sub * W, o);   // v consumed: out staging
       }
-      // B0 of the next tile: range prefix + the state accumulated so far;
-      // lane 32 q + l (l < 16) of warps 0..3 holds row d = 16 q + l
       if (i + 1 < it.ntiles && sub == 0) {
         const int d = 16 * quad + lane;
         float stv[2 * SP];
@@ -536,15 +556,15 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 1)
       fence_before();
       __syncthreads();
       if (tid == 0 && !failed) {
-        tma_store_tile<T, D>(&maps.map[3], sm + LY::GM, prm.lo, prm, n, tile0);
+        tma_store_tile<T, D>(&maps.map[3], sm + LY::VX, prm.lo, prm, n, tile0);
         bulk_commit();
       }
+      if (i + 1 < it.ntiles) load_v(i + 1);
       if (T5_VOTE()) break;
     }
   }
   T5_EPILOGUE
 }
-
 
 // ------------------------------------------------------------------ B1 query backward
 // Per tile (prefix B0, A0 at the tile start as in the forward):
@@ -1017,8 +1037,7 @@ struct BwdKVLayC {
   static constexpr int VX = 0;
   static constexpr int GX = VX + Slot<D>::FLOATS;
   static constexpr int PJX = GX + Slot<D>::FLOATS;      // projQ [TT][16] then projK [TT][16]
-  static constexpr int MM = PJX + 2 * TT * PJ;          // bf16 [TT x TT] masked matrix (hi, lo);
-                                                        // later the dv and dk staging
+  static constexpr int MM = PJX + 2 * TT * PJ;          // dv and dk staging (fp32 [TT x D] each)
   static constexpr int PK = MM + TT * TT;               // bf16 [TT x 2SP] pK (hi | lo)
   static constexpr int WH = PK + TT * SP;               // bf16 [TT x 2SP] W (hi | hi)
   static constexpr int WL = WH + TT * SP;               // bf16 [TT x SP] W lo
@@ -1069,8 +1088,6 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
   bf16* bstl = reinterpret_cast<bf16*>(sm + LY::BSTL);
   bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
   bf16* pt = reinterpret_cast<bf16*>(sm + LY::PT);
-  bf16* mm_hi = reinterpret_cast<bf16*>(sm + LY::MM);
-  bf16* mm_lo = mm_hi + TT * TT;
   float* bsf = sm + LY::BSF;
   double* as = reinterpret_cast<double*>(sm + LY::AS);
   double* a0t = reinterpret_cast<double*>(sm + LY::A0T);
@@ -1317,64 +1334,83 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
         // v and the projections are consumed: the next walk step's
         if (i + 1 < it.ntiles) load_v(i + 1);
         fence_after();
-        // masked MT rows (t >= tau kept)
+        // masked MT and GT rows (t >= tau kept), split to packed bf16 hi / lo
+        // and written back in place as the A operands of the second batch
+        {
+          uint32_t mh[GC / 2], ml[GC / 2], gh[GC / 2], gl[GC / 2];
 #pragma unroll
-        for (int c0 = 0; c0 < GC; c0 += 16) {
-          float g[16];
-          tld16(tlane + LY::C_MT + GC * sub + c0, g);
-          tld_wait();
+          for (int c0 = 0; c0 < GC; c0 += 16) {
+            float g[16];
+            tld16(tlane + LY::C_MT + GC * sub + c0, g);
+            tld_wait();
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (GC * sub + c0 + e < row) g[e] = 0.f;
+            for (int e = 0; e < 16; ++e)
+              if (GC * sub + c0 + e < row) g[e] = 0.f;
 #pragma unroll
-          for (int c8 = 0; c8 < 2; ++c8) {
-            uint4 hi, lo;
-            split8(g + 8 * c8, hi, lo);
-            const int c = (GC * sub + c0) / 8 + c8;
-            put_chunk<TT>(mm_hi, row, c, hi);
-            put_chunk<TT>(mm_lo, row, c, lo);
+            for (int e = 0; e < 16; e += 2) split2(g[e], g[e + 1], mh[(c0 + e) / 2], ml[(c0 + e) / 2]);
+            tld16(tlane + LY::C_GT + GC * sub + c0, g);
+            tld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (GC * sub + c0 + e < row) g[e] = 0.f;
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) split2(g[e], g[e + 1], gh[(c0 + e) / 2], gl[(c0 + e) / 2]);
           }
+          fence_before();
+          __syncthreads();   // every MT / GT column has been read before any is overwritten
+          fence_after();
+#pragma unroll
+          for (int c = 0; c < GC / 2; c += 8) {
+            uint32_t x8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x8[e] = mh[c + e];
+            tst8(tlane + LY::C_MT + GC / 2 * sub + c, x8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x8[e] = ml[c + e];
+            tst8(tlane + LY::C_MT + 64 + GC / 2 * sub + c, x8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x8[e] = gh[c + e];
+            tst8(tlane + LY::C_GT + GC / 2 * sub + c, x8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x8[e] = gl[c + e];
+            tst8(tlane + LY::C_GT + 64 + GC / 2 * sub + c, x8);
+          }
+          tst_wait();
         }
-        fence_async_smem();
         fence_before();
         __syncthreads();
         if (tid == 0 && !failed) {
           fence_after();
+          const bf16* gp[2] = {Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1)};
           // VB += mask'(MT) . W  (block 0: W hi, block 1: W lo; lo.lo dropped)
 #pragma unroll
-          for (int a = 0; a < 2; ++a) {
-            const bf16* mp = a ? mm_lo : mm_hi;
+          for (int a = 0; a < 2; ++a)
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks) {
-              mma(tbase + LY::C_VB, desc<TT>(mp, ks), desc_mn<2 * SP>(wh, ks), idesc_bmn<SP>(), true);
+              mma_ta(tbase + LY::C_VB, tbase + LY::C_MT + 64 * a + 8 * ks, desc_mn<2 * SP>(wh, ks),
+                     idesc_bmn<SP>(), true);
               if (a == 0)
-                mma(tbase + LY::C_VB + SP, desc<TT>(mp, ks), desc_mn<SP>(wl, ks), idesc_bmn<SP>(),
-                    true);
+                mma_ta(tbase + LY::C_VB + SP, tbase + LY::C_MT + 8 * ks, desc_mn<SP>(wl, ks),
+                       idesc_bmn<SP>(), true);
             }
-          }
+          // DV += mask'(GT) . dO
+#pragma unroll
+          for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              if (a + b == 2 || (!F32 && b == 1)) continue;
+#pragma unroll
+              for (int ks = 0; ks < TT / 16; ++ks)
+                mma_ta(tbase + LY::C_DV, tbase + LY::C_GT + 64 * a + 8 * ks, desc_mn<D>(gp[b], ks),
+                       idesc_bmn<D>(), true);
+            }
           { commit(barB); ++issB; }
         }
         T5_WAIT(barB, phB);
         phB ^= 1;
+        // dO is consumed: the next walk step's
+        if (i + 1 < it.ntiles) load_do(i + 1);
         fence_after();
-        // masked GT rows into the (consumed) masked-matrix area
-#pragma unroll
-        for (int c0 = 0; c0 < GC; c0 += 16) {
-          float g[16];
-          tld16(tlane + LY::C_GT + GC * sub + c0, g);
-          tld_wait();
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (GC * sub + c0 + e < row) g[e] = 0.f;
-#pragma unroll
-          for (int c8 = 0; c8 < 2; ++c8) {
-            uint4 hi, lo;
-            split8(g + 8 * c8, hi, lo);
-            const int c = (GC * sub + c0) / 8 + c8;
-            put_chunk<TT>(mm_hi, row, c, hi);
-            put_chunk<TT>(mm_lo, row, c, lo);
-          }
-        }
         // dpK and the hash backward of the keys
 #pragma unroll 1
         for (int a = 0; a < MYG; ++a) {
@@ -1406,18 +1442,6 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
         __syncthreads();
         if (tid == 0 && !failed) {
           fence_after();
-          const bf16* gp[2] = {Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1)};
-          // DV += mask'(GT) . dO
-#pragma unroll
-          for (int a = 0; a < 2; ++a)
-#pragma unroll
-            for (int b = 0; b < 2; ++b) {
-              if (a + b == 2 || (!F32 && b == 1)) continue;
-              const bf16* mp = a ? mm_lo : mm_hi;
-#pragma unroll
-              for (int ks = 0; ks < TT / 16; ++ks)
-                mma(tbase + LY::C_DV, desc<TT>(mp, ks), desc_mn<D>(gp[b], ks), idesc_bmn<D>(), true);
-            }
           // DK = dproj . P (into the consumed MT columns)
           gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DK, dj, dj + TT * PJ, nullptr, 2, pt,
                                             false);
@@ -1425,7 +1449,6 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
         }
         T5_WAIT(barA, phA);
         phA ^= 1;
-        if (i + 1 < it.ntiles) load_do(i + 1);
         fence_after();
         {
           float o[W];
