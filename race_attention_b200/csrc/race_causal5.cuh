@@ -111,11 +111,11 @@ __device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
 // parts (24 significant bits: fp32 accuracy, which the temperature gradient's
 // cancelling sum needs) and multiplied on the tensor core by the planes' three
 // parts (all nine cross products, N = 3 x 16); the fp32 rows leave by a TMA
-// store.  Persistent, two CTAs per SM, the next tile loading while this one
-// is converted.
+// store.  Persistent, two CTAs of 256 threads per SM (two per token), the
+// next tile loading while this one is converted.
 template <int D>
 struct ProjLay {
-  static constexpr int NTH = 1;
+  static constexpr int NTH = 2;                            // threads per token (half a row each)
   static constexpr int NFULL = 2;
   static constexpr int XS = 0;                             // [2] slots: landed, then 3 parts
   static constexpr int PS = XS + 2 * Slot<D, 3>::FLOATS;   // bf16 [3 PJ x D] planes (hi; mid; lo)
@@ -128,14 +128,15 @@ struct ProjLay {
 
 // maps: 0 x (5-D), 1 proj ([N][T][16] float32)
 template <typename T, int D>
-__global__ void __launch_bounds__(TT, 2) k_c5_proj(const Params prm, const __grid_constant__ TmaMaps maps) {
+__global__ void __launch_bounds__(TT * ProjLay<D>::NTH, 2)
+    k_c5_proj(const Params prm, const __grid_constant__ TmaMaps maps) {
   using LY = ProjLay<D>;
+  constexpr int NTH = LY::NTH, W = D / NTH, PW = PJ / NTH;
   constexpr bool F32 = sizeof(T) == 4;
   T5_PROLOGUE
   (void)cur_n;
   (void)L;
   (void)inv_scale;
-  (void)sub;
   bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
   float* stg = sm + LY::STG;
   for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(TT, 2) k_c5_proj(const Params prm, const __gri
     __syncthreads();
     if (m != cur_m) {
       const float* pl = prm.planes + (size_t)m * prm.LK * D;
-      put_stack<PJ, D, 3, TT>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+      put_stack<PJ, D, 3, TT * NTH>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
       cur_m = m;
     }
     auto load = [&](int j) {
@@ -172,11 +173,11 @@ __global__ void __launch_bounds__(TT, 2) k_c5_proj(const Params prm, const __gri
         inflight &= ~(1u << f);
       }
       {
-        float x[D];
-        read_cols<T, D, D>(X, row, 0, x);
+        float x[W];
+        read_cols<T, D, W>(X, row, sub * W, x);
         __syncthreads();
-        put_cols<D, D, F32 ? 3 : 1>(Slot<D, 3>::part(X, 0), Slot<D, 3>::part(X, 1),
-                                    Slot<D, 3>::part(X, 2), row, 0, x);
+        put_cols<D, W, F32 ? 3 : 1>(Slot<D, 3>::part(X, 0), Slot<D, 3>::part(X, 1),
+                                    Slot<D, 3>::part(X, 2), row, sub * W, x);
       }
       fence_async_smem();
       fence_before();
@@ -192,11 +193,11 @@ __global__ void __launch_bounds__(TT, 2) k_c5_proj(const Params prm, const __gri
       phA ^= 1;
       fence_after();
       {
-        float pr[PJ];
-        tld_sum<PJ, 3>(tlane, PJ, pr);
-        float4* dst = reinterpret_cast<float4*>(stg + row * PJ);
+        float pr[PW];
+        tld_sum<PW, 3>(tlane + sub * PW, PJ, pr);
+        float4* dst = reinterpret_cast<float4*>(stg + row * PJ + sub * PW);
 #pragma unroll
-        for (int q4 = 0; q4 < PJ / 4; ++q4)
+        for (int q4 = 0; q4 < PW / 4; ++q4)
           dst[q4] = make_float4(pr[4 * q4], pr[4 * q4 + 1], pr[4 * q4 + 2], pr[4 * q4 + 3]);
       }
       fence_async_smem();
