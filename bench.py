@@ -363,6 +363,10 @@ def run_ours(args):
     # (causal, dtype, normalize): the last is the global-normalised causal mode
     configs = [(False, torch.float32, 0), (True, torch.float32, 0), (False, torch.bfloat16, 0),
                (True, torch.bfloat16, 0), (True, torch.float32, 1)]
+    if args.variants:   # profiling runs: a subset of the variants (the first listed leads)
+        names = {"noncausal_f32": 0, "causal_f32": 1, "noncausal_bf16": 2, "causal_bf16": 3,
+                 "global_f32": 4}
+        configs = [configs[names[v]] for v in args.variants.split(",")]
     results = []
     head = None
     clocks = None
@@ -595,6 +599,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-strong", action="store_true")
     ap.add_argument("--no-shapes", action="store_true")
+    ap.add_argument("--variants", default="",
+                    help="comma list of noncausal_f32, causal_f32, noncausal_bf16, causal_bf16, "
+                         "global_f32 (default: all, headline first); for profiling runs")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
             float wv[G::GB];
 #pragma unroll
             for (int b = 0; b < G::GB; ++b)
-              wv[b] = prm.global_norm ? pq[a][b] * rden : pq[a][b] / (av[a][b] + prm.eps);
+              wv[b] = prm.global_norm ? pq[a][b] * rden : __fdividef(pq[a][b], av[a][b] + prm.eps);
 #pragma unroll
             for (int c8 = 0; c8 < G::GB / 8; ++c8) {
               const int c = gi * G::GB / 8 + c8;
@@ -761,7 +761,7 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
               // per-bucket mode keeps 1 / (A + eps) in am, global mode keeps A
 #pragma unroll
               for (int b = 0; b < G::GB; ++b) {
-                if (!prm.global_norm) am[a][b] = 1.f / (am[a][b] + prm.eps);
+                if (!prm.global_norm) am[a][b] = __fdividef(1.f, am[a][b] + prm.eps);
                 wv[a][b] = pq[a][b] * (prm.global_norm ? rden : am[a][b]);
               }
 #pragma unroll
@@ -1043,9 +1043,7 @@ struct BwdKVLayC {
   static constexpr int WH = PK + TT * SP;               // bf16 [TT x 2SP] W (hi | hi)
   static constexpr int WL = WH + TT * SP;               // bf16 [TT x SP] W lo
   static constexpr int BSS = WL + TT * SP / 2;          // bf16 [2SP x D] BS (hi rows; lo rows)
-  static constexpr int BST2 = BSS + SP * D;             // bf16 [D x 2SP] BS^T (hi | hi)
-  static constexpr int BSTL = BST2 + SP * D;            // bf16 [D x SP] BS^T lo
-  static constexpr int DJ = BSTL + SP * D / 2;          // bf16 [TT x PJ] hi, then lo
+  static constexpr int DJ = BSS + SP * D;               // bf16 [TT x PJ] hi, then lo
   static constexpr int PT = DJ + TT * PJ;               // bf16 [2D x PJ] planes^T (hi; lo)
   static constexpr int BSF = PT + D * PJ;               // fp32 [SP][D] suffix at the range end
   static constexpr int AS = BSF + SP * D;               // double [SP] alpha suffix, running
@@ -1085,8 +1083,6 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
   bf16* wh = reinterpret_cast<bf16*>(sm + LY::WH);
   bf16* wl = reinterpret_cast<bf16*>(sm + LY::WL);
   bf16* bss = reinterpret_cast<bf16*>(sm + LY::BSS);
-  bf16* bst2 = reinterpret_cast<bf16*>(sm + LY::BST2);
-  bf16* bstl = reinterpret_cast<bf16*>(sm + LY::BSTL);
   bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
   bf16* pt = reinterpret_cast<bf16*>(sm + LY::PT);
   float* bsf = sm + LY::BSF;
@@ -1098,15 +1094,12 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
   const int64_t tiles_n = (prm.T + TT - 1) / TT;
   for (int i = tid; i < TT * PJ; i += NTHR) reinterpret_cast<float*>(dj)[i] = 0.f;
 
-  // BS operands (BSS, BST2, BSTL) from BS values x(s, d): one (s, d) entry
+  // BS operand from BS values x(s, d): rows s (hi) and SP + s (lo), column d
+  // (K-major B of v . BS^T, MN-major B of pK . BS)
   auto put_bs = [&](int s2, int d, float x) {
     const bf16 h = __float2bfloat16_rn(x);
-    const bf16 l = __float2bfloat16_rn(x - __bfloat162float(h));
     bss[elem<D>(s2, d)] = h;
-    bss[elem<D>(SP + s2, d)] = l;
-    bst2[elem<2 * SP>(d, s2)] = h;
-    bst2[elem<2 * SP>(d, SP + s2)] = h;
-    bstl[elem<SP>(d, s2)] = l;
+    bss[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
   };
 
   for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
@@ -1255,7 +1248,7 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
             if (gi < NG) {
 #pragma unroll
               for (int b = 0; b < G::GB; ++b)
-                wv[a][b] = prm.global_norm ? pq[a][b] * rden : pq[a][b] / (am[a][b] + prm.eps);
+                wv[a][b] = prm.global_norm ? pq[a][b] * rden : __fdividef(pq[a][b], am[a][b] + prm.eps);
 #pragma unroll
               for (int c8 = 0; c8 < G::GB / 8; ++c8) {
                 const int c = gi * G::GB / 8 + c8;
@@ -1304,13 +1297,15 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
             for (int ks = 0; ks < D / 16; ++ks)
               mma(tbase + LY::C_VB, desc<D>(vp[a], ks), desc<D>(bss, ks), idesc<2 * SP>(),
                   a > 0 || ks > 0);
-          // DV = pK . BS
+          // DV = pK . BS (hi.hi, lo.hi, hi.lo; BS rows read MN-major)
 #pragma unroll
-          for (int ks = 0; ks < 2 * SP / 16; ++ks)
-            mma(tbase + LY::C_DV, desc<2 * SP>(pk, ks), desc<2 * SP>(bst2, ks), idesc<D>(), ks > 0);
-#pragma unroll
-          for (int ks = 0; ks < SP / 16; ++ks)
-            mma(tbase + LY::C_DV, desc<2 * SP>(pk, ks), desc<SP>(bstl, ks), idesc<D>(), true);
+          for (int ks = 0; ks < SP / 16; ++ks) {
+            mma(tbase + LY::C_DV, desc<2 * SP>(pk, ks), desc_mn<D>(bss, ks), idesc_bmn<D>(), ks > 0);
+            mma(tbase + LY::C_DV, desc<2 * SP>(pk, SP / 16 + ks), desc_mn<D>(bss, ks), idesc_bmn<D>(),
+                true);
+            mma(tbase + LY::C_DV, desc<2 * SP>(pk, ks), desc_mn<D>(bss, SP / 16 + ks),
+                idesc_bmn<D>(), true);
+          }
           // BS[d][s] += dO^T W over the range (block 0: W hi, block 1: W lo)
 #pragma unroll
           for (int a = 0; a < (F32 ? 2 : 1); ++a)
