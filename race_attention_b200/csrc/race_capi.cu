@@ -8,6 +8,12 @@
 #include "race_b200.h"
 #include "race_launch.h"
 
+#define RACE_TRY(x)                  \
+  do {                               \
+    const int rc_ = (x);             \
+    if (rc_ != RACE_OK) return rc_;  \
+  } while (0)
+
 namespace race {
 namespace {
 
@@ -21,6 +27,8 @@ char g_kernels_last[512] = "";
 char g_kernels_copy[512] = "";
 thread_local char g_kernels[512] = "";
 thread_local int g_api_depth = 0;
+thread_local bool g_bound_valid = false;   // bind_device already ran in this call
+thread_local cudaStream_t g_bound_stream = nullptr;
 
 // Clears the calling thread's log when the outermost entry point of a call
 // starts and publishes it when that entry point returns.
@@ -29,6 +37,7 @@ struct ApiScope {
     if (g_api_depth++ == 0) {
       g_kernels[0] = '\0';
       g_cuda_err[0] = '\0';
+      g_bound_valid = false;
     }
   }
   ~ApiScope() {
@@ -52,6 +61,24 @@ int cuda_fail(cudaError_t e) {
   std::snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", cudaGetErrorName(e),
                 cudaGetErrorString(e));
   return RACE_ERR_CUDA;
+}
+
+// The caller's stream decides the device.  This library carries its own
+// (static) CUDA runtime, whose per-thread current device is not the caller
+// runtime's, and threads that only ever ran the caller's runtime (a
+// framework's autograd worker, for one) may have no current driver context
+// at all -- which the tensor-map encoder needs.  So every entry point makes
+// the stream's device current (cudaSetDevice also binds its primary context).
+int bind_device(cudaStream_t stream) {
+  if (g_bound_valid && g_bound_stream == stream) return RACE_OK;
+  int dev = -1;
+  cudaError_t e = cudaStreamGetDevice(stream, &dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  g_bound_valid = true;
+  g_bound_stream = stream;
+  return RACE_OK;
 }
 
 int sm_count() {
@@ -565,6 +592,7 @@ const char* kernel_name(KernelId id) {
 
 int launch(const race_desc_t* d, const Call& c, KernelId id, cudaStream_t stream,
            const char* note = nullptr) {
+  RACE_TRY(bind_device(stream));
   KernelInfo ki;
   const int K = d->num_bits, sp = c.plan.spad;
   bool ok;
@@ -666,6 +694,7 @@ int post(cudaStream_t) {
 }
 
 int sum_partials(const Call& c, float* out, cudaStream_t stream) {
+  RACE_TRY(bind_device(stream));
   log_kernel("sum_partials");
   dim3 grid((c.plan.SS + 31) / 32, c.plan.N), block(32, 32);
   k_sum_partials<<<grid, block, 0, stream>>>(c.part, c.plan.P, c.plan.SS, out);
@@ -673,6 +702,7 @@ int sum_partials(const Call& c, float* out, cudaStream_t stream) {
 }
 
 int chunk_scan(const Call& c, float* slots, int reverse, float* total, cudaStream_t stream) {
+  RACE_TRY(bind_device(stream));
   log_kernel("chunk_scan");
   dim3 grid((c.plan.width + 31) / 32, c.plan.N), block(32, 32);
   k_chunk_scan<<<grid, block, 0, stream>>>(slots, c.plan.NC, c.plan.SS, c.plan.width, reverse,
@@ -681,6 +711,7 @@ int chunk_scan(const Call& c, float* slots, int reverse, float* total, cudaStrea
 }
 
 int dscale_final(const Call& c, int count, float* dscale, int accumulate, cudaStream_t stream) {
+  RACE_TRY(bind_device(stream));
   log_kernel("dscale_final");
   k_dscale_final<<<1, 1024, 0, stream>>>(c.dscale_part, count, c.prm.scale, dscale, accumulate);
   return post(stream);
@@ -700,6 +731,7 @@ void c5_pointers(Call& c, const float* state, const float* gstate, int64_t T) {
 
 int zero_fill(void* p, size_t bytes, cudaStream_t stream) {
   if (bytes == 0 || p == nullptr) return RACE_OK;
+  RACE_TRY(bind_device(stream));
   const cudaError_t e = cudaMemsetAsync(p, 0, bytes, stream);
   return e == cudaSuccess ? RACE_OK : cuda_fail(e);
 }
@@ -716,6 +748,7 @@ int normalize_into(const race_desc_t* d, const Call& c, race_tensor_t* t, char* 
   const int64_t T = d->tokens, D = d->head_dim;
   const int64_t rows = (int64_t)c.plan.N * T;
   if (rows == 0) return RACE_OK;
+  RACE_TRY(bind_device(stream));
   Layout l;
   fill_layout(l, *t);
   if (d->dtype == RACE_F32)
@@ -744,6 +777,7 @@ int normalize_backward(const race_desc_t* d, const Call& c, const race_tensor_t&
   const int64_t T = d->tokens;
   const int64_t rows = (int64_t)c.plan.N * T;
   if (rows == 0) return RACE_OK;
+  RACE_TRY(bind_device(stream));
   Layout lx, lg;
   fill_layout(lx, x);
   fill_layout(lg, g);
@@ -761,11 +795,6 @@ int normalize_backward(const race_desc_t* d, const Call& c, const race_tensor_t&
   return RACE_OK;
 }
 
-#define RACE_TRY(x)                  \
-  do {                               \
-    const int rc_ = (x);             \
-    if (rc_ != RACE_OK) return rc_;  \
-  } while (0)
 
 }  // namespace
 }  // namespace race
@@ -813,6 +842,7 @@ int race_probs(const race_desc_t* desc, race_tensor_t x, const float* planes, co
   RACE_TRY(probs_params(desc, x, planes, scale, &plan, &p));
   if (probs == nullptr) return RACE_ERR_INVALID;
   if (desc->tokens == 0) return RACE_OK;
+  RACE_TRY(bind_device(stream));
   const cudaError_t e =
       launch_probs(false, desc->dtype == RACE_BF16, desc->head_dim, p, probs, nullptr, stream);
   return e == cudaSuccess ? RACE_OK : cuda_fail(e);
@@ -842,6 +872,7 @@ int race_probs_backward(const race_desc_t* desc, race_tensor_t x, const float* p
   }
   fill_layout(p.ldq, dx);
   p.dq = dx.data;
+  RACE_TRY(bind_device(stream));
   float* part = static_cast<float*>(workspace);
   cudaError_t e = launch_probs(true, desc->dtype == RACE_BF16, desc->head_dim, p,
                                const_cast<float*>(dprobs), part, stream);
@@ -1181,6 +1212,7 @@ int race_add_offset(const race_desc_t* desc, float* slots, const float* offset, 
   if (!desc->causal || slots == nullptr || offset == nullptr) return RACE_ERR_INVALID;
   const int64_t total = (int64_t)p.N * p.NC * p.width;
   if (total == 0) return RACE_OK;
+  RACE_TRY(bind_device(stream));
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4096);
   k_add_offset<<<blocks, 256, 0, stream>>>(slots, offset, p.NC, p.SS, p.width, total);
   return post(stream);
@@ -1227,6 +1259,7 @@ extern "C" int race_forward_static(const race_desc_t* desc, race_tensor_t q, rac
   RACE_TRY(race_query(desc, &sz));
   const size_t state_bytes = (sz.state_bytes + 255) / 256 * 256;
   if (state_bytes + sz.workspace_bytes > RACE_STATIC_SCRATCH_BYTES) return RACE_ERR_TOO_LARGE;
+  RACE_TRY(bind_device(stream));   // the array's address is per device
   float* base = nullptr;
   RACE_TRY(static_scratch(&base));
   float* state = base;
@@ -1238,6 +1271,7 @@ extern "C" int race_forward_static(const race_desc_t* desc, race_tensor_t q, rac
 extern "C" int race_device_status(const void* workspace, size_t workspace_bytes,
                                   uint32_t* status, cudaStream_t stream) {
   if (status == nullptr) return RACE_ERR_INVALID;
+  RACE_TRY(bind_device(stream));
   if (workspace == nullptr) {   // the allocation-free forward's array
     float* base = nullptr;
     RACE_TRY(static_scratch(&base));

@@ -31,13 +31,22 @@ def _data():
     return q, k, v, dout, planes
 
 
+def _log(rank, *a):
+    import sys
+    print(f"[rank {rank}]", *a, file=sys.stderr, flush=True)
+
+
 def _worker(rank, world, port, outdir):
+    import datetime
+
     import torch.distributed as dist
     from race_attention_b200 import race_attention
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
-                            device_id=torch.device("cuda", rank))
+                            device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=120))
+    _log(rank, "process group up")
     try:
         q, k, v, dout, planes = _data()
         lo, hi = T * rank // world, T * (rank + 1) // world
@@ -53,6 +62,7 @@ def _worker(rank, world, port, outdir):
             f = lambda x: x.detach().squeeze(3).squeeze(0).double().cpu().numpy()
             np.savez(os.path.join(outdir, f"r{rank}_c{int(causal)}.npz"), out=f(out),
                      dq=f(qt.grad), dk=f(kt.grad), dv=f(vt.grad), ds=float(sc.grad))
+            _log(rank, "race_attention done, causal =", causal)
         # the host-buffer pipeline, sharded the same way (non-causal)
         from race_attention_b200.streaming import fwd_bwd_host
         h = lambda a: torch.tensor(a[:, lo:hi]).unsqueeze(0).unsqueeze(3).contiguous().pin_memory()
@@ -63,6 +73,11 @@ def _worker(rank, world, port, outdir):
         np.savez(os.path.join(outdir, f"r{rank}_host.npz"), out=g(out), dq=g(dq), dk=g(dk),
                  dv=g(dv), ds=float(ds))
         torch.cuda.synchronize()
+        _log(rank, "host pipeline done")
+    except BaseException:
+        import traceback
+        _log(rank, traceback.format_exc())
+        raise
     finally:
         dist.destroy_process_group()
 
