@@ -215,17 +215,21 @@ class Layer:
 
 
 # Measured DRAM bytes (read + write) of the dominant phase's main kernel per
-# launch at 2^18 tokens, from
-#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
-#       --clock-control none python bench.py --steps 2 --warmup 3 --no-e2e --no-cpu
-#       --tokens 262144
-TRAFFIC_2P18 = {
-    (False, "f32", "backward_kv"): 216.0e6,
-    (False, "f32", "backward_q"): 169.4e6,
-    (False, "bf16", "backward_kv"): 86.0e6,
-    (False, "bf16", "backward_q"): 72.1e6,
-    (True, "f32", "backward_kv"): 396.3e6,
-    (True, "bf16", "backward_kv"): 197.7e6,
+# launch and token.  fp32 entries: one step captured at 2^19 tokens with
+#   ncu --set full --clock-control none -k regex:k_t5_ (or k_c5_) python bench.py
+#       --variants noncausal_f32 (or causal_f32) --tokens 524288 --steps 2 --warmup 3
+#       --no-e2e --no-cpu --no-strong --no-shapes
+# bf16 entries: ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,
+# dram__bytes_write.sum --clock-control none python bench.py --steps 2 --warmup 3
+# --no-e2e --no-cpu --tokens 262144 (2^18 tokens).
+TRAFFIC_PER_TOKEN = {
+    (False, "f32", "backward_kv"): (268.6e6 + 217.9e6) / 2 ** 19,
+    (False, "f32", "backward_q"): (268.5e6 + 107.0e6) / 2 ** 19,
+    (False, "bf16", "backward_kv"): 86.0e6 / 2 ** 18,
+    (False, "bf16", "backward_q"): 72.1e6 / 2 ** 18,
+    (True, "f32", "backward_kv"): (380.5e6 + 227.4e6) / 2 ** 19,
+    (True, "f32", "backward_q"): (337.6e6 + 148.5e6) / 2 ** 19,
+    (True, "bf16", "backward_kv"): 197.7e6 / 2 ** 18,
 }
 
 
@@ -394,15 +398,15 @@ def run_ours(args):
             rec["phases_ms"] = ph
             dom = max(ph, key=ph.get)
             ach = pb[dom] * args.tokens / (ph[dom] / 1e3) / 1e9
-            tr = None if norm else TRAFFIC_2P18.get((causal, rec["dtype"], dom))
+            tr = None if norm else TRAFFIC_PER_TOKEN.get((causal, rec["dtype"], dom))
             rec["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak,
                                "unit": "GB/s", "frac": ach / peak,
-                               "traffic": None if tr is None else tr * args.tokens / 2 ** 18,
+                               "traffic": None if tr is None else tr * args.tokens,
                                "peak_kind": peak_kind}
             if tr is not None:
                 rec["roofline"]["traffic_note"] = (
-                    "DRAM read+write bytes per launch from one ncu capture at 2^18 tokens, "
-                    "scaled by tokens; reads equal the algorithmic bytes, writes of the last "
+                    "DRAM read+write bytes per launch from one ncu capture at 2^19 (fp32) or "
+                    "2^18 (bf16) tokens, scaled by tokens; reads equal the algorithmic bytes, writes of the last "
                     "tiles are still in L2 when a launch ends")
         rec["gpu_launches_per_step"] = layer.kernels_per_step()
         results.append(rec)
