@@ -1495,6 +1495,7 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
 #undef T5_VOTE
 #undef T5_PROLOGUE
 #undef T5_EPILOGUE
+#undef T5_STAGE_DRAIN
 
 }  // namespace c5
 }  // namespace race

@@ -111,21 +111,63 @@ __host__ __device__ constexpr uint32_t idesc64_mn() {
          ((uint32_t)(64 >> 4) << 24);
 }
 
+// Landed bf16 tiles used in place (D = 64: one 128-byte row per token, the
+// copy engine's 128-byte swizzle, 1 KB aligned slots).  K-major: the row is
+// the K axis and fits one swizzle atom, 8-row groups 1024 B apart (stride
+// byte offset), a K = 16 step moves the start 32 B inside the atom.
+__device__ __forceinline__ uint64_t desc_sw128(const void* base, int ks) {
+  const uint32_t a = saddr(base) + ks * 32;
+  uint64_t d = (uint64_t)((a >> 4) & 0x3fff);
+  d |= (uint64_t)1 << 16;                  // leading byte offset (unused inside one atom)
+  d |= (uint64_t)(1024 >> 4) << 32;        // stride byte offset: next 8 rows
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;                  // 128-byte swizzle
+  return d;
+}
+// MN-major: the row holds the 64 MN elements (one atom), K runs over the
+// tokens; 8-token groups 1024 B apart (stride byte offset), a K = 16 step is
+// 16 rows = 2048 B.
+__device__ __forceinline__ uint64_t desc_sw128_mn(const void* base, int ks) {
+  const uint32_t a = saddr(base) + ks * 2048;
+  uint64_t d = (uint64_t)((a >> 4) & 0x3fff);
+  d |= (uint64_t)1 << 16;                  // leading byte offset (one atom along MN)
+  d |= (uint64_t)(1024 >> 4) << 32;        // stride byte offset: next 8 tokens
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+// MN-major A operand over a tile's tokens: a converted part, or (SW) the landed tile
+template <int C, bool SW>
+__device__ __forceinline__ uint64_t desc_a_mn(const void* base, int ks) {
+  if constexpr (SW) {
+    return desc_sw128_mn(base, ks);
+  } else {
+    return desc_mn<C>(base, ks);
+  }
+}
+
 // Split product D = A . B^T with K = 16 KS.  A is given as NA bf16 parts
 // (a[0] + a[1] + ..., the later ones nullptr-free), B as BP parts stacked
 // along its rows ([B0; B1; ...], BP*N rows).  Column block j of D receives
 // sum_i A_i . B_j^T -- every part product, since an instruction costs the
 // same at N and BP*N.  The caller adds the BP column blocks.
-template <int N, int BP, int KS, int CA, int CB>
+// SW: A is one landed bf16 tile read in place (desc_sw128).
+template <int N, int BP, int KS, int CA, int CB, bool SW = false>
 __device__ __forceinline__ void gemm_parts(uint32_t d, const bf16* a0, const bf16* a1,
                                            const bf16* a2, int na, const bf16* b, bool acc) {
-  const bf16* a[3] = {a0, a1, a2};
+  if constexpr (SW) {
 #pragma unroll
-  for (int i = 0; i < 3; ++i) {
-    if (i < na) {
+    for (int ks = 0; ks < KS; ++ks)
+      mma(d, desc_sw128(a0, ks), desc<CB>(b, ks), idesc<BP * N>(), acc || ks > 0);
+  } else {
+    const bf16* a[3] = {a0, a1, a2};
 #pragma unroll
-      for (int ks = 0; ks < KS; ++ks)
-        mma(d, desc<CA>(a[i], ks), desc<CB>(b, ks), idesc<BP * N>(), acc || i > 0 || ks > 0);
+    for (int i = 0; i < 3; ++i) {
+      if (i < na) {
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks)
+          mma(d, desc<CA>(a[i], ks), desc<CB>(b, ks), idesc<BP * N>(), acc || i > 0 || ks > 0);
+      }
     }
   }
 }
@@ -218,6 +260,14 @@ __device__ __forceinline__ void tld8(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tld4(uint32_t taddr, float* v) {
+  uint32_t r[4];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tld1(uint32_t taddr, float& v) {
   uint32_t r;
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
@@ -251,9 +301,15 @@ template <int GK, int NB>
 __device__ __forceinline__ void tld_group(uint32_t taddr, int c0, float (&out)[GK]) {
   float v[NB][GK];
 #pragma unroll
-  for (int b = 0; b < NB; ++b)
+  for (int b = 0; b < NB; ++b) {
+    if constexpr (GK % 4 == 0) {   // c0 is then a multiple of 4: x4 loads
 #pragma unroll
-    for (int k = 0; k < GK; ++k) tld1(taddr + b * PJ + c0 + k, v[b][k]);
+      for (int k = 0; k < GK; k += 4) tld4(taddr + b * PJ + c0 + k, &v[b][k]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < GK; ++k) tld1(taddr + b * PJ + c0 + k, v[b][k]);
+    }
+  }
   tld_wait();
 #pragma unroll
   for (int k = 0; k < GK; ++k) {
@@ -261,6 +317,20 @@ __device__ __forceinline__ void tld_group(uint32_t taddr, int c0, float (&out)[G
 #pragma unroll
     for (int b = 1; b < NB; ++b) x += v[b][k];
     out[k] = x;
+  }
+}
+
+// Conversion barrier.  At D = 64 the in-place conversion of a landed tile
+// (box layout -> K-major bf16 parts) moves data only within 8-row groups, so
+// only the NTH warps that hold rows [32 q, 32 q + 32) (warps q, q + 4, ...)
+// must have read before any of them writes: a named barrier per row quarter
+// (ids 1..4) instead of the CTA-wide one.  Other widths cross row groups.
+template <int D, int NTH>
+__device__ __forceinline__ void convert_sync(int warp) {
+  if constexpr (D == 64) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + (warp & 3)), "n"(32 * NTH) : "memory");
+  } else {
+    __syncthreads();
   }
 }
 
@@ -512,7 +582,7 @@ __device__ __forceinline__ void group_probs(const float* proj, int l0, int L, fl
       h[u * K + k] = hh;
       const float uu = hh * inv_scale;
       const float ex = __expf(-2.f * fabsf(uu));
-      const float rc = __frcp_rn(1.f + ex);
+      const float rc = tiles::rcp_approx(1.f + ex);
       sp[k] = uu >= 0.f ? rc : ex * rc;
       sn[k] = uu >= 0.f ? ex * rc : rc;
     }
@@ -695,6 +765,14 @@ struct BwdKVLay {
   bool failed = false;                                                       \
   int cur_n = -1, cur_m = -1;
 
+// Before staging into a slot that a bulk store issued by thread 0 may still
+// be reading: thread 0 waits for its stores' reads, then the CTA.
+#define T5_STAGE_DRAIN()                 \
+  do {                                  \
+    if (tid == 0) bulk_wait_read();     \
+    __syncthreads();                    \
+  } while (0)
+
 // On the way out every thread waits (full poll count) for the tiles it saw
 // issued into its slots, thread 0 for its bulk stores and for the last MMA
 // commit of each barrier (MMAs complete in issue order, and at most one
@@ -727,6 +805,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
   constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
   using G = Groups<K>;
   constexpr bool F32 = sizeof(T) == 4;
+  constexpr bool DIRECT = !F32 && D == 64;   // bf16 tiles are MMA operands as they land
   T5_PROLOGUE
   bf16* pq = reinterpret_cast<bf16*>(sm + LY::PQ);
   bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
@@ -787,10 +866,10 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
         phF ^= 1u << (i & 1);
         inflight &= ~(1u << (i & 1));
       }
-      {
+      if constexpr (!DIRECT) {   // bf16 at D = 64: the landed tiles are the operands
         float x[W];
         read_cols<T, D, W>(X, row, sub * W, x);
-        __syncthreads();
+        convert_sync<D, NTH>(warp);
         put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(X, 0), Slot<D>::part(X, 1), nullptr, row,
                                     sub * W, x);
       }
@@ -799,7 +878,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       __syncthreads();
       if (tid == 0 && !failed) {
         fence_after();
-        gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(X, 0),
+        gemm_parts<PJ, 2, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(X, 0),
                                         Slot<D>::part(X, 1), nullptr, F32 ? 2 : 1, ps, false);
         { commit(barA); ++issA; }
       }
@@ -833,6 +912,9 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       }
       if (T5_VOTE()) break;
     }
+    // the last tile leaves through its own slot, which the store of the
+    // tile before may still be reading
+    T5_STAGE_DRAIN();
     if (!failed)
       store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT,
                  sm + LY::QX + ((it.ntiles - 1) & 1) * Slot<D>::FLOATS);
@@ -879,6 +961,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
   constexpr int NG = SP / G::GB;                       // bucket groups
   constexpr int MYG = (NG + NTH - 1) / NTH;            // groups per thread (at most)
   constexpr bool F32 = sizeof(T) == 4;
+  constexpr bool DIRECT = !F32 && D == 64;   // bf16 tiles are MMA operands as they land
   T5_PROLOGUE
   (void)cur_n;
   bf16* pk3 = reinterpret_cast<bf16*>(sm + LY::PK3);
@@ -941,7 +1024,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
       landed(0);
       landed(1);
       const bool valid = tile0 + row < it.t1;
-      {
+      if constexpr (!DIRECT) {   // bf16 at D = 64: the landed tiles are the operands
         float x[W], y[W];
         read_cols<T, D, W>(KXt, row, sub * W, x);
         read_cols<T, D, W>(VXt, row, sub * W, y);
@@ -949,7 +1032,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
 #pragma unroll
           for (int c = 0; c < W; ++c) y[c] = 0.f;
         }
-        __syncthreads();
+        convert_sync<D, NTH>(warp);
         put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), nullptr, row,
                                     sub * W, x);
         put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), vl, row,
@@ -960,7 +1043,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
       __syncthreads();
       if (tid == 0 && !failed) {
         fence_after();
-        gemm_parts<PJ, 2, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
+        gemm_parts<PJ, 2, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
                                         Slot<D>::part(KXt, 1), nullptr, F32 ? 2 : 1, ps, false);
         { commit(barA); ++issA; }
       }
@@ -1010,7 +1093,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
         for (int a = 0; a < (F32 ? 3 : 1); ++a)   // bf16 v is exact in its first part
 #pragma unroll
           for (int ks = 0; ks < TT / 16; ++ks)
-            mma(tbase + LY::C_ST, desc_mn<D>(va[a], ks), desc_mn<3 * SP>(pk3, ks),
+            mma(tbase + LY::C_ST, desc_a_mn<D, DIRECT>(va[a], ks), desc_mn<3 * SP>(pk3, ks),
                 idesc64_mn<3 * SP>(), i > 0 || a > 0 || ks > 0);
         { commit(barB); ++issB; }
       }
@@ -1106,6 +1189,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
   constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
   using G = Groups<K>;
   constexpr bool F32 = sizeof(T) == 4;
+  constexpr bool DIRECT = !F32 && D == 64;   // bf16 tiles are MMA operands as they land
   T5_PROLOGUE
   bf16* pq = reinterpret_cast<bf16*>(sm + LY::PQ);
   bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
@@ -1139,7 +1223,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
         cur_n = n;
       }
       __syncthreads();
-      // dq of tile i-1 leaves through q slot i (its parts are consumed by then)
+      // dq of tile i-1 leaves through a consumed dO slot (or, LATE, the q slot)
       auto store_prev = [&](int64_t tprev, float* stage_slot) {
         T5_WAIT(barB, phB);
         phB ^= 1;
@@ -1182,7 +1266,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
           inflight &= ~(1u << fb);
         }
         const bool valid = tile0 + row < it.t1;
-        {
+        if constexpr (!DIRECT) {   // bf16 at D = 64: the landed tiles are the operands
           float x[W], y[W];
           read_cols<T, D, W>(QXt, row, sub * W, x);
           read_cols<T, D, W>(GXt, row, sub * W, y);
@@ -1190,7 +1274,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
 #pragma unroll
             for (int c = 0; c < W; ++c) y[c] = 0.f;
           }
-          __syncthreads();
+          convert_sync<D, NTH>(warp);
           // hi | mid in place, the third part beside (read only by this tile's
           // projection MMAs, which finish before the next conversion)
           put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(QXt, 0), Slot<D>::part(QXt, 1), ql, row,
@@ -1205,15 +1289,21 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
           fence_after();
           // projections in three parts on both sides: they feed the
           // temperature gradient, a sum with heavy cancellation
-          gemm_parts<PJ, 3, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(QXt, 0),
+          gemm_parts<PJ, 3, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(QXt, 0),
                                           Slot<D>::part(QXt, 1), ql, F32 ? 3 : 1, ps, false);
-          gemm_parts<SP, 3, D / 16, D, D>(tbase + LY::C_DPQ, Slot<D>::part(GXt, 0),
+          gemm_parts<SP, 3, D / 16, D, D, DIRECT>(tbase + LY::C_DPQ, Slot<D>::part(GXt, 0),
                                           Slot<D>::part(GXt, 1), nullptr, F32 ? 2 : 1, et, false);
           { commit(barA); ++issA; }
         }
+        // Up to 32 buckets dq of tile i-1 leaves through dO slot i-1 (free
+        // once its dE MMAs are done; the next load into it waits for the
+        // store's reads) while the tensor core forms tile i's projections;
+        // LATE through the q slot once those are done.
+        if (!LY::LATE && i > 0)
+          store_prev(tile0 - TT, sm + LY::GX + ((i + LY::NFULL - 1) % LY::NFULL) * Slot<D>::FLOATS);
         T5_WAIT(barA, phA);   // also covers the previous tile's dE / dq MMAs
         phA ^= 1;
-        if (i > 0) store_prev(tile0 - TT, QXt);
+        if (LY::LATE && i > 0) store_prev(tile0 - TT, QXt);
         // LATE: the q slot is free (projections done, dq(i-1) read by its
         // store) and so is dO slot i+1 (dE(i-1) done)
         if (LY::LATE && i + 1 < it.ntiles) load(i + 1);
@@ -1273,7 +1363,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
           for (int a = 0; a < (F32 ? 2 : 1); ++a)
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks)
-              mma(tbase + LY::C_DE, desc_mn<D>(Slot<D>::part(GXt, a), ks), desc_mn<2 * SP>(pq, ks),
+              mma(tbase + LY::C_DE, desc_a_mn<D, DIRECT>(Slot<D>::part(GXt, a), ks), desc_mn<2 * SP>(pq, ks),
                   idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
           gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DQ, dj, dj + TT * PJ, nullptr, 2, pt,
                                             false);
@@ -1281,6 +1371,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
         }
         if (T5_VOTE()) break;
       }
+      T5_STAGE_DRAIN();   // LATE: the store of the tile before may still read the q slot
       if (!failed)
         store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT,
                    sm + LY::QX + ((it.ntiles - 1) % LY::NQ) * Slot<D>::FLOATS);
@@ -1332,6 +1423,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
   constexpr int SP = LY::SP, NTH = LY::NTH, NTHR = TT * NTH, W = D / NTH;
   using G = Groups<K>;
   constexpr bool F32 = sizeof(T) == 4;
+  constexpr bool DIRECT = !F32 && D == 64;   // bf16 tiles are MMA operands as they land
   T5_PROLOGUE
   bf16* pk = reinterpret_cast<bf16*>(sm + LY::PK);
   bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
@@ -1426,11 +1518,11 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
           phF ^= 1u << fb;
           inflight &= ~(1u << fb);
         }
-        {
+        if constexpr (!DIRECT) {   // bf16 at D = 64: the landed tiles are the operands
           float x[W], y[W];
           read_cols<T, D, W>(KXt, row, sub * W, x);
           read_cols<T, D, W>(VXt, row, sub * W, y);
-          __syncthreads();
+          convert_sync<D, NTH>(warp);
           // hi | mid in place, the third part beside (read only by this tile's
           // projection / dpK MMAs, which finish before the next conversion)
           put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), kl, row,
@@ -1447,9 +1539,9 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
           // three parts on both sides: the projections feed the temperature
           // gradient (a sum with heavy cancellation), and where v matches a
           // bucket's mean (tiny buckets) v . dB and dA cancel to far below |v| |dB|
-          gemm_parts<PJ, 3, D / 16, D, D>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
+          gemm_parts<PJ, 3, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
                                           Slot<D>::part(KXt, 1), kl, F32 ? 3 : 1, ps, false);
-          gemm_parts<SP, 3, D / 16, D, D>(tbase + LY::C_DPK, Slot<D>::part(VXt, 0),
+          gemm_parts<SP, 3, D / 16, D, D, DIRECT>(tbase + LY::C_DPK, Slot<D>::part(VXt, 0),
                                           Slot<D>::part(VXt, 1), vl, F32 ? 3 : 1, db, false);
           { commit(barA); ++issA; }
         }
@@ -1504,6 +1596,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         }
         if (T5_VOTE()) break;
       }
+      T5_STAGE_DRAIN();   // the stores of the tile before may still read these slots
       if (!failed) {
         const int lt = (it.ntiles - 1) % LY::NS;
         store_prev(it.t0 + (int64_t)(it.ntiles - 1) * TT, sm + LY::KX + lt * Slot<D>::FLOATS,

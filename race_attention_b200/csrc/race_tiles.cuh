@@ -58,12 +58,20 @@ __device__ __forceinline__ void cp_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// Hardware approximate reciprocal (one MUFU op, relative error ~2^-23);
+// the hash only takes it of 1 + e with e in [0, 1].
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // tanh(x) = sign(x) (1 - e) / (1 + e), e = exp(-2|x|) (the exponential
 // identity of the hyperbolic tangent); absolute error ~1e-7, which is all the
 // soft hash needs since it only uses tanh(x)/scale as a logit.
 __device__ __forceinline__ float tanh_exp(float x) {
   const float e = __expf(-2.f * fabsf(x));
-  const float t = (1.f - e) * __frcp_rn(1.f + e);
+  const float t = (1.f - e) * rcp_approx(1.f + e);
   return copysignf(t, x);
 }
 
