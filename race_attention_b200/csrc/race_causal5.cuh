@@ -104,6 +104,30 @@ __device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
   split2(v[6], v[7], hi.w, lo.w);
 }
 
+// the 8 floats as one 16-byte chunk of bf16 (single-part operands)
+__device__ __forceinline__ void cvt8(const float* v, uint4& hi) {
+  uint32_t* h = &hi.x;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+    h[j] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+}
+
+// Writes 8 values as the hi chunk c8 (and, with two parts, the lo chunk
+// c8 + LOFF) of row r of an operand with C columns.
+template <int C, int LOFF, bool ONE>
+__device__ __forceinline__ void put_parts8(bf16* op, int r, int c8, const float* v) {
+  uint4 hi, lo;
+  if constexpr (ONE) {
+    cvt8(v, hi);
+  } else {
+    split8(v, hi, lo);
+    put_chunk<C>(op, r, c8 + LOFF, lo);
+  }
+  put_chunk<C>(op, r, c8, hi);
+}
+
 // ------------------------------------------------------------------ projections
 // proj[n][t][j] = x[n][t] . planes[m][j] (j < L K; columns up to 16 are zero)
 // for one of q or k: the soft hash of every causal kernel reads these, so q and
@@ -285,6 +309,11 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
   constexpr int NG = SP / G::GB;
   constexpr int MYG = (NG + NTH - 1) / NTH;
   constexpr int GC = TT / NTH;                         // G columns per thread
+  // bf16 inputs: W, pK, B0 and the masked G as one bf16 part each (the
+  // path's bf16 tolerance), fp32: two (hi + lo)
+  constexpr bool ONE = sizeof(T) == 2;
+  constexpr int KP = ONE ? SP : 2 * SP;                // K extent of the W / pK / B0 products
+  constexpr bool DIRECT = ONE && D == 64;              // the landed v tile is the MMA operand
   T5_PROLOGUE
   (void)cur_m;
   (void)cur_n;
@@ -312,10 +341,7 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = b0f[(s8 * 8 + e) * D + tid];
-        uint4 hi, lo;
-        split8(v, hi, lo);
-        put_chunk<2 * SP>(b0, tid, s8, hi);
-        put_chunk<2 * SP>(b0, tid, SP / 8 + s8, lo);
+        put_parts8<2 * SP, SP / 8, ONE>(b0, tid, s8, v);
       }
     }
     auto load_p = [&](int j) {
@@ -360,7 +386,7 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
       const bool valid = tile0 + row < it.t1;
       {
         float y[W];
-        read_cols<T, D, W>(VXt, row, sub * W, y);
+        if constexpr (!DIRECT) read_cols<T, D, W>(VXt, row, sub * W, y);
         float pq[MYG][G::GB], pkv[MYG][G::GB];
 #pragma unroll
         for (int a = 0; a < MYG; ++a) {
@@ -383,8 +409,9 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
         }
         __syncthreads();   // v and the projections read
         if (i + 1 < it.ntiles) load_p(i + 1);
-        put_cols<D, W, sizeof(T) == 4 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1),
-                                               nullptr, row, sub * W, y);
+        if constexpr (!DIRECT)
+          put_cols<D, W, sizeof(T) == 4 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1),
+                                                 nullptr, row, sub * W, y);
         float incl[MYG][G::GB];
 #pragma unroll
         for (int a = 0; a < MYG; ++a) {
@@ -431,14 +458,18 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
 #pragma unroll
             for (int c8 = 0; c8 < G::GB / 8; ++c8) {
               const int c = gi * G::GB / 8 + c8;
-              uint4 hi, lo;
-              split8(pkv[a] + 8 * c8, hi, lo);
-              put_chunk<2 * SP>(pk, row, c, hi);
-              put_chunk<2 * SP>(pk, row, SP / 8 + c, lo);
-              split8(wv + 8 * c8, hi, lo);
-              put_chunk<2 * SP>(wh, row, c, hi);
-              put_chunk<2 * SP>(wh, row, SP / 8 + c, hi);
-              put_chunk<SP>(wl, row, c, lo);
+              put_parts8<2 * SP, SP / 8, ONE>(pk, row, c, pkv[a] + 8 * c8);
+              if constexpr (ONE) {
+                uint4 hi;
+                cvt8(wv + 8 * c8, hi);
+                put_chunk<2 * SP>(wh, row, c, hi);
+              } else {
+                uint4 hi, lo;
+                split8(wv + 8 * c8, hi, lo);
+                put_chunk<2 * SP>(wh, row, c, hi);
+                put_chunk<2 * SP>(wh, row, SP / 8 + c, hi);
+                put_chunk<SP>(wl, row, c, lo);
+              }
             }
           }
         }
@@ -449,17 +480,21 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
       if (tid == 0 && !failed) {
         fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 2 * SP / 16; ++ks)
+        for (int ks = 0; ks < KP / 16; ++ks)
           mma(tbase + LY::C_G, desc<2 * SP>(wh, ks), desc<2 * SP>(pk, ks), idesc<TT>(), ks > 0);
+        if constexpr (!ONE) {
 #pragma unroll
-        for (int ks = 0; ks < SP / 16; ++ks)
-          mma(tbase + LY::C_G, desc<SP>(wl, ks), desc<2 * SP>(pk, ks), idesc<TT>(), true);
+          for (int ks = 0; ks < SP / 16; ++ks)
+            mma(tbase + LY::C_G, desc<SP>(wl, ks), desc<2 * SP>(pk, ks), idesc<TT>(), true);
+        }
 #pragma unroll
-        for (int ks = 0; ks < 2 * SP / 16; ++ks)
+        for (int ks = 0; ks < KP / 16; ++ks)
           mma(tbase + LY::C_OUT, desc<2 * SP>(wh, ks), desc<2 * SP>(b0, ks), idesc<D>(), ks > 0);
+        if constexpr (!ONE) {
 #pragma unroll
-        for (int ks = 0; ks < SP / 16; ++ks)
-          mma(tbase + LY::C_OUT, desc<SP>(wl, ks), desc<2 * SP>(b0, ks), idesc<D>(), true);
+          for (int ks = 0; ks < SP / 16; ++ks)
+            mma(tbase + LY::C_OUT, desc<SP>(wl, ks), desc<2 * SP>(b0, ks), idesc<D>(), true);
+        }
         { commit(barA); ++issA; }
       }
       if (sub == 0 && tid < SP) {
@@ -471,56 +506,90 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
       phA ^= 1;
       fence_after();
       {
-        // masked G row (columns [GC sub, GC sub + GC)), split to packed bf16 pairs
-        uint32_t hw[GC / 2], lw[GC / 2];
+        if constexpr (ONE) {
+          // masked G row as packed bf16 pairs, written over the first half
+          // of the thread's own columns (no other thread reads them)
+          uint32_t hw[GC / 2];
 #pragma unroll
-        for (int c0 = 0; c0 < GC; c0 += 16) {
-          float g[16];
-          tld16(tlane + LY::C_G + GC * sub + c0, g);
-          tld_wait();
+          for (int c0 = 0; c0 < GC; c0 += 16) {
+            float g[16];
+            tld16(tlane + LY::C_G + GC * sub + c0, g);
+            tld_wait();
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (GC * sub + c0 + e > row) g[e] = 0.f;
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) split2(g[e], g[e + 1], hw[(c0 + e) / 2], lw[(c0 + e) / 2]);
-        }
-        fence_before();
-        __syncthreads();   // every G column has been read before any is overwritten
-        fence_after();
-#pragma unroll
-        for (int c = 0; c < GC / 2; c += 8) {
-          uint32_t h8[8], l8[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            h8[e] = hw[c + e];
-            l8[e] = lw[c + e];
+            for (int e = 0; e < 16; e += 2) {
+              const float x0 = GC * sub + c0 + e > row ? 0.f : g[e];
+              const float x1 = GC * sub + c0 + e + 1 > row ? 0.f : g[e + 1];
+              const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+              hw[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
           }
-          tst8(tlane + LY::C_G + GC / 2 * sub + c, h8);
-          tst8(tlane + LY::C_G + 64 + GC / 2 * sub + c, l8);
+#pragma unroll
+          for (int c = 0; c < GC / 2; c += 8) {
+            uint32_t h8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) h8[e] = hw[c + e];
+            tst8(tlane + LY::C_G + GC * sub + c, h8);
+          }
+          tst_wait();
+        } else {
+          // masked G row (columns [GC sub, GC sub + GC)), split to packed bf16 pairs
+          uint32_t hw[GC / 2], lw[GC / 2];
+  #pragma unroll
+          for (int c0 = 0; c0 < GC; c0 += 16) {
+            float g[16];
+            tld16(tlane + LY::C_G + GC * sub + c0, g);
+            tld_wait();
+  #pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (GC * sub + c0 + e > row) g[e] = 0.f;
+  #pragma unroll
+            for (int e = 0; e < 16; e += 2) split2(g[e], g[e + 1], hw[(c0 + e) / 2], lw[(c0 + e) / 2]);
+          }
+          fence_before();
+          __syncthreads();   // every G column has been read before any is overwritten
+          fence_after();
+  #pragma unroll
+          for (int c = 0; c < GC / 2; c += 8) {
+            uint32_t h8[8], l8[8];
+  #pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              h8[e] = hw[c + e];
+              l8[e] = lw[c + e];
+            }
+            tst8(tlane + LY::C_G + GC / 2 * sub + c, h8);
+            tst8(tlane + LY::C_G + 64 + GC / 2 * sub + c, l8);
+          }
+          tst_wait();
         }
-        tst_wait();
       }
       fence_before();
       __syncthreads();
       if (tid == 0 && !failed) {
         fence_after();
         const bf16* vp[2] = {Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1)};
+        if constexpr (ONE) {   // hi of tokens [GC j, GC j + GC) at columns [GC j, GC j + GC / 2)
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
+          for (int ks = 0; ks < TT / 16; ++ks)
+            mma_ta(tbase + LY::C_OUT, tbase + LY::C_G + GC * (16 * ks / GC) + (16 * ks % GC) / 2,
+                   desc_a_mn<D, DIRECT>(vp[0], ks), idesc_bmn<D>(), true);
+        } else {
 #pragma unroll
-          for (int b = 0; b < 2; ++b) {
-            if (a + b == 2 || (sizeof(T) == 2 && b == 1)) continue;
+          for (int a = 0; a < 2; ++a)
 #pragma unroll
-            for (int ks = 0; ks < TT / 16; ++ks)
-              mma_ta(tbase + LY::C_OUT, tbase + LY::C_G + 64 * a + 8 * ks, desc_mn<D>(vp[b], ks),
-                     idesc_bmn<D>(), true);
-          }
+            for (int b = 0; b < 2; ++b) {
+              if (a + b == 2) continue;
+#pragma unroll
+              for (int ks = 0; ks < TT / 16; ++ks)
+                mma_ta(tbase + LY::C_OUT, tbase + LY::C_G + 64 * a + 8 * ks, desc_mn<D>(vp[b], ks),
+                       idesc_bmn<D>(), true);
+            }
+        }
 #pragma unroll
         for (int a = 0; a < (sizeof(T) == 4 ? 2 : 1); ++a)
 #pragma unroll
           for (int ks = 0; ks < TT / 16; ++ks)
-            mma(tbase + LY::C_ST, desc_mn<D>(vp[a], ks), desc_mn<2 * SP>(pk, ks),
-                idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
+            mma(tbase + LY::C_ST, desc_a_mn<D, DIRECT>(vp[a], ks), desc_mn<2 * SP>(pk, ks),
+                idesc64_mn<KP>(), i > 0 || a > 0 || ks > 0);
         { commit(barB); ++issB; }
       }
       T5_WAIT(barB, phB);
@@ -535,7 +604,7 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
         const int d = 16 * quad + lane;
         float stv[2 * SP];
 #pragma unroll
-        for (int c = 0; c < 2 * SP; c += 8) tld8(tlane + LY::C_ST + c, stv + c);
+        for (int c = 0; c < KP; c += 8) tld8(tlane + LY::C_ST + c, stv + c);
         tld_wait();
         if (lane < 16 && d < D) {
 #pragma unroll
@@ -544,12 +613,9 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const int s = s8 * 8 + e;
-              v[e] = b0f[s * D + d] + stv[s] + stv[SP + s];
+              v[e] = b0f[s * D + d] + stv[s] + (ONE ? 0.f : stv[SP + s]);
             }
-            uint4 hi, lo;
-            split8(v, hi, lo);
-            put_chunk<2 * SP>(b0, d, s8, hi);
-            put_chunk<2 * SP>(b0, d, SP / 8 + s8, lo);
+            put_parts8<2 * SP, SP / 8, ONE>(b0, d, s8, v);
           }
         }
       }
@@ -618,6 +684,11 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
   constexpr int MYG = (NG + NTH - 1) / NTH;
   constexpr int GC = TT / NTH;
   constexpr bool F32 = sizeof(T) == 4;
+  // bf16 inputs: pK, W, B0, the masked M and dproj as one bf16 part each
+  // (the path's bf16 tolerance); fp32: two
+  constexpr bool ONE = !F32;
+  constexpr int KP = ONE ? SP : 2 * SP;                // N extent of the bucket products
+  constexpr bool DIRECT = ONE && D == 64;              // landed v / dO tiles are MMA operands
   T5_PROLOGUE
   (void)cur_n;
   bf16* pk = reinterpret_cast<bf16*>(sm + LY::PK);
@@ -662,7 +733,7 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
         const float x = b0f[e];
         const bf16 h = __float2bfloat16_rn(x);
         b0s[elem<D>(s2, d)] = h;
-        b0s[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
+        if constexpr (!ONE) b0s[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
       }
       auto load = [&](int j) {
         if (failed) return;
@@ -694,8 +765,10 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
         float den = 0.f, rden = 0.f;   // global mode
         {
           float y[W], g[W];
-          read_cols<T, D, W>(VXt, row, sub * W, y);
-          read_cols<T, D, W>(GXt, row, sub * W, g);
+          if constexpr (!DIRECT) {
+            read_cols<T, D, W>(VXt, row, sub * W, y);
+            read_cols<T, D, W>(GXt, row, sub * W, g);
+          }
           float pkv[MYG][G::GB];
 #pragma unroll
           for (int a = 0; a < MYG; ++a) {
@@ -717,10 +790,12 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
             }
           }
           __syncthreads();   // raw tiles read; scan scratch free
-          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), nullptr, row,
-                                      sub * W, y);
-          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1), nullptr, row,
-                                      sub * W, g);
+          if constexpr (!DIRECT) {
+            put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), nullptr, row,
+                                        sub * W, y);
+            put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1), nullptr, row,
+                                        sub * W, g);
+          }
           float incl[MYG][G::GB];
 #pragma unroll
           for (int a = 0; a < MYG; ++a) {
@@ -767,13 +842,8 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
 #pragma unroll
               for (int c8 = 0; c8 < G::GB / 8; ++c8) {
                 const int c = gi * G::GB / 8 + c8;
-                uint4 hi, lo;
-                split8(pkv[a] + 8 * c8, hi, lo);
-                put_chunk<2 * SP>(pk, row, c, hi);
-                put_chunk<2 * SP>(pk, row, SP / 8 + c, lo);
-                split8(wv[a] + 8 * c8, hi, lo);
-                put_chunk<2 * SP>(wp, row, c, hi);
-                put_chunk<2 * SP>(wp, row, SP / 8 + c, lo);
+                put_parts8<2 * SP, SP / 8, ONE>(pk, row, c, pkv[a] + 8 * c8);
+                put_parts8<2 * SP, SP / 8, ONE>(wp, row, c, wv[a] + 8 * c8);
               }
             }
           }
@@ -797,25 +867,25 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
               if (a + b == 2 || (!F32 && a + b > 0)) continue;
 #pragma unroll
               for (int ks = 0; ks < D / 16; ++ks)
-                mma(tbase + LY::C_M, desc<D>(gp[a], ks), desc<D>(vp[b], ks), idesc<TT>(),
-                    a + b > 0 || ks > 0);
+                mma(tbase + LY::C_M, desc_a_k<D, DIRECT>(gp[a], ks), desc_a_k<D, DIRECT>(vp[b], ks),
+                    idesc<TT>(), a + b > 0 || ks > 0);
             }
           // R = dO . B0^T (B0 hi and lo stacked along N)
 #pragma unroll
           for (int a = 0; a < (F32 ? 2 : 1); ++a)
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks)
-              mma(tbase + LY::C_R, desc<D>(gp[a], ks), desc<D>(b0s, ks), idesc<2 * SP>(),
+              mma(tbase + LY::C_R, desc_a_k<D, DIRECT>(gp[a], ks), desc<D>(b0s, ks), idesc<KP>(),
                   a > 0 || ks > 0);
           // ST[d][s] += v^T pK (the next tiles' B0);  WD[d][s] += dO^T W (range total)
 #pragma unroll
           for (int a = 0; a < (F32 ? 2 : 1); ++a)
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks) {
-              mma(tbase + LY::C_ST, desc_mn<D>(vp[a], ks), desc_mn<2 * SP>(pk, ks),
-                  idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
-              mma(tbase + LY::C_WD, desc_mn<D>(gp[a], ks), desc_mn<2 * SP>(wp, ks),
-                  idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
+              mma(tbase + LY::C_ST, desc_a_mn<D, DIRECT>(vp[a], ks), desc_mn<2 * SP>(pk, ks),
+                  idesc64_mn<KP>(), i > 0 || a > 0 || ks > 0);
+              mma(tbase + LY::C_WD, desc_a_mn<D, DIRECT>(gp[a], ks), desc_mn<2 * SP>(wp, ks),
+                  idesc64_mn<KP>(), i > 0 || a > 0 || ks > 0);
             }
           { commit(barA); ++issA; }
         }
@@ -839,11 +909,17 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
             if (GC * sub + c0 + e > row) g[e] = 0.f;
 #pragma unroll
           for (int c8 = 0; c8 < 2; ++c8) {
-            uint4 hi, lo;
-            split8(g + 8 * c8, hi, lo);
             const int c = (GC * sub + c0) / 8 + c8;
-            put_chunk<TT>(mm_hi, row, c, hi);
-            put_chunk<TT>(mm_lo, row, c, lo);
+            if constexpr (ONE) {
+              uint4 hi;
+              cvt8(g + 8 * c8, hi);
+              put_chunk<TT>(mm_hi, row, c, hi);
+            } else {
+              uint4 hi, lo;
+              split8(g + 8 * c8, hi, lo);
+              put_chunk<TT>(mm_hi, row, c, hi);
+              put_chunk<TT>(mm_lo, row, c, lo);
+            }
           }
         }
         fence_async_smem();
@@ -853,11 +929,11 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
           fence_after();
           // R += mask(M) . pK  (both parts of pK along N, both parts of M)
 #pragma unroll
-          for (int a = 0; a < 2; ++a) {
+          for (int a = 0; a < (ONE ? 1 : 2); ++a) {
             const bf16* mp = a ? mm_lo : mm_hi;
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks)
-              mma(tbase + LY::C_R, desc<TT>(mp, ks), desc_mn<2 * SP>(pk, ks), idesc_bmn<2 * SP>(),
+              mma(tbase + LY::C_R, desc<TT>(mp, ks), desc_mn<2 * SP>(pk, ks), idesc_bmn<KP>(),
                   true);
           }
           { commit(barB); ++issB; }
@@ -872,7 +948,7 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
         for (int a = 0; a < MYG; ++a) {
           const int gi = sub + a * NTH;
           if (gi < NG) {
-            tld_sum<G::GB, 2>(tlane + LY::C_R + gi * G::GB, SP, rr[a]);
+            tld_sum<G::GB, ONE ? 1 : 2>(tlane + LY::C_R + gi * G::GB, SP, rr[a]);
 #pragma unroll
             for (int b = 0; b < G::GB; ++b) wr = fmaf(wv[a][b], rr[a][b], wr);
           }
@@ -917,8 +993,9 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
                 if (jj < PJ) {
                   const bf16 hb = __float2bfloat16_rn(valid ? dj_[j] : 0.f);
                   dj[elem<PJ>(row, jj)] = hb;
-                  dj[TT * PJ + elem<PJ>(row, jj)] =
-                      __float2bfloat16_rn((valid ? dj_[j] : 0.f) - __bfloat162float(hb));
+                  if constexpr (!ONE)
+                    dj[TT * PJ + elem<PJ>(row, jj)] =
+                        __float2bfloat16_rn((valid ? dj_[j] : 0.f) - __bfloat162float(hb));
                 }
               }
             }
@@ -929,8 +1006,8 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
         __syncthreads();
         if (tid == 0 && !failed) {
           fence_after();
-          gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DQ, dj, dj + TT * PJ, nullptr, 2, pt,
-                                            false);
+          gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DQ, dj, dj + TT * PJ, nullptr,
+                                            ONE ? 1 : 2, pt, false);
           { commit(barA); ++issA; }
           tma_store3(&maps.map[5], stg_a, 0, (int)tile0, n);
           bulk_commit();
@@ -948,15 +1025,15 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
           const int d = 16 * quad + lane;
           float stv[2 * SP];
 #pragma unroll
-          for (int c = 0; c < 2 * SP; c += 8) tld8(tlane + LY::C_ST + c, stv + c);
+          for (int c = 0; c < KP; c += 8) tld8(tlane + LY::C_ST + c, stv + c);
           tld_wait();
           if (lane < 16 && d < D) {
 #pragma unroll
             for (int s2 = 0; s2 < SP; ++s2) {
-              const float x = b0f[s2 * D + d] + stv[s2] + stv[SP + s2];
+              const float x = b0f[s2 * D + d] + stv[s2] + (ONE ? 0.f : stv[SP + s2]);
               const bf16 h = __float2bfloat16_rn(x);
               b0s[elem<D>(s2, d)] = h;
-              b0s[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
+              if constexpr (!ONE) b0s[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
             }
           }
         }
@@ -976,9 +1053,9 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
         const int d = 16 * quad + lane;
 #pragma unroll
         for (int c = 0; c < SP; c += 8) {
-          float e0[8], e1[8];
+          float e0[8], e1[8] = {};
           tld8(tlane + LY::C_WD + c, e0);
-          tld8(tlane + LY::C_WD + SP + c, e1);
+          if constexpr (!ONE) tld8(tlane + LY::C_WD + SP + c, e1);
           tld_wait();
           if (lane < 16 && d < D) {
 #pragma unroll
@@ -1077,6 +1154,11 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
   constexpr int MYG = (NG + NTH - 1) / NTH;
   constexpr int GC = TT / NTH;
   constexpr bool F32 = sizeof(T) == 4;
+  // bf16 inputs: pK, W, BS, the masked MT / GT and dproj as one bf16 part
+  // each (the path's bf16 tolerance); fp32: two
+  constexpr bool ONE = !F32;
+  constexpr int KP = ONE ? SP : 2 * SP;                // K / N extent of the bucket products
+  constexpr bool DIRECT = ONE && D == 64;              // landed v / dO tiles are MMA operands
   T5_PROLOGUE
   (void)cur_n;
   bf16* pk = reinterpret_cast<bf16*>(sm + LY::PK);
@@ -1099,7 +1181,7 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
   auto put_bs = [&](int s2, int d, float x) {
     const bf16 h = __float2bfloat16_rn(x);
     bss[elem<D>(s2, d)] = h;
-    bss[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
+    if constexpr (!ONE) bss[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
   };
 
   for (int w = blockIdx.x; w < items && !failed; w += gridDim.x) {
@@ -1165,8 +1247,10 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
         float pkv[MYG][G::GB], hk[MYG][G::GK], asf[MYG][G::GB], wv[MYG][G::GB];
         {
           float y[W], g[W];
-          read_cols<T, D, W>(VXt, row, sub * W, y);
-          read_cols<T, D, W>(GXt, row, sub * W, g);
+          if constexpr (!DIRECT) {
+            read_cols<T, D, W>(VXt, row, sub * W, y);
+            read_cols<T, D, W>(GXt, row, sub * W, g);
+          }
           float pq[MYG][G::GB], al[MYG][G::GB];
 #pragma unroll
           for (int a = 0; a < MYG; ++a) {
@@ -1194,10 +1278,12 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
             }
           }
           __syncthreads();   // raw tiles read, the tile's key mass loaded, scratch free
-          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), nullptr, row,
-                                      sub * W, y);
-          put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1), nullptr, row,
-                                      sub * W, g);
+          if constexpr (!DIRECT) {
+            put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), nullptr, row,
+                                        sub * W, y);
+            put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1), nullptr, row,
+                                        sub * W, g);
+          }
           float incl[MYG][G::GB], rincl[MYG][G::GB];
 #pragma unroll
           for (int a = 0; a < MYG; ++a) {
@@ -1252,14 +1338,18 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
 #pragma unroll
               for (int c8 = 0; c8 < G::GB / 8; ++c8) {
                 const int c = gi * G::GB / 8 + c8;
-                uint4 hi, lo;
-                split8(pkv[a] + 8 * c8, hi, lo);
-                put_chunk<2 * SP>(pk, row, c, hi);
-                put_chunk<2 * SP>(pk, row, SP / 8 + c, lo);
-                split8(wv[a] + 8 * c8, hi, lo);
-                put_chunk<2 * SP>(wh, row, c, hi);
-                put_chunk<2 * SP>(wh, row, SP / 8 + c, hi);
-                put_chunk<SP>(wl, row, c, lo);
+                put_parts8<2 * SP, SP / 8, ONE>(pk, row, c, pkv[a] + 8 * c8);
+                if constexpr (ONE) {
+                  uint4 hi;
+                  cvt8(wv[a] + 8 * c8, hi);
+                  put_chunk<2 * SP>(wh, row, c, hi);
+                } else {
+                  uint4 hi, lo;
+                  split8(wv[a] + 8 * c8, hi, lo);
+                  put_chunk<2 * SP>(wh, row, c, hi);
+                  put_chunk<2 * SP>(wh, row, SP / 8 + c, hi);
+                  put_chunk<SP>(wl, row, c, lo);
+                }
               }
             }
           }
@@ -1280,40 +1370,44 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
               if (a + b == 2 || (!F32 && a + b > 0)) continue;
 #pragma unroll
               for (int ks = 0; ks < D / 16; ++ks)
-                mma(tbase + LY::C_MT, desc<D>(vp[a], ks), desc<D>(gp[b], ks), idesc<TT>(),
-                    a + b > 0 || ks > 0);
+                mma(tbase + LY::C_MT, desc_a_k<D, DIRECT>(vp[a], ks), desc_a_k<D, DIRECT>(gp[b], ks),
+                    idesc<TT>(), a + b > 0 || ks > 0);
             }
           // GT[tau][t] = pK(tau) . W(t)
 #pragma unroll
-          for (int ks = 0; ks < 2 * SP / 16; ++ks)
+          for (int ks = 0; ks < KP / 16; ++ks)
             mma(tbase + LY::C_GT, desc<2 * SP>(pk, ks), desc<2 * SP>(wh, ks), idesc<TT>(), ks > 0);
+          if constexpr (!ONE) {
 #pragma unroll
-          for (int ks = 0; ks < SP / 16; ++ks)
-            mma(tbase + LY::C_GT, desc<2 * SP>(pk, ks), desc<SP>(wl, ks), idesc<TT>(), true);
+            for (int ks = 0; ks < SP / 16; ++ks)
+              mma(tbase + LY::C_GT, desc<2 * SP>(pk, ks), desc<SP>(wl, ks), idesc<TT>(), true);
+          }
           // VB = v . BS^T (BS hi and lo along N)
 #pragma unroll
           for (int a = 0; a < (F32 ? 2 : 1); ++a)
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks)
-              mma(tbase + LY::C_VB, desc<D>(vp[a], ks), desc<D>(bss, ks), idesc<2 * SP>(),
+              mma(tbase + LY::C_VB, desc_a_k<D, DIRECT>(vp[a], ks), desc<D>(bss, ks), idesc<KP>(),
                   a > 0 || ks > 0);
           // DV = pK . BS (hi.hi, lo.hi, hi.lo; BS rows read MN-major)
 #pragma unroll
           for (int ks = 0; ks < SP / 16; ++ks) {
             mma(tbase + LY::C_DV, desc<2 * SP>(pk, ks), desc_mn<D>(bss, ks), idesc_bmn<D>(), ks > 0);
-            mma(tbase + LY::C_DV, desc<2 * SP>(pk, SP / 16 + ks), desc_mn<D>(bss, ks), idesc_bmn<D>(),
-                true);
-            mma(tbase + LY::C_DV, desc<2 * SP>(pk, ks), desc_mn<D>(bss, SP / 16 + ks),
-                idesc_bmn<D>(), true);
+            if constexpr (!ONE) {
+              mma(tbase + LY::C_DV, desc<2 * SP>(pk, SP / 16 + ks), desc_mn<D>(bss, ks),
+                  idesc_bmn<D>(), true);
+              mma(tbase + LY::C_DV, desc<2 * SP>(pk, ks), desc_mn<D>(bss, SP / 16 + ks),
+                  idesc_bmn<D>(), true);
+            }
           }
           // BS[d][s] += dO^T W over the range (block 0: W hi, block 1: W lo)
 #pragma unroll
           for (int a = 0; a < (F32 ? 2 : 1); ++a)
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks) {
-              mma(tbase + LY::C_BS, desc_mn<D>(gp[a], ks), desc_mn<2 * SP>(wh, ks), idesc64_mn<SP>(),
-                  i > 0 || a > 0 || ks > 0);
-              if (a == 0)
+              mma(tbase + LY::C_BS, desc_a_mn<D, DIRECT>(gp[a], ks), desc_mn<2 * SP>(wh, ks),
+                  idesc64_mn<SP>(), i > 0 || a > 0 || ks > 0);
+              if (!ONE && a == 0)
                 mma(tbase + LY::C_BS + SP, desc_mn<D>(gp[a], ks), desc_mn<SP>(wl, ks),
                     idesc64_mn<SP>(), i > 0 || ks > 0);
             }
@@ -1330,6 +1424,37 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
         // v and the projections are consumed: the next walk step's
         if (i + 1 < it.ntiles) load_v(i + 1);
         fence_after();
+        if constexpr (ONE) {
+          // masked MT and GT rows (t >= tau kept) as packed bf16, over the
+          // first half of the thread's own columns (no other thread reads them)
+          uint32_t mh[GC / 2], gh[GC / 2];
+#pragma unroll
+          for (int c0 = 0; c0 < GC; c0 += 16) {
+            float g[16], h[16];
+            tld16(tlane + LY::C_MT + GC * sub + c0, g);
+            tld16(tlane + LY::C_GT + GC * sub + c0, h);
+            tld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const bool k0 = GC * sub + c0 + e >= row, k1 = GC * sub + c0 + e + 1 >= row;
+              __nv_bfloat162 x = __floats2bfloat162_rn(k0 ? g[e] : 0.f, k1 ? g[e + 1] : 0.f);
+              mh[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&x);
+              x = __floats2bfloat162_rn(k0 ? h[e] : 0.f, k1 ? h[e + 1] : 0.f);
+              gh[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&x);
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < GC / 2; c += 8) {
+            uint32_t x8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x8[e] = mh[c + e];
+            tst8(tlane + LY::C_MT + GC * sub + c, x8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x8[e] = gh[c + e];
+            tst8(tlane + LY::C_GT + GC * sub + c, x8);
+          }
+          tst_wait();
+        } else
         // masked MT and GT rows (t >= tau kept), split to packed bf16 hi / lo
         // and written back in place as the A operands of the second batch
         {
@@ -1380,6 +1505,17 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
           const bf16* gp[2] = {Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1)};
           // VB += mask'(MT) . W  (block 0: W hi, block 1: W lo; lo.lo dropped)
 #pragma unroll
+          if constexpr (ONE) {   // hi of tokens [GC j, GC j + GC) at columns [GC j, GC j + GC / 2)
+#pragma unroll
+            for (int ks = 0; ks < TT / 16; ++ks) {
+              const uint32_t col = GC * (16 * ks / GC) + (16 * ks % GC) / 2;
+              mma_ta(tbase + LY::C_VB, tbase + LY::C_MT + col, desc_mn<2 * SP>(wh, ks),
+                     idesc_bmn<SP>(), true);
+              mma_ta(tbase + LY::C_DV, tbase + LY::C_GT + col, desc_a_mn<D, DIRECT>(gp[0], ks),
+                     idesc_bmn<D>(), true);
+            }
+          } else {
+#pragma unroll
           for (int a = 0; a < 2; ++a)
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks) {
@@ -1394,12 +1530,13 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
           for (int a = 0; a < 2; ++a)
 #pragma unroll
             for (int b = 0; b < 2; ++b) {
-              if (a + b == 2 || (!F32 && b == 1)) continue;
+              if (a + b == 2) continue;
 #pragma unroll
               for (int ks = 0; ks < TT / 16; ++ks)
                 mma_ta(tbase + LY::C_DV, tbase + LY::C_GT + 64 * a + 8 * ks, desc_mn<D>(gp[b], ks),
                        idesc_bmn<D>(), true);
             }
+          }
           { commit(barB); ++issB; }
         }
         T5_WAIT(barB, phB);
@@ -1413,7 +1550,7 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
           const int gi = sub + a * NTH;
           if (gi < NG) {
             float vb[G::GB], dpk[G::GB], dj_[G::GK];
-            tld_sum<G::GB, 2>(tlane + LY::C_VB + gi * G::GB, SP, vb);
+            tld_sum<G::GB, ONE ? 1 : 2>(tlane + LY::C_VB + gi * G::GB, SP, vb);
 #pragma unroll
             for (int b = 0; b < G::GB; ++b) dpk[b] = valid ? asf[a][b] + vb[b] : 0.f;
             float dsl = 0.f;
@@ -1427,7 +1564,8 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
                   const float x = valid ? dj_[j] : 0.f;
                   const bf16 hb = __float2bfloat16_rn(x);
                   dj[elem<PJ>(row, jj)] = hb;
-                  dj[TT * PJ + elem<PJ>(row, jj)] = __float2bfloat16_rn(x - __bfloat162float(hb));
+                  if constexpr (!ONE)
+                    dj[TT * PJ + elem<PJ>(row, jj)] = __float2bfloat16_rn(x - __bfloat162float(hb));
                 }
               }
             }
@@ -1439,8 +1577,8 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
         if (tid == 0 && !failed) {
           fence_after();
           // DK = dproj . P (into the consumed MT columns)
-          gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DK, dj, dj + TT * PJ, nullptr, 2, pt,
-                                            false);
+          gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DK, dj, dj + TT * PJ, nullptr,
+                                            ONE ? 1 : 2, pt, false);
           { commit(barA); ++issA; }
         }
         T5_WAIT(barA, phA);
@@ -1459,10 +1597,11 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
           const int d = 16 * quad + lane;
           float bsv[2 * SP];
 #pragma unroll
-          for (int c = 0; c < 2 * SP; c += 8) tld8(tlane + LY::C_BS + c, bsv + c);
+          for (int c = 0; c < KP; c += 8) tld8(tlane + LY::C_BS + c, bsv + c);
           tld_wait();
           if (lane < 16 && d < D) {
-            for (int s2 = 0; s2 < SP; ++s2) put_bs(s2, d, bsf[s2 * D + d] + bsv[s2] + bsv[SP + s2]);
+            for (int s2 = 0; s2 < SP; ++s2)
+              put_bs(s2, d, bsf[s2 * D + d] + bsv[s2] + (ONE ? 0.f : bsv[SP + s2]));
           }
         }
         fence_async_smem();

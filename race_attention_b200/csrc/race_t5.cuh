@@ -136,7 +136,16 @@ __device__ __forceinline__ uint64_t desc_sw128_mn(const void* base, int ks) {
   d |= (uint64_t)2 << 61;
   return d;
 }
-// MN-major A operand over a tile's tokens: a converted part, or (SW) the landed tile
+// K-major operand with C columns: a converted part, or (SW) the landed tile
+template <int C, bool SW>
+__device__ __forceinline__ uint64_t desc_a_k(const void* base, int ks) {
+  if constexpr (SW) {
+    return desc_sw128(base, ks);
+  } else {
+    return desc<C>(base, ks);
+  }
+}
+// MN-major operand over a tile's tokens: a converted part, or (SW) the landed tile
 template <int C, bool SW>
 __device__ __forceinline__ uint64_t desc_a_mn(const void* base, int ks) {
   if constexpr (SW) {
