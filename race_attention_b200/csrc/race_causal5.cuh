@@ -506,10 +506,11 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
       phA ^= 1;
       fence_after();
       {
-        if constexpr (ONE) {
-          // masked G row as packed bf16 pairs, written over the first half
-          // of the thread's own columns (no other thread reads them)
-          uint32_t hw[GC / 2];
+        {
+          // masked G row (columns [GC sub, GC sub + GC)) as packed bf16 parts
+          // over the thread's own columns -- hi in the first half, lo (fp32
+          // inputs) in the second -- so no other thread's reads are in the way
+          uint32_t hw[GC / 2], lw[GC / 2];
 #pragma unroll
           for (int c0 = 0; c0 < GC; c0 += 16) {
             float g[16];
@@ -519,8 +520,12 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
             for (int e = 0; e < 16; e += 2) {
               const float x0 = GC * sub + c0 + e > row ? 0.f : g[e];
               const float x1 = GC * sub + c0 + e + 1 > row ? 0.f : g[e + 1];
-              const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-              hw[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+              if constexpr (ONE) {
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+                hw[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+              } else {
+                split2(x0, x1, hw[(c0 + e) / 2], lw[(c0 + e) / 2]);
+              }
             }
           }
 #pragma unroll
@@ -529,35 +534,11 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
 #pragma unroll
             for (int e = 0; e < 8; ++e) h8[e] = hw[c + e];
             tst8(tlane + LY::C_G + GC * sub + c, h8);
-          }
-          tst_wait();
-        } else {
-          // masked G row (columns [GC sub, GC sub + GC)), split to packed bf16 pairs
-          uint32_t hw[GC / 2], lw[GC / 2];
-  #pragma unroll
-          for (int c0 = 0; c0 < GC; c0 += 16) {
-            float g[16];
-            tld16(tlane + LY::C_G + GC * sub + c0, g);
-            tld_wait();
-  #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              if (GC * sub + c0 + e > row) g[e] = 0.f;
-  #pragma unroll
-            for (int e = 0; e < 16; e += 2) split2(g[e], g[e + 1], hw[(c0 + e) / 2], lw[(c0 + e) / 2]);
-          }
-          fence_before();
-          __syncthreads();   // every G column has been read before any is overwritten
-          fence_after();
-  #pragma unroll
-          for (int c = 0; c < GC / 2; c += 8) {
-            uint32_t h8[8], l8[8];
-  #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              h8[e] = hw[c + e];
-              l8[e] = lw[c + e];
+            if constexpr (!ONE) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) h8[e] = lw[c + e];
+              tst8(tlane + LY::C_G + GC * sub + GC / 2 + c, h8);
             }
-            tst8(tlane + LY::C_G + GC / 2 * sub + c, h8);
-            tst8(tlane + LY::C_G + 64 + GC / 2 * sub + c, l8);
           }
           tst_wait();
         }
@@ -567,23 +548,18 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
       if (tid == 0 && !failed) {
         fence_after();
         const bf16* vp[2] = {Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1)};
-        if constexpr (ONE) {   // hi of tokens [GC j, GC j + GC) at columns [GC j, GC j + GC / 2)
+        // part a of the masked G for tokens [GC j, GC j + GC): columns GC j + a GC / 2 + ...
 #pragma unroll
-          for (int ks = 0; ks < TT / 16; ++ks)
-            mma_ta(tbase + LY::C_OUT, tbase + LY::C_G + GC * (16 * ks / GC) + (16 * ks % GC) / 2,
-                   desc_a_mn<D, DIRECT>(vp[0], ks), idesc_bmn<D>(), true);
-        } else {
+        for (int a2 = 0; a2 < (ONE ? 1 : 2); ++a2)
 #pragma unroll
-          for (int a = 0; a < 2; ++a)
+          for (int b2 = 0; b2 < (ONE ? 1 : 2); ++b2) {
+            if (a2 + b2 == 2) continue;
 #pragma unroll
-            for (int b = 0; b < 2; ++b) {
-              if (a + b == 2) continue;
-#pragma unroll
-              for (int ks = 0; ks < TT / 16; ++ks)
-                mma_ta(tbase + LY::C_OUT, tbase + LY::C_G + 64 * a + 8 * ks, desc_mn<D>(vp[b], ks),
-                       idesc_bmn<D>(), true);
-            }
-        }
+            for (int ks = 0; ks < TT / 16; ++ks)
+              mma_ta(tbase + LY::C_OUT,
+                     tbase + LY::C_G + GC * (16 * ks / GC) + a2 * (GC / 2) + (16 * ks % GC) / 2,
+                     desc_a_mn<D, DIRECT>(vp[b2], ks), idesc_bmn<D>(), true);
+          }
 #pragma unroll
         for (int a = 0; a < (sizeof(T) == 4 ? 2 : 1); ++a)
 #pragma unroll
@@ -1424,10 +1400,11 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
         // v and the projections are consumed: the next walk step's
         if (i + 1 < it.ntiles) load_v(i + 1);
         fence_after();
-        if constexpr (ONE) {
-          // masked MT and GT rows (t >= tau kept) as packed bf16, over the
-          // first half of the thread's own columns (no other thread reads them)
-          uint32_t mh[GC / 2], gh[GC / 2];
+        {
+          // masked MT and GT rows (t >= tau kept) as packed bf16 parts over the
+          // thread's own columns -- hi in the first half, lo (fp32 inputs) in
+          // the second -- so no other thread's reads are in the way
+          uint32_t mh[GC / 2], ml[GC / 2], gh[GC / 2], gl[GC / 2];
 #pragma unroll
           for (int c0 = 0; c0 < GC; c0 += 16) {
             float g[16], h[16];
@@ -1437,10 +1414,17 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
 #pragma unroll
             for (int e = 0; e < 16; e += 2) {
               const bool k0 = GC * sub + c0 + e >= row, k1 = GC * sub + c0 + e + 1 >= row;
-              __nv_bfloat162 x = __floats2bfloat162_rn(k0 ? g[e] : 0.f, k1 ? g[e + 1] : 0.f);
-              mh[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&x);
-              x = __floats2bfloat162_rn(k0 ? h[e] : 0.f, k1 ? h[e + 1] : 0.f);
-              gh[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&x);
+              const float m0 = k0 ? g[e] : 0.f, m1 = k1 ? g[e + 1] : 0.f;
+              const float g0 = k0 ? h[e] : 0.f, g1 = k1 ? h[e + 1] : 0.f;
+              if constexpr (ONE) {
+                __nv_bfloat162 x = __floats2bfloat162_rn(m0, m1);
+                mh[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&x);
+                x = __floats2bfloat162_rn(g0, g1);
+                gh[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&x);
+              } else {
+                split2(m0, m1, mh[(c0 + e) / 2], ml[(c0 + e) / 2]);
+                split2(g0, g1, gh[(c0 + e) / 2], gl[(c0 + e) / 2]);
+              }
             }
           }
 #pragma unroll
@@ -1452,49 +1436,14 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
 #pragma unroll
             for (int e = 0; e < 8; ++e) x8[e] = gh[c + e];
             tst8(tlane + LY::C_GT + GC * sub + c, x8);
-          }
-          tst_wait();
-        } else
-        // masked MT and GT rows (t >= tau kept), split to packed bf16 hi / lo
-        // and written back in place as the A operands of the second batch
-        {
-          uint32_t mh[GC / 2], ml[GC / 2], gh[GC / 2], gl[GC / 2];
+            if constexpr (!ONE) {
 #pragma unroll
-          for (int c0 = 0; c0 < GC; c0 += 16) {
-            float g[16];
-            tld16(tlane + LY::C_MT + GC * sub + c0, g);
-            tld_wait();
+              for (int e = 0; e < 8; ++e) x8[e] = ml[c + e];
+              tst8(tlane + LY::C_MT + GC * sub + GC / 2 + c, x8);
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              if (GC * sub + c0 + e < row) g[e] = 0.f;
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) split2(g[e], g[e + 1], mh[(c0 + e) / 2], ml[(c0 + e) / 2]);
-            tld16(tlane + LY::C_GT + GC * sub + c0, g);
-            tld_wait();
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-              if (GC * sub + c0 + e < row) g[e] = 0.f;
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) split2(g[e], g[e + 1], gh[(c0 + e) / 2], gl[(c0 + e) / 2]);
-          }
-          fence_before();
-          __syncthreads();   // every MT / GT column has been read before any is overwritten
-          fence_after();
-#pragma unroll
-          for (int c = 0; c < GC / 2; c += 8) {
-            uint32_t x8[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x8[e] = mh[c + e];
-            tst8(tlane + LY::C_MT + GC / 2 * sub + c, x8);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x8[e] = ml[c + e];
-            tst8(tlane + LY::C_MT + 64 + GC / 2 * sub + c, x8);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x8[e] = gh[c + e];
-            tst8(tlane + LY::C_GT + GC / 2 * sub + c, x8);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x8[e] = gl[c + e];
-            tst8(tlane + LY::C_GT + 64 + GC / 2 * sub + c, x8);
+              for (int e = 0; e < 8; ++e) x8[e] = gl[c + e];
+              tst8(tlane + LY::C_GT + GC * sub + GC / 2 + c, x8);
+            }
           }
           tst_wait();
         }
@@ -1505,38 +1454,25 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
           const bf16* gp[2] = {Slot<D>::part(GXt, 0), Slot<D>::part(GXt, 1)};
           // VB += mask'(MT) . W  (block 0: W hi, block 1: W lo; lo.lo dropped)
 #pragma unroll
-          if constexpr (ONE) {   // hi of tokens [GC j, GC j + GC) at columns [GC j, GC j + GC / 2)
+          // part a of the masked MT / GT for tokens [GC j, GC j + GC): columns GC j + a GC / 2 + ...
+#pragma unroll
+          for (int a2 = 0; a2 < (ONE ? 1 : 2); ++a2)
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks) {
-              const uint32_t col = GC * (16 * ks / GC) + (16 * ks % GC) / 2;
+              const uint32_t col = GC * (16 * ks / GC) + a2 * (GC / 2) + (16 * ks % GC) / 2;
+              // VB += mask'(MT) . W  (block 0: W hi, block 1: W lo; lo.lo dropped)
               mma_ta(tbase + LY::C_VB, tbase + LY::C_MT + col, desc_mn<2 * SP>(wh, ks),
                      idesc_bmn<SP>(), true);
-              mma_ta(tbase + LY::C_DV, tbase + LY::C_GT + col, desc_a_mn<D, DIRECT>(gp[0], ks),
-                     idesc_bmn<D>(), true);
-            }
-          } else {
-#pragma unroll
-          for (int a = 0; a < 2; ++a)
-#pragma unroll
-            for (int ks = 0; ks < TT / 16; ++ks) {
-              mma_ta(tbase + LY::C_VB, tbase + LY::C_MT + 64 * a + 8 * ks, desc_mn<2 * SP>(wh, ks),
-                     idesc_bmn<SP>(), true);
-              if (a == 0)
-                mma_ta(tbase + LY::C_VB + SP, tbase + LY::C_MT + 8 * ks, desc_mn<SP>(wl, ks),
+              if (!ONE && a2 == 0)
+                mma_ta(tbase + LY::C_VB + SP, tbase + LY::C_MT + col, desc_mn<SP>(wl, ks),
                        idesc_bmn<SP>(), true);
+              // DV += mask'(GT) . dO  (lo.lo dropped)
+#pragma unroll
+              for (int b2 = 0; b2 < (ONE ? 1 : 2); ++b2)
+                if (a2 + b2 < 2)
+                  mma_ta(tbase + LY::C_DV, tbase + LY::C_GT + col, desc_a_mn<D, DIRECT>(gp[b2], ks),
+                         idesc_bmn<D>(), true);
             }
-          // DV += mask'(GT) . dO
-#pragma unroll
-          for (int a = 0; a < 2; ++a)
-#pragma unroll
-            for (int b = 0; b < 2; ++b) {
-              if (a + b == 2) continue;
-#pragma unroll
-              for (int ks = 0; ks < TT / 16; ++ks)
-                mma_ta(tbase + LY::C_DV, tbase + LY::C_GT + 64 * a + 8 * ks, desc_mn<D>(gp[b], ks),
-                       idesc_bmn<D>(), true);
-            }
-          }
           { commit(barB); ++issB; }
         }
         T5_WAIT(barB, phB);

@@ -912,14 +912,14 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       }
       fence_async_smem();
       fence_before();
-      __syncthreads();
+      if (__syncthreads_or(failed)) failed = true;   // the tile's vote
       if (tid == 0 && !failed) {
         fence_after();
         gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_OUT, pq, pq + TT * SP, nullptr, 2, et,
                                           false);
         { commit(barB); ++issB; }
       }
-      if (T5_VOTE()) break;
+      if (failed) break;
     }
     // the last tile leaves through its own slot, which the store of the
     // tile before may still be reading
@@ -1364,7 +1364,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
         }
         fence_async_smem();
         fence_before();
-        __syncthreads();
+        if (__syncthreads_or(failed)) failed = true;   // the tile's vote
         if (tid == 0 && !failed) {
           fence_after();
           // dE^T[d][s-block j] += sum_a dO_a^T . pQ_j (MN-major over the tile's tokens)
@@ -1378,7 +1378,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
                                             false);
           { commit(barB); ++issB; }
         }
-        if (T5_VOTE()) break;
+        if (failed) break;
       }
       T5_STAGE_DRAIN();   // LATE: the store of the tile before may still read the q slot
       if (!failed)
@@ -1594,7 +1594,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         }
         fence_async_smem();
         fence_before();
-        __syncthreads();
+        if (__syncthreads_or(failed)) failed = true;   // the tile's vote
         if (tid == 0 && !failed) {
           fence_after();
           gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_DV, pk, pk + TT * SP, nullptr, 2, dbt,
@@ -1603,7 +1603,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
                                             false);
           { commit(barB); ++issB; }
         }
-        if (T5_VOTE()) break;
+        if (failed) break;
       }
       T5_STAGE_DRAIN();   // the stores of the tile before may still read these slots
       if (!failed) {
