@@ -815,6 +815,12 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
   using G = Groups<K>;
   constexpr bool F32 = sizeof(T) == 4;
   constexpr bool DIRECT = !F32 && D == 64;   // bf16 tiles are MMA operands as they land
+  // bf16 inputs: the per-token operands (pQ / pK, dproj) and the readout's
+  // tables as one bf16 part -- the path's bf16 tolerance; the tables whose
+  // products cancel (E against its bucket average in dpQ, dB against dA in
+  // dpK, the key state against its mass, the backward projections) keep
+  // their three parts; fp32: 2 or 3 parts throughout
+  constexpr int B2 = F32 ? 2 : 1;
   T5_PROLOGUE
   bf16* pq = reinterpret_cast<bf16*>(sm + LY::PQ);
   bf16* ps = reinterpret_cast<bf16*>(sm + LY::PS);
@@ -827,13 +833,13 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
     __syncthreads();   // the previous item's MMAs are complete; tables may change
     if (m != cur_m) {
       const float* pl = prm.planes + (size_t)m * prm.LK * D;
-      put_stack<PJ, D, 2, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+      put_stack<PJ, D, B2, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
       cur_m = m;
     }
     if (n != cur_n) {
       const float* st = prm.state + (size_t)n * prm.SS;
       const float* mass = st + prm.S * D;
-      put_stack<D, SP, 2, NTHR>(et, [&](int d, int s) {
+      put_stack<D, SP, B2, NTHR>(et, [&](int d, int s) {
         return s < prm.S ? st[s * D + d] / (mass[s] + prm.eps) : 0.f;
       });
       cur_n = n;
@@ -845,7 +851,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       phB ^= 1;
       fence_after();
       float o[W];
-      tld_sum<W>(tlane + LY::C_OUT + sub * W, D, o);
+      tld_sum<W, B2>(tlane + LY::C_OUT + sub * W, D, o);
       put_tile_cols<T, D, W>(stage_slot, row, sub * W, o);
       fence_async_smem();
       fence_before();
@@ -887,7 +893,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       __syncthreads();
       if (tid == 0 && !failed) {
         fence_after();
-        gemm_parts<PJ, 2, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(X, 0),
+        gemm_parts<PJ, B2, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(X, 0),
                                         Slot<D>::part(X, 1), nullptr, F32 ? 2 : 1, ps, false);
         { commit(barA); ++issA; }
       }
@@ -898,7 +904,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       {
         // two threads per token take two groups each: unrolled (constant offsets)
         float proj[PJ];
-        tld_sum<PJ>(tlane + LY::C_PROJ, PJ, proj);
+        tld_sum<PJ, B2>(tlane + LY::C_PROJ, PJ, proj);
 #pragma unroll
         for (int gi = 0; gi < SP / G::GB; ++gi) {
           if (gi % NTH == sub) {
@@ -906,7 +912,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
             const bool has = gi * G::GK < PJ;
             group_probs<K>(has ? proj + gi * G::GK : proj, gi * G::GT, has ? L : 0, inv_scale, p,
                            h);
-            put_cols<SP, G::GB, 2>(pq, pq + TT * SP, nullptr, row, gi * G::GB, p);
+            put_cols<SP, G::GB, B2>(pq, pq + TT * SP, nullptr, row, gi * G::GB, p);
           }
         }
       }
@@ -915,7 +921,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       if (__syncthreads_or(failed)) failed = true;   // the tile's vote
       if (tid == 0 && !failed) {
         fence_after();
-        gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_OUT, pq, pq + TT * SP, nullptr, 2, et,
+        gemm_parts<D, B2, SP / 16, SP, SP>(tbase + LY::C_OUT, pq, pq + TT * SP, nullptr, B2, et,
                                           false);
         { commit(barB); ++issB; }
       }
@@ -971,6 +977,12 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
   constexpr int MYG = (NG + NTH - 1) / NTH;            // groups per thread (at most)
   constexpr bool F32 = sizeof(T) == 4;
   constexpr bool DIRECT = !F32 && D == 64;   // bf16 tiles are MMA operands as they land
+  // bf16 inputs: the per-token operands (pQ / pK, dproj) and the readout's
+  // tables as one bf16 part -- the path's bf16 tolerance; the tables whose
+  // products cancel (E against its bucket average in dpQ, dB against dA in
+  // dpK, the key state against its mass, the backward projections) keep
+  // their three parts; fp32: 2 or 3 parts throughout
+  constexpr int B2 = F32 ? 2 : 1;
   T5_PROLOGUE
   (void)cur_n;
   bf16* pk3 = reinterpret_cast<bf16*>(sm + LY::PK3);
@@ -983,7 +995,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
     __syncthreads();
     if (m != cur_m) {
       const float* pl = prm.planes + (size_t)m * prm.LK * D;
-      put_stack<PJ, D, 2, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+      put_stack<PJ, D, B2, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
       cur_m = m;
     }
     float mass[MYG][G::GB];
@@ -1052,7 +1064,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
       __syncthreads();
       if (tid == 0 && !failed) {
         fence_after();
-        gemm_parts<PJ, 2, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
+        gemm_parts<PJ, B2, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
                                         Slot<D>::part(KXt, 1), nullptr, F32 ? 2 : 1, ps, false);
         { commit(barA); ++issA; }
       }
@@ -1067,7 +1079,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
           if (gi < NG) {
             float pj[G::GK], p[G::GB], h[G::GK];
             const bool has = gi * G::GK < PJ;
-            tld_group<G::GK, 2>(tlane + LY::C_PROJ, has ? gi * G::GK : 0, pj);
+            tld_group<G::GK, B2>(tlane + LY::C_PROJ, has ? gi * G::GK : 0, pj);
             group_probs<K>(pj, gi * G::GT, has ? L : 0, inv_scale, p, h);
 #pragma unroll
             for (int b = 0; b < G::GB; ++b) {
@@ -1125,7 +1137,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
         const int l = tid & 31, d = 16 * (warp & 3) + l;
 #pragma unroll
         for (int c = 0; c < SP; c += 8) {
-          float st[3][8];
+          float st[3][8] = {};
 #pragma unroll
           for (int j = 0; j < 3; ++j) tld8(tlane + LY::C_ST + j * SP + c, st[j]);
           tld_wait();
@@ -1199,6 +1211,12 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
   using G = Groups<K>;
   constexpr bool F32 = sizeof(T) == 4;
   constexpr bool DIRECT = !F32 && D == 64;   // bf16 tiles are MMA operands as they land
+  // bf16 inputs: the per-token operands (pQ / pK, dproj) and the readout's
+  // tables as one bf16 part -- the path's bf16 tolerance; the tables whose
+  // products cancel (E against its bucket average in dpQ, dB against dA in
+  // dpK, the key state against its mass, the backward projections) keep
+  // their three parts; fp32: 2 or 3 parts throughout
+  constexpr int B2 = F32 ? 2 : 1;
   T5_PROLOGUE
   bf16* pq = reinterpret_cast<bf16*>(sm + LY::PQ);
   bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
@@ -1218,7 +1236,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
       if (m != cur_m) {
         const float* pl = prm.planes + (size_t)m * prm.LK * D;
         put_stack<PJ, D, 3, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
-        put_stack<D, PJ, 2, NTHR>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+        put_stack<D, PJ, B2, NTHR>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
         cur_m = m;
       }
       if (n != cur_n) {
@@ -1238,7 +1256,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
         phB ^= 1;
         fence_after();
         float o[W];
-        tld_sum<W>(tlane + LY::C_DQ + sub * W, D, o);
+        tld_sum<W, B2>(tlane + LY::C_DQ + sub * W, D, o);
         put_tile_cols<T, D, W>(stage_slot, row, sub * W, o);
         fence_async_smem();
         fence_before();
@@ -1338,6 +1356,10 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
               // one row of [hi | lo] bucket blocks
 #pragma unroll
               for (int c8 = 0; c8 < G::GB / 8; ++c8) {
+                if constexpr (!F32) {
+                  put_cols<2 * SP, 8, 1>(pq, nullptr, nullptr, row, gi * G::GB + 8 * c8, p + 8 * c8);
+                  continue;
+                }
                 uint4 hq, lq;
                 split2(p[8 * c8 + 0], p[8 * c8 + 1], hq.x, lq.x);
                 split2(p[8 * c8 + 2], p[8 * c8 + 3], hq.y, lq.y);
@@ -1355,7 +1377,8 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
                   if (jj < PJ) {
                     const bf16 hb = __float2bfloat16_rn(dj_[j]);
                     dj[elem<PJ>(row, jj)] = hb;
-                    dj[TT * PJ + elem<PJ>(row, jj)] = __float2bfloat16_rn(dj_[j] - __bfloat162float(hb));
+                    if constexpr (F32)
+                      dj[TT * PJ + elem<PJ>(row, jj)] = __float2bfloat16_rn(dj_[j] - __bfloat162float(hb));
                   }
                 }
               }
@@ -1373,8 +1396,8 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks)
               mma(tbase + LY::C_DE, desc_a_mn<D, DIRECT>(Slot<D>::part(GXt, a), ks), desc_mn<2 * SP>(pq, ks),
-                  idesc64_mn<2 * SP>(), i > 0 || a > 0 || ks > 0);
-          gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DQ, dj, dj + TT * PJ, nullptr, 2, pt,
+                  idesc64_mn<B2 * SP>(), i > 0 || a > 0 || ks > 0);
+          gemm_parts<D, B2, PJ / 16, PJ, PJ>(tbase + LY::C_DQ, dj, dj + TT * PJ, nullptr, B2, pt,
                                             false);
           { commit(barB); ++issB; }
         }
@@ -1392,9 +1415,9 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
         const int l = tid & 31, d = 16 * (warp & 3) + l;
 #pragma unroll
         for (int c = 0; c < SP; c += 8) {
-          float e[2][8];
+          float e[2][8] = {};
           tld8(tlane + LY::C_DE + c, e[0]);
-          tld8(tlane + LY::C_DE + SP + c, e[1]);
+          if constexpr (F32) tld8(tlane + LY::C_DE + SP + c, e[1]);
           tld_wait();
           if (l < 16 && d < D) {
 #pragma unroll
@@ -1433,6 +1456,12 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
   using G = Groups<K>;
   constexpr bool F32 = sizeof(T) == 4;
   constexpr bool DIRECT = !F32 && D == 64;   // bf16 tiles are MMA operands as they land
+  // bf16 inputs: the per-token operands (pQ / pK, dproj) and the readout's
+  // tables as one bf16 part -- the path's bf16 tolerance; the tables whose
+  // products cancel (E against its bucket average in dpQ, dB against dA in
+  // dpK, the key state against its mass, the backward projections) keep
+  // their three parts; fp32: 2 or 3 parts throughout
+  constexpr int B2 = F32 ? 2 : 1;
   T5_PROLOGUE
   bf16* pk = reinterpret_cast<bf16*>(sm + LY::PK);
   bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
@@ -1453,7 +1482,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
       if (m != cur_m) {
         const float* pl = prm.planes + (size_t)m * prm.LK * D;
         put_stack<PJ, D, 3, NTHR>(ps, [&](int j, int d) { return j < prm.LK ? pl[j * D + d] : 0.f; });
-        put_stack<D, PJ, 2, NTHR>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
+        put_stack<D, PJ, B2, NTHR>(pt, [&](int d, int j) { return j < prm.LK ? pl[j * D + d] : 0.f; });
         cur_m = m;
       }
       if (n != cur_n) {
@@ -1464,7 +1493,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         put_stack<SP, D, 3, NTHR>(db, [&](int s, int d) {
           return s < prm.S ? gs[s * D + d] / (mass[s] + prm.eps) : 0.f;
         });
-        put_stack<D, SP, 2, NTHR>(dbt, [&](int d, int s) {
+        put_stack<D, SP, B2, NTHR>(dbt, [&](int d, int s) {
           return s < prm.S ? gs[s * D + d] / (mass[s] + prm.eps) : 0.f;
         });
         if (tid < SP) {
@@ -1488,9 +1517,9 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         fence_after();
         {
           float o[W];
-          tld_sum<W>(tlane + LY::C_DV + sub * W, D, o);
+          tld_sum<W, B2>(tlane + LY::C_DV + sub * W, D, o);
           put_tile_cols<T, D, W>(stage_k, row, sub * W, o);
-          tld_sum<W>(tlane + LY::C_DK + sub * W, D, o);
+          tld_sum<W, B2>(tlane + LY::C_DK + sub * W, D, o);
           put_tile_cols<T, D, W>(stage_v, row, sub * W, o);
         }
         fence_async_smem();
@@ -1577,7 +1606,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
               float dsl = 0.f;
               group_probs_bwd<K>(p, g, h, inv_scale, dj_, dsl);
               if (valid) ds += dsl;
-              put_cols<SP, G::GB, 2>(pk, pk + TT * SP, nullptr, row, gi * G::GB, p);
+              put_cols<SP, G::GB, B2>(pk, pk + TT * SP, nullptr, row, gi * G::GB, p);
               if (has) {
 #pragma unroll
                 for (int j = 0; j < G::GK; ++j) {
@@ -1585,7 +1614,8 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
                   if (jj < PJ) {
                     const bf16 hb = __float2bfloat16_rn(dj_[j]);
                     dj[elem<PJ>(row, jj)] = hb;
-                    dj[TT * PJ + elem<PJ>(row, jj)] = __float2bfloat16_rn(dj_[j] - __bfloat162float(hb));
+                    if constexpr (F32)
+                      dj[TT * PJ + elem<PJ>(row, jj)] = __float2bfloat16_rn(dj_[j] - __bfloat162float(hb));
                   }
                 }
               }
@@ -1597,9 +1627,9 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         if (__syncthreads_or(failed)) failed = true;   // the tile's vote
         if (tid == 0 && !failed) {
           fence_after();
-          gemm_parts<D, 2, SP / 16, SP, SP>(tbase + LY::C_DV, pk, pk + TT * SP, nullptr, 2, dbt,
+          gemm_parts<D, B2, SP / 16, SP, SP>(tbase + LY::C_DV, pk, pk + TT * SP, nullptr, B2, dbt,
                                             false);
-          gemm_parts<D, 2, PJ / 16, PJ, PJ>(tbase + LY::C_DK, dj, dj + TT * PJ, nullptr, 2, pt,
+          gemm_parts<D, B2, PJ / 16, PJ, PJ>(tbase + LY::C_DK, dj, dj + TT * PJ, nullptr, B2, pt,
                                             false);
           { commit(barB); ++issB; }
         }
