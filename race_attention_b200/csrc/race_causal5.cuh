@@ -576,21 +576,18 @@ __global__ void __launch_bounds__(TT * FwdLay<D, SPAD>::NTH, 2)
         tld_sum<W, 1>(tlane + LY::C_OUT + sub * W, 0, o);
         put_tile_cols<T, D, W>(sm + LY::VX, row, sub * W, o);   // v consumed: out staging
       }
-      if (i + 1 < it.ntiles && sub == 0) {
+      // B0 of the next tile (M = 64 lanes: row d = 16 q + l); the NTH warps of
+      // a lane quarter take every NTH-th 8-bucket chunk
+      if (i + 1 < it.ntiles) {
         const int d = 16 * quad + lane;
-        float stv[2 * SP];
+        for (int s8 = sub; s8 < SP / 8; s8 += NTH) {
+          float lo8[8] = {}, v[8];
+          tld8(tlane + LY::C_ST + 8 * s8, v);
+          if constexpr (!ONE) tld8(tlane + LY::C_ST + SP + 8 * s8, lo8);
+          tld_wait();
+          if (lane < 16 && d < D) {
 #pragma unroll
-        for (int c = 0; c < KP; c += 8) tld8(tlane + LY::C_ST + c, stv + c);
-        tld_wait();
-        if (lane < 16 && d < D) {
-#pragma unroll
-          for (int s8 = 0; s8 < SP / 8; ++s8) {
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int s = s8 * 8 + e;
-              v[e] = b0f[s * D + d] + stv[s] + (ONE ? 0.f : stv[SP + s]);
-            }
+            for (int e = 0; e < 8; ++e) v[e] += b0f[(s8 * 8 + e) * D + d] + lo8[e];
             put_parts8<2 * SP, SP / 8, ONE>(b0, d, s8, v);
           }
         }
@@ -625,8 +622,7 @@ struct BwdQLayC {
   static constexpr int VX = 0;                          // v (landed, then hi | lo)
   static constexpr int GX = VX + Slot<D>::FLOATS;       // dO (landed, then hi | lo)
   static constexpr int PJX = GX + Slot<D>::FLOATS;      // projQ [TT][16] then projK [TT][16]
-  static constexpr int MM = PJX + 2 * TT * PJ;          // bf16 [TT x TT] masked dO V^T, hi then lo;
-                                                        // later alpha [TT][SA] and dq staging
+  static constexpr int MM = PJX + 2 * TT * PJ;          // alpha [TT][SA] and dq staging
   static constexpr int STG_DQ = MM + TT * SP;           // dq staging (1 KB aligned)
   static constexpr int PK = MM + TT * TT;               // bf16 [TT x 2SP] pK (hi | lo)
   static constexpr int WP = PK + TT * SP;               // bf16 [TT x 2SP] W (hi | lo)
@@ -672,8 +668,6 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
   bf16* b0s = reinterpret_cast<bf16*>(sm + LY::B0S);
   bf16* dj = reinterpret_cast<bf16*>(sm + LY::DJ);
   bf16* pt = reinterpret_cast<bf16*>(sm + LY::PT);
-  bf16* mm_hi = reinterpret_cast<bf16*>(sm + LY::MM);
-  bf16* mm_lo = mm_hi + TT * TT;
   float* b0f = sm + LY::B0F;
   double* a0 = reinterpret_cast<double*>(sm + LY::A0);
   float* scan = sm + LY::SCAN;
@@ -875,43 +869,54 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
         // every MMA that reads the input slots has completed: next tile's loads
         if (i + 1 < it.ntiles) load(i + 1);
         fence_after();
+        {
+          // masked M row (columns [GC sub, GC sub + GC)) as packed bf16 parts
+          // over the thread's own tensor-memory columns -- hi in the first
+          // half, lo (fp32 inputs) in the second: the A operand of R += mask(M) pK
+          uint32_t hw[GC / 2], lw[GC / 2];
 #pragma unroll
-        for (int c0 = 0; c0 < GC; c0 += 16) {
-          float g[16];
-          tld16(tlane + LY::C_M + GC * sub + c0, g);
-          tld_wait();
+          for (int c0 = 0; c0 < GC; c0 += 16) {
+            float g[16];
+            tld16(tlane + LY::C_M + GC * sub + c0, g);
+            tld_wait();
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (GC * sub + c0 + e > row) g[e] = 0.f;
-#pragma unroll
-          for (int c8 = 0; c8 < 2; ++c8) {
-            const int c = (GC * sub + c0) / 8 + c8;
-            if constexpr (ONE) {
-              uint4 hi;
-              cvt8(g + 8 * c8, hi);
-              put_chunk<TT>(mm_hi, row, c, hi);
-            } else {
-              uint4 hi, lo;
-              split8(g + 8 * c8, hi, lo);
-              put_chunk<TT>(mm_hi, row, c, hi);
-              put_chunk<TT>(mm_lo, row, c, lo);
+            for (int e = 0; e < 16; e += 2) {
+              const float x0 = GC * sub + c0 + e > row ? 0.f : g[e];
+              const float x1 = GC * sub + c0 + e + 1 > row ? 0.f : g[e + 1];
+              if constexpr (ONE) {
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+                hw[(c0 + e) / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+              } else {
+                split2(x0, x1, hw[(c0 + e) / 2], lw[(c0 + e) / 2]);
+              }
             }
           }
+#pragma unroll
+          for (int c = 0; c < GC / 2; c += 8) {
+            uint32_t h8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) h8[e] = hw[c + e];
+            tst8(tlane + LY::C_M + GC * sub + c, h8);
+            if constexpr (!ONE) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) h8[e] = lw[c + e];
+              tst8(tlane + LY::C_M + GC * sub + GC / 2 + c, h8);
+            }
+          }
+          tst_wait();
         }
-        fence_async_smem();
         fence_before();
         __syncthreads();
         if (tid == 0 && !failed) {
           fence_after();
-          // R += mask(M) . pK  (both parts of pK along N, both parts of M)
+          // R += mask(M) . pK  (both parts of M, both parts of pK along N)
 #pragma unroll
-          for (int a = 0; a < (ONE ? 1 : 2); ++a) {
-            const bf16* mp = a ? mm_lo : mm_hi;
+          for (int a = 0; a < (ONE ? 1 : 2); ++a)
 #pragma unroll
             for (int ks = 0; ks < TT / 16; ++ks)
-              mma(tbase + LY::C_R, desc<TT>(mp, ks), desc_mn<2 * SP>(pk, ks), idesc_bmn<KP>(),
-                  true);
-          }
+              mma_ta(tbase + LY::C_R,
+                     tbase + LY::C_M + GC * (16 * ks / GC) + a * (GC / 2) + (16 * ks % GC) / 2,
+                     desc_mn<2 * SP>(pk, ks), idesc_bmn<KP>(), true);
           { commit(barB); ++issB; }
         }
         T5_WAIT(barB, phB);
@@ -997,19 +1002,22 @@ __global__ void __launch_bounds__(TT * BwdQLayC<D, SPAD>::NTH, 1)
           put_tile_cols<T, D, W>(sm + LY::STG_DQ, row, sub * W, o);
         }
         // B0 of the next tile: range prefix + the state so far (M = 64 lanes)
-        if (i + 1 < it.ntiles && sub == 0) {
+        if (i + 1 < it.ntiles) {   // the NTH warps of a lane quarter take every NTH-th chunk
           const int d = 16 * quad + lane;
-          float stv[2 * SP];
+          for (int s8 = sub; s8 < SP / 8; s8 += NTH) {
+            float lo8[8] = {}, v[8];
+            tld8(tlane + LY::C_ST + 8 * s8, v);
+            if constexpr (!ONE) tld8(tlane + LY::C_ST + SP + 8 * s8, lo8);
+            tld_wait();
+            if (lane < 16 && d < D) {
 #pragma unroll
-          for (int c = 0; c < KP; c += 8) tld8(tlane + LY::C_ST + c, stv + c);
-          tld_wait();
-          if (lane < 16 && d < D) {
-#pragma unroll
-            for (int s2 = 0; s2 < SP; ++s2) {
-              const float x = b0f[s2 * D + d] + stv[s2] + (ONE ? 0.f : stv[SP + s2]);
-              const bf16 h = __float2bfloat16_rn(x);
-              b0s[elem<D>(s2, d)] = h;
-              if constexpr (!ONE) b0s[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
+              for (int e = 0; e < 8; ++e) {
+                const int s2 = 8 * s8 + e;
+                const float x = b0f[s2 * D + d] + v[e] + lo8[e];
+                const bf16 h = __float2bfloat16_rn(x);
+                b0s[elem<D>(s2, d)] = h;
+                if constexpr (!ONE) b0s[elem<D>(SP + s2, d)] = __float2bfloat16_rn(x - __bfloat162float(h));
+              }
             }
           }
         }
@@ -1529,15 +1537,18 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
         }
         // BS operands of the next (earlier) tile: range-end suffix + the
         // tiles walked so far (M = 64 lanes: row d = 16 q + l)
-        if (i + 1 < it.ntiles && sub == 0) {
+        if (i + 1 < it.ntiles) {   // the NTH warps of a lane quarter take every NTH-th chunk
           const int d = 16 * quad + lane;
-          float bsv[2 * SP];
+          for (int s8 = sub; s8 < SP / 8; s8 += NTH) {
+            float lo8[8] = {}, v[8];
+            tld8(tlane + LY::C_BS + 8 * s8, v);
+            if constexpr (!ONE) tld8(tlane + LY::C_BS + SP + 8 * s8, lo8);
+            tld_wait();
+            if (lane < 16 && d < D) {
 #pragma unroll
-          for (int c = 0; c < KP; c += 8) tld8(tlane + LY::C_BS + c, bsv + c);
-          tld_wait();
-          if (lane < 16 && d < D) {
-            for (int s2 = 0; s2 < SP; ++s2)
-              put_bs(s2, d, bsf[s2 * D + d] + bsv[s2] + (ONE ? 0.f : bsv[SP + s2]));
+              for (int e = 0; e < 8; ++e)
+                put_bs(8 * s8 + e, d, bsf[(8 * s8 + e) * D + d] + v[e] + lo8[e]);
+            }
           }
         }
         fence_async_smem();
