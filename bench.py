@@ -220,16 +220,18 @@ class Layer:
 #       --variants noncausal_f32 (or causal_f32) --tokens 524288 --steps 2 --warmup 3
 #       --no-e2e --no-cpu --no-strong --no-shapes
 # bf16 entries: ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,
-# dram__bytes_write.sum --clock-control none python bench.py --steps 2 --warmup 3
-# --no-e2e --no-cpu --tokens 262144 (2^18 tokens).
+# dram__bytes_write.sum --clock-control none -k regex:'k_t5_|k_c5_' python bench.py
+# --variants noncausal_bf16,causal_bf16 --tokens 262144 --steps 2 --warmup 3
+# --no-e2e --no-cpu --no-strong --no-shapes (2^18 tokens).
 TRAFFIC_PER_TOKEN = {
-    (False, "f32", "backward_kv"): (268.6e6 + 217.9e6) / 2 ** 19,
-    (False, "f32", "backward_q"): (268.5e6 + 107.0e6) / 2 ** 19,
-    (False, "bf16", "backward_kv"): 86.0e6 / 2 ** 18,
-    (False, "bf16", "backward_q"): 72.1e6 / 2 ** 18,
-    (True, "f32", "backward_kv"): (380.5e6 + 227.4e6) / 2 ** 19,
-    (True, "f32", "backward_q"): (337.6e6 + 148.5e6) / 2 ** 19,
-    (True, "bf16", "backward_kv"): 197.7e6 / 2 ** 18,
+    (False, "f32", "backward_kv"): (268.58e6 + 221.34e6) / 2 ** 19,
+    (False, "f32", "backward_q"): (268.51e6 + 105.29e6) / 2 ** 19,
+    (False, "bf16", "backward_kv"): (67.18e6 + 18.79e6) / 2 ** 18,
+    (False, "bf16", "backward_q"): (67.17e6 + 3.48e6) / 2 ** 18,
+    (True, "f32", "backward_kv"): (381.16e6 + 229.57e6) / 2 ** 19,
+    (True, "f32", "backward_q"): (337.17e6 + 144.85e6) / 2 ** 19,
+    (True, "bf16", "backward_kv"): (124.33e6 + 33.24e6) / 2 ** 18,
+    (True, "bf16", "backward_q"): (102.28e6 + 20.94e6) / 2 ** 18,
 }
 
 
