@@ -890,7 +890,7 @@ __global__ void __launch_bounds__(TT * ReadoutLay<D, SPAD>::NTH, 2) k_t5_readout
       }
       fence_async_smem();
       fence_before();
-      __syncthreads();
+      if constexpr (!DIRECT) __syncthreads();   // bf16 in place: nothing was converted
       if (tid == 0 && !failed) {
         fence_after();
         gemm_parts<PJ, B2, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(X, 0),
@@ -1061,7 +1061,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
       }
       fence_async_smem();
       fence_before();
-      __syncthreads();
+      if constexpr (!DIRECT) __syncthreads();   // bf16 in place: nothing was converted
       if (tid == 0 && !failed) {
         fence_after();
         gemm_parts<PJ, B2, D / 16, D, D, DIRECT>(tbase + LY::C_PROJ, Slot<D>::part(KXt, 0),
@@ -1311,7 +1311,7 @@ __global__ void __launch_bounds__(TT * BwdQLay<D, SPAD>::NTH, 1)
         }
         fence_async_smem();
         fence_before();
-        __syncthreads();
+        if constexpr (!DIRECT) __syncthreads();   // bf16 in place: nothing was converted
         if (tid == 0 && !failed) {
           fence_after();
           // projections in three parts on both sides: they feed the
@@ -1570,7 +1570,7 @@ __global__ void __launch_bounds__(TT * BwdKVLay<D, SPAD>::NTH, 1) k_t5_bwd_kv(co
         }
         fence_async_smem();
         fence_before();
-        __syncthreads();
+        if constexpr (!DIRECT) __syncthreads();   // bf16 in place: nothing was converted
         // projections and dpK = v . dB^T
         if (tid == 0 && !failed) {
           fence_after();
