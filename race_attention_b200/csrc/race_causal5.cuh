@@ -1216,6 +1216,23 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
         float* GXt = sm + LY::GX;
         const float* pj = sm + LY::PJX;
         if (tid < SP) a0t[tid] = prm.range_mass[((size_t)n * tiles_n + tile0 / TT) * SP + tid];
+        // the tile's alpha rows from global memory, issued before the waits so
+        // their latency overlaps the copies in flight
+        float alr[MYG][G::GB];
+        {
+          const int64_t ta = tile0 + row;
+          const bool va = ta < it.t1;
+          const float* arow = prm.alpha + ((size_t)n * prm.T + (va ? ta : 0)) * prm.SA;
+#pragma unroll
+          for (int a = 0; a < MYG; ++a) {
+            const int gi = sub + a * NTH;
+#pragma unroll
+            for (int b = 0; b < G::GB; ++b) {
+              const int s2 = gi * G::GB + b;
+              alr[a][b] = (gi < NG && va && s2 < prm.S) ? __ldg(arow + s2) : 0.f;
+            }
+          }
+        }
         T5_WAIT(full, phF & 1);
         if (!failed) {
           phF ^= 1u;
@@ -1249,12 +1266,8 @@ __global__ void __launch_bounds__(TT * BwdKVLayC<D, SPAD>::NTH, 1)
               for (int k = 0; k < G::GK; ++k)
                 pj_[k] = has ? pj[TT * PJ + row * PJ + gi * G::GK + k] : 0.f;
               group_probs<K>(pj_, gi * G::GT, has ? L : 0, inv_scale, pkv[a], hk[a]);
-              const float* arow = prm.alpha + ((size_t)n * prm.T + (valid ? t : 0)) * prm.SA;
 #pragma unroll
-              for (int b = 0; b < G::GB; ++b) {
-                const int s2 = gi * G::GB + b;
-                al[a][b] = (valid && s2 < prm.S) ? arow[s2] : 0.f;
-              }
+              for (int b = 0; b < G::GB; ++b) al[a][b] = alr[a][b];
               if (!valid) {
 #pragma unroll
                 for (int b = 0; b < G::GB; ++b) pq[a][b] = pkv[a][b] = 0.f;
