@@ -1031,8 +1031,10 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
         inflight &= ~(1u << f);
       }
     };
-    // Per tile i: k and v parts (v in place) -> MMA proj(i) -> load k(i+1) ->
-    // probabilities -> pK parts -> MMA state(i) -> [state(i) done] load v(i+1)
+    // Per tile i: k parts -> MMA proj(i) -> load k(i+1) -> probabilities ->
+    // pK parts -> v parts (in place) -> MMA state(i) -> [thread 0: state(i)
+    // done] load v(i+1).  v(i+1) lands while tile i+1's projections and
+    // probabilities are formed; only thread 0 waits for the state MMAs.
     if (it.ntiles > 0) {
       load_one(0, 0);
       load_one(0, 1);
@@ -1043,21 +1045,13 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
       float* VXt = sm + LY::VX;
       bf16* vl = reinterpret_cast<bf16*>(sm + LY::VL);
       landed(0);
-      landed(1);
       const bool valid = tile0 + row < it.t1;
       if constexpr (!DIRECT) {   // bf16 at D = 64: the landed tiles are the operands
-        float x[W], y[W];
+        float x[W];
         read_cols<T, D, W>(KXt, row, sub * W, x);
-        read_cols<T, D, W>(VXt, row, sub * W, y);
-        if (!valid) {   // v rows past the range are zero
-#pragma unroll
-          for (int c = 0; c < W; ++c) y[c] = 0.f;
-        }
         convert_sync<D, NTH>(warp);
         put_cols<D, W, F32 ? 2 : 1>(Slot<D>::part(KXt, 0), Slot<D>::part(KXt, 1), nullptr, row,
                                     sub * W, x);
-        put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), vl, row,
-                                    sub * W, y);
       }
       fence_async_smem();
       fence_before();
@@ -1103,6 +1097,18 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
           }
         }
       }
+      landed(1);
+      if constexpr (!DIRECT) {
+        float y[W];
+        read_cols<T, D, W>(VXt, row, sub * W, y);
+        if (!valid) {   // v rows past the range are zero
+#pragma unroll
+          for (int c = 0; c < W; ++c) y[c] = 0.f;
+        }
+        convert_sync<D, NTH>(warp);
+        put_cols<D, W, F32 ? 3 : 1>(Slot<D>::part(VXt, 0), Slot<D>::part(VXt, 1), vl, row,
+                                    sub * W, y);
+      }
       fence_async_smem();
       fence_before();
       __syncthreads();
@@ -1119,7 +1125,7 @@ __global__ void __launch_bounds__(TT * ReduceLay<D, SPAD>::NTH, 2)
         { commit(barB); ++issB; }
       }
       if (i + 1 < it.ntiles) {   // the state MMAs read the v slot in place
-        T5_WAIT(barB, phB);
+        if (tid == 0) T5_WAIT(barB, phB);   // the other threads move on to tile i + 1
         phB ^= 1;
         load_one(i + 1, 1);
       }
